@@ -1,0 +1,413 @@
+"""Benchmark of the fused per-Gaussian backward-and-update step on B200.
+
+Workload (one "step"): the fused per-Gaussian pass over 1,100,000 Gaussians,
+SH degree 3 — SH colour VJP wrt coefficients and view direction, torch-fused
+Adam on features_dc / features_rest, position adjoint into dm, and the
+rotation / scaling / opacity activation VJPs with their Adam updates — with
+the step counter advancing every step (bias corrections of steps 1, 2, ...),
+moments carried over. Synthetic, seeded inputs with the distributions of the
+fused-step configuration: features_dc ~ N(0.5, 0.1), features_rest ~
+N(0, 0.05), means ~ U[-1, 1]^3 seen by one pinhole camera at (0, 0, -4)
+(980x545, fov 60 deg: visibility and radii from the projection, clamped
+channels from the SH colour), dL/dcolor ~ N(0, 1e-3), rotations ~ N(0, 1),
+log-scales ~ U(-6, -2), opacity logits ~ N(-2, 1), activation seeds ~
+N(0, 1e-4).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Multi-GPU runs go through torchrun; every rank steps its own 1.1M-Gaussian
+shard (Gaussian-index sharding, no collective on the data path: weak scaling).
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "clad-3dgs_b200"))
+
+N_GAUSSIANS = 1_100_000
+DEGREE = 3
+BYTES_PER_GAUSSIAN = 1451          # SH 1207 + activations 244 (algorithmic)
+H2D_BYTES_PER_GAUSSIAN = 767       # inputs of one host-buffer step
+D2H_BYTES_PER_GAUSSIAN = 684       # outputs of one host-buffer step
+METRIC = "Gaussians/s fused SH-grad+Adam & % HBM peak; train iters/s at 1/2/4/8 B200"
+WORKLOAD = "fused per-Gaussian step (SH deg 3 VJP + Adam, activation VJPs + Adam)"
+L2_NOTE = "inputs 1.60 GB per step exceed the 126 MB L2; no flush needed"
+WIDTH, HEIGHT, FOV = 980, 545, math.radians(60.0)
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS,
+                    help="Gaussians per GPU (smaller cases are for profiling only)")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the measurement.
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.out = self.path.open("w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.out.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
+                                 power=float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], cap=parts[8]))
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r["power"] > 200] or rows
+        reasons = set()
+        for r in loaded:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("cap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(loaded)}
+
+
+# ---------------------------------------------------------------------------
+# Synthetic state of one shard.
+
+def make_state(n, device, seed):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    randn = lambda *s: torch.randn(s, generator=g, device=device)
+    rand = lambda *s: torch.rand(s, generator=g, device=device)
+    means = rand(n, 3) * 2 - 1
+    camera = torch.tensor([0.0, 0.0, -4.0], device=device)
+    dc = randn(n, 1, 3) * 0.1 + 0.5
+    rest = randn(n, 15, 3) * 0.05
+    log_scale = rand(n, 3) * 4 - 6
+    rotation = randn(n, 4)
+    opacity = randn(n, 1) - 2
+    # Pinhole camera at (0,0,-4) looking down +z: visibility and pixel radii.
+    rel = means - camera
+    focal = (WIDTH / 2) / math.tan(FOV / 2)
+    depth = rel[:, 2]
+    px = rel[:, 0] / depth * focal
+    py = rel[:, 1] / depth * focal
+    inside = (depth > 0.2) & (px.abs() < WIDTH / 2 + 64) & (py.abs() < HEIGHT / 2 + 64)
+    sigma_px = 3.0 * log_scale.exp().max(1).values * focal / depth
+    radii = torch.where(inside, torch.ceil(sigma_px).clamp_min(1), 0).to(torch.int32)
+    # Clamped channels: SH colour + 0.5 < 0 (the renderer's convention).
+    dirs = rel / rel.norm(dim=1, keepdim=True)
+    from_sh = _eval_sh3(torch.cat((dc, rest), 1).transpose(1, 2), dirs) + 0.5
+    clamped = (from_sh < 0).contiguous()
+    state = dict(
+        means=means.contiguous(), radii=radii.contiguous(), clamped=clamped,
+        camera=camera, seed=(randn(n, 3) * 1e-3).contiguous(),
+        dm=torch.zeros(n, 3, device=device), dc=dc.contiguous(), rest=rest.contiguous(),
+        dc_first=torch.zeros(n, 1, 3, device=device), dc_second=torch.zeros(n, 1, 3, device=device),
+        rest_first=torch.zeros(n, 15, 3, device=device),
+        rest_second=torch.zeros(n, 15, 3, device=device))
+    params = [rotation.contiguous(), log_scale.contiguous(), opacity.contiguous()]
+    state["act"] = dict(
+        params=params,
+        seeds=[(randn(*p.shape) * 1e-4).contiguous() for p in params],
+        saved=[rotation.norm(2, dim=1, keepdim=True).contiguous(), log_scale.exp().contiguous(),
+               opacity.sigmoid().contiguous()],
+        first=[torch.zeros_like(p) for p in params],
+        second=[torch.zeros_like(p) for p in params],
+        rates=[0.001, 0.005, 0.025])
+    return state
+
+
+def _eval_sh3(sh, dirs):
+    """Degree-3 real-SH colour of sh [n, 3, 16] along unit dirs [n, 3]; used
+    only to draw the clamped flags of the synthetic inputs."""
+    x, y, z = dirs[:, 0:1], dirs[:, 1:2], dirs[:, 2:3]
+    xx, yy, zz = x * x, y * y, z * z
+    basis = [0.28209479177387814 + 0 * x, -0.4886025119029199 * y, 0.4886025119029199 * z,
+             -0.4886025119029199 * x, 1.0925484305920792 * x * y,
+             -1.0925484305920792 * y * z, 0.31539156525252005 * (2 * zz - xx - yy),
+             -1.0925484305920792 * x * z, 0.5462742152960396 * (xx - yy),
+             -0.5900435899266435 * y * (3 * xx - yy), 2.890611442640554 * x * y * z,
+             -0.4570457994644658 * y * (4 * zz - xx - yy),
+             0.3731763325901154 * z * (2 * zz - 3 * xx - 3 * yy),
+             -0.4570457994644658 * x * (4 * zz - xx - yy),
+             1.445305721320277 * z * (xx - yy), -0.5900435899266435 * x * (xx - 3 * yy)]
+    out = 0
+    for j, b in enumerate(basis):
+        out = out + b * sh[..., j]
+    return out
+
+
+def step_bias(t):
+    import numpy as np
+
+    return float(np.float32(1 - 0.9 ** t)), float(np.float32(math.sqrt(1 - 0.999 ** t)))
+
+
+def run_step(consume, s, t):
+    b1, b2 = step_bias(t)
+    a = s["act"]
+    consume.gaussian_step(s["means"], s["radii"], s["clamped"], s["camera"], s["seed"],
+                          s["dm"], s["dc"], s["rest"], s["dc_first"], s["dc_second"],
+                          s["rest_first"], s["rest_second"], bias1=b1, bias2_sqrt=b2,
+                          degree=DEGREE, act_parameters=a["params"], act_seeds=a["seeds"],
+                          act_saved=a["saved"], act_first=a["first"], act_second=a["second"],
+                          act_rates=a["rates"], act_bias1=[b1] * 3, act_bias2=[b2] * 3)
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "fused_gaussian_step_traffic.json"
+    if not path.exists():
+        return None
+    try:
+        data = json.loads(path.read_text())
+        return float(data["bytes_per_launch_at_1.1M"])
+    except (ValueError, KeyError):
+        return None
+
+
+def cpu_baseline(budget_s=15.0):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch_cpu_path
+
+    probe = torch_cpu_path.time_cpu_path(20_000, steps=2, warmup=1)
+    per_g = probe["total_s"] / (probe["n"] * probe["steps"])
+    n = int(min(N_GAUSSIANS, max(20_000, budget_s / 12 / per_g)))
+    res = torch_cpu_path.time_cpu_path(n, steps=10, warmup=1)
+    return {"value": res["gaussians_per_s"], "unit": "Gaussians/s", "cores": res["threads"],
+            "kind": "port",
+            "sample": f"{n} Gaussians (of {N_GAUSSIANS}), 10 timed steps after 1 warm-up; "
+                      "torch CPU eval_sh + autograd + torch.optim.Adam, fp32"}
+
+
+# ---------------------------------------------------------------------------
+
+def native_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=device)
+    import consume
+    import _native as native
+
+    n_g = args.gaussians
+    state = make_state(n_g, device, seed=42 + rank)
+    torch.cuda.synchronize()
+    t = 0
+    with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            t += 1
+            run_step(consume, state, t)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        events[0].record(stream)
+        for k in range(args.steps):
+            t += 1
+            run_step(consume, state, t)
+            events[k + 1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    per_step = [events[k].elapsed_time(events[k + 1]) for k in range(args.steps)]
+    elapsed_ms = events[0].elapsed_time(events[-1])
+    fault = native.fault_status()
+    local_ms = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(local_ms, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(local_ms.item())
+
+    e2e = e2e_measurement(args, device, consume) if rank == 0 and not args.no_e2e else None
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    total_g = n_g * world * args.steps
+    value = total_g / (elapsed_ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    mean_step_s = statistics.mean(per_step) / 1e3
+    achieved = BYTES_PER_GAUSSIAN * n_g / mean_step_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "Gaussians/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+f64",
+        "data": "synthetic (seeded; distributions of the fused-step configuration)",
+        "config": {"workload": WORKLOAD, "gaussians_per_gpu": n_g,
+                   "sh_degree": DEGREE, "camera": "980x545 pinhole, fov 60",
+                   "parallelism": f"Gaussian-index shards x{world}", "l2": L2_NOTE},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": ncu_traffic(),
+                     "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
+                     "algorithmic_bytes_per_gaussian": BYTES_PER_GAUSSIAN,
+                     "kernel_time_ms": mean_step_s * 1e3},
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps,
+        "device_fault_word": fault,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(line), flush=True)
+
+
+def e2e_measurement(args, device, consume):
+    """Same metric through the C ABI with pinned host buffers: every step copies
+    its inputs in and its results out (chunked, overlapped) inside the timing."""
+    import torch
+
+    s = make_state(N_GAUSSIANS, device, seed=1042)
+    host = {k: (v.cpu().pin_memory() if torch.is_tensor(v) else v) for k, v in s.items()
+            if k != "act"}
+    act = {k: ([x.cpu().pin_memory() for x in v] if k != "rates" else v)
+           for k, v in s["act"].items()}
+    del s
+    chunk = 65536
+    ws = torch.empty(consume.host_step_workspace(chunk), dtype=torch.uint8, device=device)
+
+    def one(t):
+        b1, b2 = step_bias(t)
+        consume.gaussian_step_host(
+            host["means"], host["radii"], host["clamped"], host["camera"], host["seed"],
+            host["dm"], host["dc"], host["rest"], host["dc_first"], host["dc_second"],
+            host["rest_first"], host["rest_second"], bias1=b1, bias2_sqrt=b2, degree=DEGREE,
+            act_parameters=act["params"], act_seeds=act["seeds"], act_saved=act["saved"],
+            act_first=act["first"], act_second=act["second"], act_rates=act["rates"],
+            act_bias1=[b1] * 3, act_bias2=[b2] * 3, workspace=ws, chunk=chunk)
+
+    steps = max(3, args.e2e_steps)
+    for t in range(1, 3):
+        one(t)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for t in range(3, 3 + steps):
+        one(t)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    return {"value": N_GAUSSIANS * steps / (ms / 1e3), "unit": "Gaussians/s",
+            "h2d_bytes_per_step": H2D_BYTES_PER_GAUSSIAN * N_GAUSSIANS + 12,
+            "d2h_bytes_per_step": D2H_BYTES_PER_GAUSSIAN * N_GAUSSIANS,
+            "steps": steps, "ms_per_step": ms / steps,
+            "path": "clad3dgs_gaussian_step_host (C ABI), pinned host buffers, 64K-Gaussian "
+                    "chunks on 3 streams"}
+
+
+def reference_arm(args):
+    """The reference's CPU path (eval_sh + autograd + torch.optim.Adam) on host
+    cores; rank 0 only."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch_cpu_path
+
+    probe = torch_cpu_path.time_cpu_path(20_000, steps=2, warmup=1)
+    per_g = probe["total_s"] / (probe["n"] * probe["steps"])
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    n = int(min(N_GAUSSIANS, max(1024, budget / per_g)))
+    res = torch_cpu_path.time_cpu_path(n, steps=args.steps, warmup=args.warmup)
+    sample = (f"{n} Gaussians per step (of {N_GAUSSIANS}), {args.steps} timed steps after "
+              f"{args.warmup} warm-up; torch CPU eval_sh + autograd + torch.optim.Adam")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["gaussians_per_s"],
+        "unit": "Gaussians/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["total_s"] * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; distributions of the fused-step configuration)",
+        "config": {"workload": WORKLOAD, "gaussians_per_gpu": N_GAUSSIANS, "sh_degree": DEGREE,
+                   "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": res["gaussians_per_s"], "unit": "Gaussians/s",
+                         "cores": res["threads"], "kind": "port", "sample": sample},
+        "e2e": {"value": res["gaussians_per_s"], "unit": "Gaussians/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        native_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,900 @@
+// Per-Gaussian backward-and-update kernels for B200 (sm_100a).
+//
+// One kernel template covers the reference's SH consumer (all four update
+// modes, SHGradientConsumer.cu:92-217), the activation consumer
+// (normalization.cu:79-101) and the fused pass that does both. Data layout and
+// schedule:
+//
+//  * Gaussians are processed in tiles of kTile = 64. For each tile every array
+//    the mode touches (means, radii, clamped, seeds, dm, dc/rest and their two
+//    moments, activation parameters/moments/seeds/saved values) is one
+//    contiguous byte range in HBM, so a tile is fetched with one 1D bulk copy
+//    (cp.async.bulk, the TMA engine) per array into shared memory and written
+//    back the same way. There are no per-lane 12-byte accesses.
+//  * The main kernel is persistent: one CTA per SM, a ring of stages in shared
+//    memory, one producer thread issuing bulk loads ahead and eight consumer
+//    warps doing the arithmetic. Stage reuse is gated by mbarriers, write-back
+//    by bulk-store groups, so HBM reads, compute and HBM writes overlap.
+//  * Inside a tile, warp w of the consumers owns SH terms {r, r+4, r+8, r+12}
+//    (r = w mod 4) for 32 consecutive Gaussians (lane = Gaussian). The term
+//    index is warp-uniform and compile-time after a 4-way dispatch, so there is
+//    no divergent 16-way switch. Shared-memory rows of 45 (rest) or 3 (dc)
+//    floats are odd strides, so these accesses are bank-conflict free.
+//  * The direction adjoint is reduced in the reference's order
+//    ((t_r + t_{r+8}) + (t_{r+4} + t_{r+12})) in registers, then
+//    (v0 + v2) + (v1 + v3) through shared memory (SHGradientConsumer.cu:203-207).
+//  * The tail tile and inputs that are not 16-byte aligned go through a plain
+//    one-tile-per-CTA kernel with the same arithmetic.
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+#include <utility>
+
+#include "async_copy.cuh"
+#include "gaussian_math.cuh"
+#include "clad3dgs_b200.h"
+
+namespace clad3dgs {
+
+// Per-module fault word written by bounded waits that gave up.
+__device__ unsigned int g_fault_word = 0;
+
+// ---------------------------------------------------------------------------
+// Arrays a tile can stage. Widths are per Gaussian; CLAMPED is one byte per
+// element, everything else four.
+enum Arr : int {
+  MEANS, RADII, CLAMPED, SEED, DM,
+  DC, DC_M, DC_V, REST, REST_M, REST_V, SNAP,
+  COEF, COEF_M, COEF_V,
+  ROT, ROT_M, ROT_V, SCL, SCL_M, SCL_V, OPA, OPA_M, OPA_V,
+  SEED_ROT, SEED_SCL, SEED_OPA, SAVED_NORM, SAVED_SCL, SAVED_OPA,
+  NUM_ARR
+};
+
+constexpr int kWidth[NUM_ARR] = {3, 1, 3, 3, 3,  3,  3, 3, 45, 45,
+                                 45, 48, 48, 48, 48, 4, 4, 4, 3,  3,
+                                 3, 1, 1, 1, 4, 3, 1, 1, 3, 1};
+constexpr bool kWritten[NUM_ARR] = {0, 0, 0, 0, 1, 1, 1, 1, 1, 1,
+                                    1, 0, 1, 1, 1, 1, 1, 1, 1, 1,
+                                    1, 1, 1, 1, 0, 0, 0, 0, 0, 0};
+constexpr int elem_bytes(int a) { return a == CLAMPED ? 1 : 4; }
+
+enum ShMode : int { SH_NONE, SH_SGD, SH_ADAM, SH_SPLIT_ADAM, SH_SPLIT_TORCH };
+
+constexpr int kTile = 64;                 // Gaussians per tile
+constexpr int kConsumers = 256;           // 8 consumer warps
+constexpr int kPersistThreads = kConsumers + 32;  // + 1 producer warp
+constexpr int kMaxStages = 8;
+constexpr uint32_t kStageBudget = 220u * 1024u;   // dynamic smem for stages
+
+constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+template <int Sh, bool Act, bool Snap>
+struct Cfg {
+  static constexpr int kSh = Sh;
+  static constexpr bool kAct = Act;
+  static constexpr bool kSnap = Snap;
+  static constexpr bool has(int a) {
+    if (a == MEANS || a == RADII || a == CLAMPED || a == SEED || a == DM)
+      return Sh != SH_NONE;
+    if (a == COEF) return Sh == SH_SGD || Sh == SH_ADAM;
+    if (a == COEF_M || a == COEF_V) return Sh == SH_ADAM;
+    if (a >= DC && a <= REST_V) return Sh == SH_SPLIT_ADAM || Sh == SH_SPLIT_TORCH;
+    if (a == SNAP) return Snap && (Sh == SH_SPLIT_ADAM || Sh == SH_SPLIT_TORCH);
+    return Act;  // ROT .. SAVED_OPA
+  }
+  static constexpr uint32_t tile_bytes(int a) {
+    return uint32_t(kTile) * kWidth[a] * elem_bytes(a);
+  }
+  static constexpr uint32_t offset(int a) {
+    uint32_t o = 0;
+    for (int b = 0; b < a; ++b)
+      if (has(b)) o += round_up(tile_bytes(b), 128);
+    return o;
+  }
+  static constexpr uint32_t stage_bytes = offset(NUM_ARR);
+  static constexpr uint32_t load_bytes() {
+    uint32_t s = 0;
+    for (int a = 0; a < NUM_ARR; ++a)
+      if (has(a)) s += tile_bytes(a);
+    return s;
+  }
+  static constexpr int stages =
+      (kStageBudget / stage_bytes) > kMaxStages ? kMaxStages
+                                                : int(kStageBudget / stage_bytes);
+  static_assert(stages >= 2, "stage does not fit twice in shared memory");
+};
+
+// Everything a launch needs; passed by value.
+struct StepParams {
+  const void* ptr[NUM_ARR];
+  long long n;           // Gaussians
+  long long tile_begin;  // first tile of this launch
+  long long tile_end;    // one past the last tile of this launch
+  const float* camera;   // device, 3 floats
+  int degree;
+  float sh_step_dc, sh_step_rest, sh_bias2;  // torch Adam on dc / rest
+  float inv_bias1, inv_bias2;                // float Adam (AdamConfig)
+  float act_step[3], act_bias2[3];           // rotation, scaling, opacity
+};
+
+template <class F, int... Is>
+__device__ __forceinline__ void for_each_arr_impl(F&& f,
+                                                  std::integer_sequence<int, Is...>) {
+  (f(std::integral_constant<int, Is>{}), ...);
+}
+template <class F>
+__device__ __forceinline__ void for_each_arr(F&& f) {
+  for_each_arr_impl(f, std::make_integer_sequence<int, NUM_ARR>{});
+}
+
+template <class C>
+struct Stage {
+  unsigned char* base;
+  template <int A>
+  __device__ __forceinline__ float* f() const {
+    return reinterpret_cast<float*>(base + C::offset(A));
+  }
+  template <int A>
+  __device__ __forceinline__ int* i() const {
+    return reinterpret_cast<int*>(base + C::offset(A));
+  }
+  template <int A>
+  __device__ __forceinline__ unsigned char* b() const {
+    return base + C::offset(A);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Arithmetic on one staged tile.
+
+template <class C, int J>
+__device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
+                                                          int gl) {
+  if constexpr (C::kSh == SH_SGD || C::kSh == SH_ADAM) {
+    return st.template f<COEF>() + gl * 48 + 3 * J;
+  } else if constexpr (C::kSnap) {
+    return st.template f<SNAP>() + gl * 48 + 3 * J;
+  } else if constexpr (J == 0) {
+    return st.template f<DC>() + gl * 3;
+  } else {
+    return st.template f<REST>() + gl * 45 + 3 * (J - 1);
+  }
+}
+
+template <class C, int J>
+__device__ __forceinline__ void term_update(const StepParams& p,
+                                            const Stage<C>& st, int gl,
+                                            const float g[3]) {
+  if constexpr (C::kSh == SH_SPLIT_TORCH || C::kSh == SH_SPLIT_ADAM) {
+    float* pp = J == 0 ? st.template f<DC>() + gl * 3
+                       : st.template f<REST>() + gl * 45 + 3 * (J - 1);
+    float* mm = J == 0 ? st.template f<DC_M>() + gl * 3
+                       : st.template f<REST_M>() + gl * 45 + 3 * (J - 1);
+    float* vv = J == 0 ? st.template f<DC_V>() + gl * 3
+                       : st.template f<REST_V>() + gl * 45 + 3 * (J - 1);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      if constexpr (C::kSh == SH_SPLIT_TORCH)
+        torch_adam(pp[ch], mm[ch], vv[ch], g[ch],
+                   J == 0 ? p.sh_step_dc : p.sh_step_rest, p.sh_bias2);
+      else
+        float_adam(pp[ch], mm[ch], vv[ch], g[ch], J == 0 ? kDcRate : kRestRate,
+                   p.inv_bias1, p.inv_bias2);
+    }
+  } else if constexpr (C::kSh == SH_ADAM) {
+    const int o = gl * 48 + 3 * J;
+    float* pp = st.template f<COEF>() + o;
+    float* mm = st.template f<COEF_M>() + o;
+    float* vv = st.template f<COEF_V>() + o;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch)
+      float_adam(pp[ch], mm[ch], vv[ch], g[ch], J == 0 ? kDcRate : kRestRate,
+                 p.inv_bias1, p.inv_bias2);
+  } else {
+    float* pp = st.template f<COEF>() + gl * 48 + 3 * J;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) sgd(pp[ch], g[ch]);
+  }
+}
+
+// One SH term of one Gaussian: coefficient gradient into the update, direction
+// adjoint into dd. Inactive terms (invisible Gaussian or above the degree)
+// still update the optimizer with a zero gradient.
+template <class C, int J>
+__device__ __forceinline__ void term_step(const StepParams& p,
+                                          const Stage<C>& st, int gl,
+                                          bool active, const Direction& d,
+                                          const float s[3], float dd[3]) {
+  float g[3] = {0.f, 0.f, 0.f};
+  dd[0] = dd[1] = dd[2] = 0.f;
+  if (active) {
+    float b, gx, gy, gz;
+    sh_basis<J>(d, b, gx, gy, gz);
+    const float* c = term_coefficients<C, J>(st, gl);
+    const float dot = (c[0] * s[0] + c[1] * s[1]) + c[2] * s[2];
+    dd[0] = gx * dot;
+    dd[1] = gy * dot;
+    dd[2] = gz * dot;
+    g[0] = b * s[0];
+    g[1] = b * s[1];
+    g[2] = b * s[2];
+  }
+  term_update<C, J>(p, st, gl, g);
+}
+
+template <class C, int R>
+__device__ __forceinline__ void sh_role(const StepParams& p, const Stage<C>& st,
+                                        int gl, bool visible, int nterms,
+                                        const Direction& d, const float s[3],
+                                        float part[3]) {
+  float t0[3], t1[3], t2[3], t3[3];
+  term_step<C, R>(p, st, gl, visible && R < nterms, d, s, t0);
+  term_step<C, R + 4>(p, st, gl, visible && R + 4 < nterms, d, s, t1);
+  term_step<C, R + 8>(p, st, gl, visible && R + 8 < nterms, d, s, t2);
+  term_step<C, R + 12>(p, st, gl, visible && R + 12 < nterms, d, s, t3);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) part[k] = (t0[k] + t2[k]) + (t1[k] + t3[k]);
+}
+
+template <class C>
+__device__ __forceinline__ void process_tile(const StepParams& p,
+                                             const Stage<C>& st, int cnt,
+                                             int ct, float (*partial)[kTile][3],
+                                             const float cam[3]) {
+  const int cw = ct >> 5, lane = ct & 31;
+  const int gl = ((cw >> 2) << 5) + lane;  // local Gaussian of this thread
+  const int role = cw & 3;                 // warp-uniform
+  const bool valid = gl < cnt;
+  if constexpr (C::kSh != SH_NONE) {
+    float part[3] = {0.f, 0.f, 0.f};
+    bool visible = false;
+    Direction d{};
+    if (valid) {
+      visible = st.template i<RADII>()[gl] > 0;
+      if (C::kSh != SH_SGD || visible) {
+        float s[3] = {0.f, 0.f, 0.f};
+        if (visible) {
+          const float* m = st.template f<MEANS>() + 3 * gl;
+          d = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
+          const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
+          const float* sd = st.template f<SEED>() + 3 * gl;
+#pragma unroll
+          for (int ch = 0; ch < 3; ++ch) s[ch] = cl[ch] ? 0.f : sd[ch];
+        }
+        const int nterms = (p.degree + 1) * (p.degree + 1);
+        switch (role) {
+          case 0: sh_role<C, 0>(p, st, gl, visible, nterms, d, s, part); break;
+          case 1: sh_role<C, 1>(p, st, gl, visible, nterms, d, s, part); break;
+          case 2: sh_role<C, 2>(p, st, gl, visible, nterms, d, s, part); break;
+          default: sh_role<C, 3>(p, st, gl, visible, nterms, d, s, part); break;
+        }
+      }
+    }
+    partial[role][gl][0] = part[0];
+    partial[role][gl][1] = part[1];
+    partial[role][gl][2] = part[2];
+    named_barrier(1, kConsumers);
+    if (role == 0 && valid && visible) {
+      float dd[3];
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+        dd[k] = (partial[0][gl][k] + partial[2][gl][k]) +
+                (partial[1][gl][k] + partial[3][gl][k]);
+      float o[3];
+      direction_vjp(d, dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+      float* dm = st.template f<DM>() + 3 * gl;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
+    }
+  }
+  if constexpr (C::kAct) {
+    if (valid) {
+      if (role == 1) {
+        float* q = st.template f<ROT>() + 4 * gl;
+        float* qm = st.template f<ROT_M>() + 4 * gl;
+        float* qv = st.template f<ROT_V>() + 4 * gl;
+        const float* sq = st.template f<SEED_ROT>() + 4 * gl;
+        const float norm = st.template f<SAVED_NORM>()[gl];
+        float qr[4], sr[4], g[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          qr[k] = q[k];
+          sr[k] = sq[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) g[k] = quaternion_vjp(qr, sr, norm, k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          torch_adam(q[k], qm[k], qv[k], g[k], p.act_step[0], p.act_bias2[0]);
+      } else if (role == 2) {
+        float* sc = st.template f<SCL>() + 3 * gl;
+        float* sm = st.template f<SCL_M>() + 3 * gl;
+        float* sv = st.template f<SCL_V>() + 3 * gl;
+        const float* ss = st.template f<SEED_SCL>() + 3 * gl;
+        const float* se = st.template f<SAVED_SCL>() + 3 * gl;
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          torch_adam(sc[k], sm[k], sv[k], se[k] * ss[k], p.act_step[1],
+                     p.act_bias2[1]);
+      } else if (role == 3) {
+        const float a = st.template f<SAVED_OPA>()[gl];
+        const float g = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
+        torch_adam(st.template f<OPA>()[gl], st.template f<OPA_M>()[gl],
+                   st.template f<OPA_V>()[gl], g, p.act_step[2], p.act_bias2[2]);
+      }
+    }
+  }
+}
+
+template <class C>
+__device__ __forceinline__ void load_camera(const StepParams& p, float cam[3]) {
+  if constexpr (C::kSh != SH_NONE) {
+    cam[0] = __ldg(p.camera);
+    cam[1] = __ldg(p.camera + 1);
+    cam[2] = __ldg(p.camera + 2);
+  } else {
+    cam[0] = cam[1] = cam[2] = 0.f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent pipeline: warp 0 lane 0 produces, warps 1..8 consume.
+template <class C>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    stream_kernel(const StepParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full_bar[C::stages];
+  __shared__ __align__(8) uint64_t empty_bar[C::stages];
+  __shared__ float partial[4][kTile][3];
+  __shared__ int stage_ok;
+  constexpr int S = C::stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const long long first = p.tile_begin + blockIdx.x;
+  const long long stride = gridDim.x;
+
+  if (warp == 0) {
+    if (lane != 0) return;
+    int k = 0;
+    for (long long t = first; t < p.tile_end; t += stride, ++k) {
+      const int s = k % S;
+      if (k >= S && !mbar_wait_bounded(&empty_bar[s], ((k / S) - 1) & 1)) {
+        atomicOr(&g_fault_word, kFaultProducerWait);
+        return;
+      }
+      mbar_arrive_expect_tx(&full_bar[s], C::load_bytes());
+      unsigned char* st = smem + size_t(s) * C::stage_bytes;
+      for_each_arr([&](auto a_) {
+        constexpr int a = decltype(a_)::value;
+        if constexpr (C::has(a)) {
+          const char* src = static_cast<const char*>(p.ptr[a]) +
+                            t * (long long)C::tile_bytes(a);
+          bulk_load(st + C::offset(a), src, C::tile_bytes(a), &full_bar[s]);
+        }
+      });
+    }
+    return;
+  }
+
+  const int ct = threadIdx.x - 32;
+  float cam[3];
+  load_camera<C>(p, cam);
+  int k = 0;
+  for (long long t = first; t < p.tile_end; t += stride, ++k) {
+    const int s = k % S;
+    const uint32_t parity = (k / S) & 1;
+    if (ct == 0) stage_ok = mbar_wait_bounded(&full_bar[s], parity) ? 1 : 0;
+    named_barrier(1, kConsumers);
+    if (!stage_ok) {
+      if (ct == 0) atomicOr(&g_fault_word, kFaultConsumerWait);
+      break;
+    }
+    (void)mbar_try_wait(&full_bar[s], parity);  // acquire for this thread
+    Stage<C> st{smem + size_t(s) * C::stage_bytes};
+    process_tile<C>(p, st, kTile, ct, partial, cam);
+    fence_async_shared();
+    named_barrier(1, kConsumers);
+    if (ct == 0) {
+      for_each_arr([&](auto a_) {
+        constexpr int a = decltype(a_)::value;
+        if constexpr (C::has(a) && kWritten[a]) {
+          char* dst = static_cast<char*>(const_cast<void*>(p.ptr[a])) +
+                      t * (long long)C::tile_bytes(a);
+          bulk_store(dst, st.base + C::offset(a), C::tile_bytes(a));
+        }
+      });
+      bulk_commit();
+      if (k > 0) {
+        bulk_wait_read<1>();
+        mbar_arrive(&empty_bar[(k - 1) % S]);
+      }
+    }
+  }
+  if (ct == 0) bulk_wait_read<0>();
+}
+
+// ---------------------------------------------------------------------------
+// One tile per CTA, plain loads and stores; any 4-byte alignment, any count.
+template <class C>
+__global__ void __launch_bounds__(kConsumers)
+    tile_kernel(const StepParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ float partial[4][kTile][3];
+  const long long tile = p.tile_begin + blockIdx.x;
+  const long long g0 = tile * kTile;
+  const int cnt = int(min((long long)kTile, p.n - g0));
+  Stage<C> st{smem};
+  for_each_arr([&](auto a_) {
+    constexpr int a = decltype(a_)::value;
+    if constexpr (C::has(a)) {
+      const int count = cnt * kWidth[a];
+      const long long base = g0 * kWidth[a];
+      if constexpr (a == CLAMPED) {
+        const unsigned char* src = static_cast<const unsigned char*>(p.ptr[a]);
+        for (int e = threadIdx.x; e < count; e += kConsumers)
+          st.base[C::offset(a) + e] = src[base + e];
+      } else {
+        const float* src = static_cast<const float*>(p.ptr[a]);
+        float* dst = reinterpret_cast<float*>(st.base + C::offset(a));
+        for (int e = threadIdx.x; e < count; e += kConsumers)
+          dst[e] = src[base + e];
+      }
+    }
+  });
+  float cam[3];
+  load_camera<C>(p, cam);
+  __syncthreads();
+  process_tile<C>(p, st, cnt, threadIdx.x, partial, cam);
+  __syncthreads();
+  for_each_arr([&](auto a_) {
+    constexpr int a = decltype(a_)::value;
+    if constexpr (C::has(a) && kWritten[a]) {
+      const int count = cnt * kWidth[a];
+      const long long base = g0 * kWidth[a];
+      float* dst = static_cast<float*>(const_cast<void*>(p.ptr[a]));
+      const float* src = reinterpret_cast<const float*>(st.base + C::offset(a));
+      for (int e = threadIdx.x; e < count; e += kConsumers)
+        dst[base + e] = src[e];
+    }
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Standalone quaternion VJP: one thread per Gaussian, 16-byte rows.
+template <bool Vec>
+__global__ void quaternion_kernel(long long n, const float* __restrict__ q,
+                                  const float* __restrict__ seed,
+                                  const float* __restrict__ norms,
+                                  float* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float qv[4], sv[4], r[4];
+    if constexpr (Vec) {
+      const float4 a = reinterpret_cast<const float4*>(q)[i];
+      const float4 b = reinterpret_cast<const float4*>(seed)[i];
+      qv[0] = a.x; qv[1] = a.y; qv[2] = a.z; qv[3] = a.w;
+      sv[0] = b.x; sv[1] = b.y; sv[2] = b.z; sv[3] = b.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        qv[k] = q[4 * i + k];
+        sv[k] = seed[4 * i + k];
+      }
+    }
+    const float norm = norms[i];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = quaternion_vjp(qv, sv, norm, k);
+    if constexpr (Vec) {
+      reinterpret_cast<float4*>(out)[i] = make_float4(r[0], r[1], r[2], r[3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) out[4 * i + k] = r[k];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& message) {
+  t_last_error = message;
+  return code;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+};
+
+DeviceInfo& device_info() {
+  static DeviceInfo infos[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo& info = infos[dev & 63];
+  if (info.sm_count == 0) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    info.sm_count = sms > 0 ? sms : 1;
+  }
+  return info;
+}
+
+template <class C>
+constexpr size_t persist_smem() { return size_t(C::stages) * C::stage_bytes; }
+
+template <class C>
+cudaError_t configure_kernels() {
+  // Attributes are per function and cheap to set; setting them on every call
+  // keeps multi-device processes correct without per-device bookkeeping.
+  cudaError_t e = cudaFuncSetAttribute(stream_kernel<C>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(persist_smem<C>()));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tile_kernel<C>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(C::stage_bytes));
+}
+
+template <class C>
+cudaError_t run(StepParams p, cudaStream_t stream) {
+  if (p.n <= 0) return cudaSuccess;
+  cudaError_t e = configure_kernels<C>();
+  if (e != cudaSuccess) return e;
+  const long long tiles = (p.n + kTile - 1) / kTile;
+  const long long full = p.n / kTile;
+  bool aligned = true;
+  for (int a = 0; a < NUM_ARR; ++a)
+    if (C::has(a))
+      aligned = aligned && (reinterpret_cast<uintptr_t>(p.ptr[a]) % 16 == 0);
+  long long generic_begin = 0;
+  if (aligned && full > 0) {
+    const long long grid =
+        std::min<long long>(full, (long long)device_info().sm_count);
+    p.tile_begin = 0;
+    p.tile_end = full;
+    stream_kernel<C><<<unsigned(grid), kPersistThreads, persist_smem<C>(),
+                       stream>>>(p);
+    generic_begin = full;
+  }
+  if (generic_begin < tiles) {
+    p.tile_begin = generic_begin;
+    p.tile_end = tiles;
+    tile_kernel<C><<<unsigned(tiles - generic_begin), kConsumers,
+                     C::stage_bytes, stream>>>(p);
+  }
+  return cudaPeekAtLastError();
+}
+
+StepParams base_params(long long n) {
+  StepParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n = n;
+  return p;
+}
+
+void set_sh_inputs(StepParams& p, int degree, const float* means,
+                   const int* radii, const bool* clamped, const float* camera,
+                   const float* seed, float* dm) {
+  p.degree = degree;
+  p.ptr[MEANS] = means;
+  p.ptr[RADII] = radii;
+  p.ptr[CLAMPED] = clamped;
+  p.ptr[SEED] = seed;
+  p.ptr[DM] = dm;
+  p.camera = camera;
+}
+
+void set_split(StepParams& p, const float* coefficient, float* dc, float* rest,
+               float* dc_first, float* dc_second, float* rest_first,
+               float* rest_second) {
+  p.ptr[SNAP] = coefficient;
+  p.ptr[DC] = dc;
+  p.ptr[DC_M] = dc_first;
+  p.ptr[DC_V] = dc_second;
+  p.ptr[REST] = rest;
+  p.ptr[REST_M] = rest_first;
+  p.ptr[REST_V] = rest_second;
+}
+
+void set_torch_config(StepParams& p, TorchAdamConfig c) {
+  // rate / bias1 in double, rounded once to float, as torch fused Adam does.
+  p.sh_step_dc = float(0.0025 / double(c.bias1));
+  p.sh_step_rest = float(0.000125 / double(c.bias1));
+  p.sh_bias2 = c.bias2_sqrt;
+}
+
+void set_activations(StepParams& p, float* const* parameters,
+                     const float* const* seeds, const float* const* saved,
+                     float* const* first, float* const* second,
+                     const double* rates, const float* bias1,
+                     const float* bias2) {
+  const int params[3] = {ROT, SCL, OPA};
+  for (int j = 0; j < 3; ++j) {
+    p.ptr[params[j]] = parameters[j];
+    p.ptr[params[j] + 1] = first[j];
+    p.ptr[params[j] + 2] = second[j];
+    p.ptr[SEED_ROT + j] = seeds[j];
+    p.ptr[SAVED_NORM + j] = saved[j];
+    p.act_step[j] = float(rates[j] / double(bias1[j]));
+    p.act_bias2[j] = bias2[j];
+  }
+}
+
+bool degree_ok(int degree) { return degree >= 0 && degree <= 3; }
+
+int status_of(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return CLAD3DGS_OK;
+  cudaGetLastError();  // clear a non-sticky launch error for the next call
+  return fail(CLAD3DGS_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+using SplitTorch = Cfg<SH_SPLIT_TORCH, false, false>;
+using SplitTorchSnap = Cfg<SH_SPLIT_TORCH, false, true>;
+using SplitAdam = Cfg<SH_SPLIT_ADAM, false, false>;
+using SplitAdamSnap = Cfg<SH_SPLIT_ADAM, false, true>;
+using PackedAdam = Cfg<SH_ADAM, false, false>;
+using PackedSgd = Cfg<SH_SGD, false, false>;
+using ActOnly = Cfg<SH_NONE, true, false>;
+using Fused = Cfg<SH_SPLIT_TORCH, true, false>;
+using FusedSnap = Cfg<SH_SPLIT_TORCH, true, true>;
+
+cudaError_t run_split_torch(StepParams& p, cudaStream_t stream) {
+  return p.ptr[SNAP] ? run<SplitTorchSnap>(p, stream) : run<SplitTorch>(p, stream);
+}
+
+cudaError_t launch_quaternion(long long n, const float* q, const float* seed,
+                              const float* norms, float* out,
+                              cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const bool vec = (reinterpret_cast<uintptr_t>(q) |
+                    reinterpret_cast<uintptr_t>(seed) |
+                    reinterpret_cast<uintptr_t>(out)) % 16 == 0;
+  const long long blocks = std::min<long long>(
+      (n + 255) / 256, (long long)device_info().sm_count * 16);
+  if (vec)
+    quaternion_kernel<true><<<unsigned(blocks), 256, 0, stream>>>(n, q, seed,
+                                                                  norms, out);
+  else
+    quaternion_kernel<false><<<unsigned(blocks), 256, 0, stream>>>(n, q, seed,
+                                                                   norms, out);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace clad3dgs
+
+using namespace clad3dgs;
+
+// ===================== drop-in entries =====================
+
+extern "C" void sh_consumer_sgd(int n, int degree, const float* means,
+                                const int* radii, float* coeff,
+                                const bool* clamped, const float* camera,
+                                const float* seed, float* dm) {
+  if (n <= 0) return;
+  if (!degree_ok(degree))
+    throw std::invalid_argument("SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  p.ptr[COEF] = coeff;
+  run<PackedSgd>(p, 0);
+}
+
+extern "C" void sh_consumer_adam(int n, int degree, const float* means,
+                                 const int* radii, float* coeff,
+                                 const bool* clamped, const float* camera,
+                                 const float* seed, float* dm, float* first,
+                                 float* second, AdamConfig config) {
+  if (n <= 0) return;
+  if (!degree_ok(degree))
+    throw std::invalid_argument("SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  p.ptr[COEF] = coeff;
+  p.ptr[COEF_M] = first;
+  p.ptr[COEF_V] = second;
+  p.inv_bias1 = config.inv_bias1;
+  p.inv_bias2 = config.inv_bias2;
+  run<PackedAdam>(p, 0);
+}
+
+extern "C" void sh_consumer_split_adam(int n, int degree, const float* means,
+                                       const int* radii,
+                                       const float* coefficient,
+                                       const bool* clamped, const float* camera,
+                                       const float* seed, float* dm, float* dc,
+                                       float* rest, float* dc_first,
+                                       float* dc_second, float* rest_first,
+                                       float* rest_second, AdamConfig config) {
+  if (n <= 0) return;
+  if (!degree_ok(degree))
+    throw std::invalid_argument("SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  p.inv_bias1 = config.inv_bias1;
+  p.inv_bias2 = config.inv_bias2;
+  if (coefficient)
+    run<SplitAdamSnap>(p, 0);
+  else
+    run<SplitAdam>(p, 0);
+}
+
+extern "C" void sh_consumer_split_torch_adam(
+    int n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* dc, float* rest, float* dc_first,
+    float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig config) {
+  if (n <= 0) return;
+  if (!degree_ok(degree))
+    throw std::invalid_argument("SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  set_torch_config(p, config);
+  run_split_torch(p, 0);
+}
+
+extern "C" void launch_activation_consume(int n, float* const* parameters,
+                                          const float* const* seeds,
+                                          const float* const* saved,
+                                          float* const* first,
+                                          float* const* second,
+                                          const double* rates,
+                                          const float* bias1, const float* bias2,
+                                          cudaStream_t stream) {
+  if (n <= 0) return;
+  StepParams p = base_params(n);
+  set_activations(p, parameters, seeds, saved, first, second, rates, bias1,
+                  bias2);
+  run<ActOnly>(p, stream);
+}
+
+extern "C" void launch_quaternion_backward(int n, const float* q,
+                                           const float* seed,
+                                           const float* norms, float* out,
+                                           cudaStream_t stream) {
+  launch_quaternion(n, q, seed, norms, out, stream);
+}
+
+// ===================== clad3dgs_* entries =====================
+
+extern "C" const char* clad3dgs_last_error(void) { return t_last_error.c_str(); }
+
+extern "C" int clad3dgs_describe(int* sm_count, int* tile_gaussians,
+                                 int* sh_stages, int* fused_stages) {
+  if (sm_count) *sm_count = device_info().sm_count;
+  if (tile_gaussians) *tile_gaussians = kTile;
+  if (sh_stages) *sh_stages = SplitTorch::stages;
+  if (fused_stages) *fused_stages = Fused::stages;
+  return CLAD3DGS_OK;
+}
+
+extern "C" int clad3dgs_fault_status(int clear, unsigned int* fault_word) {
+  unsigned int word = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&word, g_fault_word, sizeof(word));
+  if (e != cudaSuccess) return status_of(e, "reading the fault word");
+  if (clear && word) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_fault_word, &zero, sizeof(zero));
+    if (e != cudaSuccess) return status_of(e, "clearing the fault word");
+  }
+  if (fault_word) *fault_word = word;
+  return word ? fail(CLAD3DGS_DEVICE_FAULT, "a pipeline wait timed out")
+              : CLAD3DGS_OK;
+}
+
+extern "C" int clad3dgs_sh_consume_split_torch_adam(
+    int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* dc, float* rest, float* dc_first,
+    float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig config, cudaStream_t stream) {
+  if (n <= 0) return CLAD3DGS_OK;
+  if (!degree_ok(degree))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  set_torch_config(p, config);
+  return status_of(run_split_torch(p, stream), "SH consume launch");
+}
+
+extern "C" int clad3dgs_sh_consume_variant(
+    int mode, int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* coeff, float* first, float* second,
+    float* dc, float* rest, float* dc_first, float* dc_second,
+    float* rest_first, float* rest_second, AdamConfig config,
+    cudaStream_t stream) {
+  if (mode < 0 || mode > 2)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "unknown SH update mode");
+  if (n <= 0) return CLAD3DGS_OK;
+  if (!degree_ok(degree))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  p.inv_bias1 = config.inv_bias1;
+  p.inv_bias2 = config.inv_bias2;
+  cudaError_t e;
+  if (mode == 0) {
+    p.ptr[COEF] = coeff;
+    e = run<PackedSgd>(p, stream);
+  } else if (mode == 1) {
+    p.ptr[COEF] = coeff;
+    p.ptr[COEF_M] = first;
+    p.ptr[COEF_V] = second;
+    e = run<PackedAdam>(p, stream);
+  } else {
+    set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+              rest_second);
+    e = coefficient ? run<SplitAdamSnap>(p, stream) : run<SplitAdam>(p, stream);
+  }
+  return status_of(e, "SH consume launch");
+}
+
+extern "C" int clad3dgs_activation_consume(int64_t n, float* const* parameters,
+                                           const float* const* seeds,
+                                           const float* const* saved,
+                                           float* const* first,
+                                           float* const* second,
+                                           const double* rates,
+                                           const float* bias1,
+                                           const float* bias2,
+                                           cudaStream_t stream) {
+  if (n <= 0) return CLAD3DGS_OK;
+  StepParams p = base_params(n);
+  set_activations(p, parameters, seeds, saved, first, second, rates, bias1,
+                  bias2);
+  return status_of(run<ActOnly>(p, stream), "activation consume launch");
+}
+
+extern "C" int clad3dgs_quaternion_backward(int64_t n, const float* q,
+                                            const float* seed,
+                                            const float* norms, float* out,
+                                            cudaStream_t stream) {
+  return status_of(launch_quaternion(n, q, seed, norms, out, stream),
+                   "quaternion backward launch");
+}
+
+extern "C" int clad3dgs_gaussian_step(
+    int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* dc, float* rest, float* dc_first,
+    float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* const* parameters,
+    const float* const* seeds, const float* const* saved, float* const* first,
+    float* const* second, const double* rates, const float* bias1,
+    const float* bias2, cudaStream_t stream) {
+  if (n <= 0) return CLAD3DGS_OK;
+  if (!degree_ok(degree))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  set_torch_config(p, sh_config);
+  set_activations(p, parameters, seeds, saved, first, second, rates, bias1,
+                  bias2);
+  cudaError_t e = coefficient ? run<FusedSnap>(p, stream) : run<Fused>(p, stream);
+  return status_of(e, "fused Gaussian step launch");
+}

@@ -1,0 +1,201 @@
+/*
+ * clad3dgs_b200.h — C ABI of the B200 (sm_100a) per-Gaussian backward-and-update path.
+ *
+ * Two groups of entry points live in libclad3dgs_b200.so:
+ *
+ *  1. Drop-in entries. Same names, argument order, argument meaning and error
+ *     behaviour as the reference's extern "C" launchers, so a renderer that
+ *     links the reference's object can link this library instead:
+ *       sh_consumer_sgd / sh_consumer_adam / sh_consumer_split_adam /
+ *       sh_consumer_split_torch_adam   (SHGradientConsumer.cu:225-283)
+ *       launch_activation_consume      (normalization.cu:104-120)
+ *       launch_quaternion_backward     (normalization.cu:122-129)
+ *     As in the reference, the SH entries launch on the legacy default stream,
+ *     treat n <= 0 as a no-op and throw std::invalid_argument for a degree
+ *     outside [0, 3] (C++ callers only; see the clad3dgs_* entries otherwise).
+ *
+ *  2. clad3dgs_* entries. Same arithmetic, explicit stream, 64-bit counts and
+ *     an int status instead of exceptions (never throw across the boundary).
+ *     clad3dgs_last_error() returns the message of the last failure on the
+ *     calling host thread.
+ *
+ * Every pointer argument is a device pointer unless its name ends in _host.
+ * Layouts are the reference's (SHGradientConsumer.md:26-33, normalization.cpp):
+ *   means[N][3], radii[N] (int32), clamped[N][3] (bool bytes), seed[N][3],
+ *   dm[N][3] (+=), dc[N][1][3], rest[N][15][3], moments shaped like their
+ *   parameter, packed coefficients[N][16][3]; rotation[N][4], scaling[N][3],
+ *   opacity[N][1] with seeds of the same shapes and saved forward values
+ *   norm[N][1], exp(scaling)[N][3], sigmoid(opacity)[N][1].
+ * Writable buffers must be disjoint from each other and from every input.
+ */
+#ifndef CLAD3DGS_B200_H
+#define CLAD3DGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Inverse Adam bias corrections 1/(1-0.9^t), 1/(1-0.999^t).
+ * Replaces AdamConfig, SHGradientConsumer.cu:11-13. */
+typedef struct AdamConfig {
+  float inv_bias1, inv_bias2;
+} AdamConfig;
+
+/* torch fused-Adam bias corrections 1-0.9^t and sqrt(1-0.999^t), rounded to float.
+ * Replaces TorchAdamConfig, SHGradientConsumer.cu:15-17. */
+typedef struct TorchAdamConfig {
+  float bias1, bias2_sqrt;
+} TorchAdamConfig;
+
+/* ---- status codes of the clad3dgs_* entries ---- */
+#define CLAD3DGS_OK 0
+#define CLAD3DGS_INVALID_ARGUMENT 1
+#define CLAD3DGS_CUDA_ERROR 2
+#define CLAD3DGS_DEVICE_FAULT 3
+
+/* ===================== drop-in entries (reference symbols) ===================== */
+
+/* SGD at lr 1e-3 on packed coeff[N][16][3]; invisible Gaussians are skipped.
+ * Replaces sh_consumer_sgd, SHGradientConsumer.cu:225-235. */
+void sh_consumer_sgd(int n, int degree, const float* means, const int* radii,
+                     float* coeff, const bool* clamped, const float* camera,
+                     const float* seed, float* dm);
+
+/* Adam (float arithmetic, AdamConfig) on packed coeff/first/second[N][16][3].
+ * Replaces sh_consumer_adam, SHGradientConsumer.cu:237-248. */
+void sh_consumer_adam(int n, int degree, const float* means, const int* radii,
+                      float* coeff, const bool* clamped, const float* camera,
+                      const float* seed, float* dm, float* first, float* second,
+                      AdamConfig config);
+
+/* Adam (float arithmetic) on split dc/rest; coefficient is an optional packed
+ * [N][16][3] snapshot read for the VJP (NULL reads dc/rest directly).
+ * Replaces sh_consumer_split_adam, SHGradientConsumer.cu:250-266. */
+void sh_consumer_split_adam(int n, int degree, const float* means,
+                            const int* radii, const float* coefficient,
+                            const bool* clamped, const float* camera,
+                            const float* seed, float* dm, float* dc, float* rest,
+                            float* dc_first, float* dc_second, float* rest_first,
+                            float* rest_second, AdamConfig config);
+
+/* torch-fused-Adam arithmetic (double beta/lr, float moments) on split dc/rest.
+ * The hot path. Replaces sh_consumer_split_torch_adam,
+ * SHGradientConsumer.cu:269-283 (bound by the renderer at prepare_native.py:120,
+ * direct_inputs.py:318). */
+void sh_consumer_split_torch_adam(int n, int degree, const float* means,
+                                  const int* radii, const float* coefficient,
+                                  const bool* clamped, const float* camera,
+                                  const float* seed, float* dm, float* dc,
+                                  float* rest, float* dc_first, float* dc_second,
+                                  float* rest_first, float* rest_second,
+                                  TorchAdamConfig config);
+
+/* Rotation/scaling/opacity activation VJPs fused with their dense Adam updates.
+ * Arrays of three: [0] rotation [N][4], [1] scaling [N][3], [2] opacity [N][1].
+ * saved = {norm [N][1], exp(scaling) [N][3], sigmoid(opacity) [N][1]}.
+ * rates are the group learning rates (double); bias1 = 1-0.9^t and
+ * bias2 = sqrt(1-0.999^t) per group (float).
+ * Replaces launch_activation_consume, normalization.cu:104-120. */
+void launch_activation_consume(int n, float* const* parameters,
+                               const float* const* seeds,
+                               const float* const* saved, float* const* first,
+                               float* const* second, const double* rates,
+                               const float* bias1, const float* bias2,
+                               cudaStream_t stream);
+
+/* VJP of q / max(|q|, 1e-12) with the clamp branch picked by the saved norm.
+ * Replaces launch_quaternion_backward, normalization.cu:122-129. */
+void launch_quaternion_backward(int n, const float* q, const float* seed,
+                                const float* norms, float* out,
+                                cudaStream_t stream);
+
+/* ========================== clad3dgs_* entries ========================== */
+
+/* Message of the last failed clad3dgs_* call on this host thread ("" if none). */
+const char* clad3dgs_last_error(void);
+
+/* Number of SMs, stages and Gaussians per tile the SH kernels use on the
+ * current device (diagnostics for benchmarks). */
+int clad3dgs_describe(int* sm_count, int* tile_gaussians, int* sh_stages,
+                      int* fused_stages);
+
+/* Reads (and clears if clear != 0) the device fault word that bounded waits
+ * set when a pipeline barrier timed out. 0 means no fault. Synchronises. */
+int clad3dgs_fault_status(int clear, unsigned int* fault_word);
+
+/* Same as sh_consumer_split_torch_adam with an explicit stream. */
+int clad3dgs_sh_consume_split_torch_adam(
+    int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* dc, float* rest, float* dc_first,
+    float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig config, cudaStream_t stream);
+
+/* mode 0 = SGD (packed), 1 = Adam (packed), 2 = split Adam (float arithmetic).
+ * Packed modes use coeff/first/second; split mode uses coefficient (optional
+ * snapshot) and dc/rest/moments. Same semantics as the drop-in entries. */
+int clad3dgs_sh_consume_variant(
+    int mode, int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* coeff, float* first, float* second,
+    float* dc, float* rest, float* dc_first, float* dc_second,
+    float* rest_first, float* rest_second, AdamConfig config,
+    cudaStream_t stream);
+
+/* Same as launch_activation_consume with a status. */
+int clad3dgs_activation_consume(int64_t n, float* const* parameters,
+                                const float* const* seeds,
+                                const float* const* saved, float* const* first,
+                                float* const* second, const double* rates,
+                                const float* bias1, const float* bias2,
+                                cudaStream_t stream);
+
+/* Same as launch_quaternion_backward with a status. */
+int clad3dgs_quaternion_backward(int64_t n, const float* q, const float* seed,
+                                 const float* norms, float* out,
+                                 cudaStream_t stream);
+
+/* One fused per-Gaussian pass: SH VJP + torch-fused Adam on dc/rest (as
+ * sh_consumer_split_torch_adam) and the activation VJPs + Adam (as
+ * launch_activation_consume), reading and writing each Gaussian once. */
+int clad3dgs_gaussian_step(
+    int64_t n, int degree, const float* means, const int* radii,
+    const float* coefficient, const bool* clamped, const float* camera,
+    const float* seed, float* dm, float* dc, float* rest, float* dc_first,
+    float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* const* parameters,
+    const float* const* seeds, const float* const* saved, float* const* first,
+    float* const* second, const double* rates, const float* bias1,
+    const float* bias2, cudaStream_t stream);
+
+/* Host-buffer variant of clad3dgs_gaussian_step for callers whose Gaussians
+ * live in (pinned) host memory. Every array pointer is a host pointer;
+ * workspace_dev is device memory of clad3dgs_host_step_workspace(chunk)
+ * bytes that the call stages chunks in. Chunks are copied in, stepped and copied back on three streams so
+ * the two copy directions and the kernel overlap; the call returns after the
+ * results are in host memory. */
+size_t clad3dgs_host_step_workspace(int64_t chunk_gaussians);
+int clad3dgs_gaussian_step_host(
+    int64_t n, int degree, const float* means_host, const int* radii_host,
+    const bool* clamped_host, const float* camera_host, const float* seed_host,
+    float* dm_host, float* dc_host, float* rest_host, float* dc_first_host,
+    float* dc_second_host, float* rest_first_host, float* rest_second_host,
+    TorchAdamConfig sh_config, float* const* parameters_host,
+    const float* const* seeds_host, const float* const* saved_host,
+    float* const* first_host, float* const* second_host, const double* rates,
+    const float* bias1, const float* bias2, void* workspace_dev,
+    size_t workspace_bytes, int64_t chunk_gaussians, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLAD3DGS_B200_H */
