@@ -48,28 +48,35 @@ __device__ unsigned int g_fault_word = 0;
 // element, everything else four.
 enum Arr : int {
   MEANS, RADII, CLAMPED, SEED, DM,
-  DC, DC_M, DC_V, REST, REST_M, REST_V, SNAP,
-  COEF, COEF_M, COEF_V,
-  ROT, ROT_M, ROT_V, SCL, SCL_M, SCL_V, OPA, OPA_M, OPA_V,
-  SEED_ROT, SEED_SCL, SEED_OPA, SAVED_NORM, SAVED_SCL, SAVED_OPA,
+  // Updated parameters, then first moments, then second moments: every tile
+  // slice is a multiple of 128 bytes, so each group is one contiguous region of
+  // the stage and phase B walks it with a single index.
+  DC, REST, COEF, ROT, SCL, OPA,
+  DC_M, REST_M, COEF_M, ROT_M, SCL_M, OPA_M,
+  DC_V, REST_V, COEF_V, ROT_V, SCL_V, OPA_V,
+  SNAP, SEED_ROT, SEED_SCL, SEED_OPA, SAVED_NORM, SAVED_SCL, SAVED_OPA,
   NUM_ARR
 };
 
-constexpr int kWidth[NUM_ARR] = {3, 1, 3, 3, 3,  3,  3, 3, 45, 45,
-                                 45, 48, 48, 48, 48, 4, 4, 4, 3,  3,
-                                 3, 1, 1, 1, 4, 3, 1, 1, 3, 1};
-constexpr bool kWritten[NUM_ARR] = {0, 0, 0, 0, 1, 1, 1, 1, 1, 1,
-                                    1, 0, 1, 1, 1, 1, 1, 1, 1, 1,
-                                    1, 1, 1, 1, 0, 0, 0, 0, 0, 0};
+constexpr int kWidth[NUM_ARR] = {3, 1, 3, 3, 3,
+                                 3, 45, 48, 4, 3, 1,
+                                 3, 45, 48, 4, 3, 1,
+                                 3, 45, 48, 4, 3, 1,
+                                 48, 4, 3, 1, 1, 3, 1};
+constexpr bool kWritten[NUM_ARR] = {0, 0, 0, 0, 1,
+                                    1, 1, 1, 1, 1, 1,
+                                    1, 1, 1, 1, 1, 1,
+                                    1, 1, 1, 1, 1, 1,
+                                    0, 0, 0, 0, 0, 0, 0};
 constexpr int elem_bytes(int a) { return a == CLAMPED ? 1 : 4; }
 
 enum ShMode : int { SH_NONE, SH_SGD, SH_ADAM, SH_SPLIT_ADAM, SH_SPLIT_TORCH };
 
 constexpr int kTile = 64;                 // Gaussians per tile
-constexpr int kConsumers = 256;           // 8 consumer warps
+constexpr int kConsumers = 512;           // 16 consumer warps
 constexpr int kPersistThreads = kConsumers + 32;  // + 1 producer warp
 constexpr int kMaxStages = 8;
-constexpr uint32_t kStageBudget = 220u * 1024u;   // dynamic smem for stages
+constexpr uint32_t kStageBudget = 200u * 1024u;   // dynamic smem for stages
 
 constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
@@ -83,10 +90,16 @@ struct Cfg {
       return Sh != SH_NONE;
     if (a == COEF) return Sh == SH_SGD || Sh == SH_ADAM;
     if (a == COEF_M || a == COEF_V) return Sh == SH_ADAM;
-    if (a >= DC && a <= REST_V) return Sh == SH_SPLIT_ADAM || Sh == SH_SPLIT_TORCH;
+    if (a == DC || a == REST || a == DC_M || a == REST_M || a == DC_V || a == REST_V)
+      return Sh == SH_SPLIT_ADAM || Sh == SH_SPLIT_TORCH;
     if (a == SNAP) return Snap && (Sh == SH_SPLIT_ADAM || Sh == SH_SPLIT_TORCH);
-    return Act;  // ROT .. SAVED_OPA
+    return Act;  // activation parameters, moments, seeds, saved values
   }
+  // Updated elements per Gaussian (parameters of every group, in region order).
+  static constexpr int kDc = has(DC) ? 3 : 0, kRest = has(REST) ? 45 : 0,
+                       kCoef = has(COEF) ? 48 : 0, kRot = Act ? 4 : 0,
+                       kScl = Act ? 3 : 0, kOpa = Act ? 1 : 0;
+  static constexpr int kParams = kDc + kRest + kCoef + kRot + kScl + kOpa;
   static constexpr uint32_t tile_bytes(int a) {
     return uint32_t(kTile) * kWidth[a] * elem_bytes(a);
   }
@@ -150,12 +163,65 @@ struct Stage {
 };
 
 // ---------------------------------------------------------------------------
-// Arithmetic on one staged tile.
+// Arithmetic on one staged tile, in two phases.
+//
+// Phase A (per Gaussian and SH term): consumer warp w owns terms {r, r+8}
+// (r = w mod 8) of 32 consecutive Gaussians (lane = Gaussian); it writes the
+// coefficient gradients b_j * seed into a gradient tile laid out like the
+// parameter region, and the direction adjoint of its two terms, t_r + t_{r+8},
+// into `partial`. Warps with r = 0..2 also write the rotation / scaling /
+// opacity VJPs. The term index is warp-uniform and compile-time after an
+// 8-way dispatch, so there is no divergent 16-way switch; rows of 45 (rest) or
+// 3 (dc) floats are odd strides, so these accesses are bank-conflict free.
+//
+// Phase B (per element): all consumers walk the parameter region of the tile
+// (dc, rest, rotation, scaling, opacity share one index with the moments and
+// the gradient tile) with one compact Adam update: independent elements,
+// unit-stride shared memory, 7 elements per thread for a full fused tile. The
+// position adjoint is finished by the r = 0 warps in the reference's
+// shuffle-tree order ((t0+t8)+(t4+t12)) + ((t2+t10)+(t6+t14)) + ...
+// (SHGradientConsumer.cu:203-207).
+
+// Per-CTA scratch shared by the consumers (one copy, reused every tile).
+struct Scratch {
+  float partial[8][kTile][3];  // t_r + t_{r+8} of every Gaussian
+  float grad[kTile * 56];      // gradients, laid out like the parameter region
+  int abort;                   // set by a consumer whose wait timed out
+};
+
+template <class C>
+constexpr bool kSplit = C::kSh == SH_SPLIT_ADAM || C::kSh == SH_SPLIT_TORCH;
+
+// Element offsets of each group inside the parameter (and gradient) region.
+template <class C>
+struct Region {
+  static constexpr int kRest = kTile * C::kDc;
+  static constexpr int kRot = kTile * (C::kDc + C::kRest + C::kCoef);
+  static constexpr int kScl = kRot + kTile * C::kRot;
+  static constexpr int kOpa = kScl + kTile * C::kScl;
+  static constexpr int kTotal = kTile * C::kParams;
+  static constexpr int first_of(int a0, int a1, int a2, int a3, int a4, int a5) {
+    return C::has(a0) ? a0 : C::has(a1) ? a1 : C::has(a2) ? a2
+         : C::has(a3) ? a3 : C::has(a4) ? a4 : a5;
+  }
+  static constexpr int kParamArr = first_of(DC, REST, COEF, ROT, SCL, OPA);
+  static constexpr int kFirstArr = first_of(DC_M, REST_M, COEF_M, ROT_M, SCL_M, OPA_M);
+  static constexpr int kSecondArr = first_of(DC_V, REST_V, COEF_V, ROT_V, SCL_V, OPA_V);
+};
+
+// Offset of term J, channel 0, of local Gaussian gl in the gradient tile.
+template <class C, int J>
+__device__ __forceinline__ int grad_offset(int gl) {
+  if constexpr (kSplit<C>)
+    return J == 0 ? gl * 3 : Region<C>::kRest + gl * 45 + 3 * (J - 1);
+  else
+    return gl * 48 + 3 * J;
+}
 
 template <class C, int J>
 __device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
                                                           int gl) {
-  if constexpr (C::kSh == SH_SGD || C::kSh == SH_ADAM) {
+  if constexpr (!kSplit<C>) {
     return st.template f<COEF>() + gl * 48 + 3 * J;
   } else if constexpr (C::kSnap) {
     return st.template f<SNAP>() + gl * 48 + 3 * J;
@@ -166,51 +232,15 @@ __device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
   }
 }
 
+// One SH term of one Gaussian: coefficient gradient into the gradient tile,
+// direction adjoint into dd. Inactive terms (invisible Gaussian or above the
+// degree) get a zero gradient, which still advances Adam.
 template <class C, int J>
-__device__ __forceinline__ void term_update(const StepParams& p,
-                                            const Stage<C>& st, int gl,
-                                            const float g[3]) {
-  if constexpr (C::kSh == SH_SPLIT_TORCH || C::kSh == SH_SPLIT_ADAM) {
-    float* pp = J == 0 ? st.template f<DC>() + gl * 3
-                       : st.template f<REST>() + gl * 45 + 3 * (J - 1);
-    float* mm = J == 0 ? st.template f<DC_M>() + gl * 3
-                       : st.template f<REST_M>() + gl * 45 + 3 * (J - 1);
-    float* vv = J == 0 ? st.template f<DC_V>() + gl * 3
-                       : st.template f<REST_V>() + gl * 45 + 3 * (J - 1);
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) {
-      if constexpr (C::kSh == SH_SPLIT_TORCH)
-        torch_adam(pp[ch], mm[ch], vv[ch], g[ch],
-                   J == 0 ? p.sh_step_dc : p.sh_step_rest, p.sh_bias2);
-      else
-        float_adam(pp[ch], mm[ch], vv[ch], g[ch], J == 0 ? kDcRate : kRestRate,
-                   p.inv_bias1, p.inv_bias2);
-    }
-  } else if constexpr (C::kSh == SH_ADAM) {
-    const int o = gl * 48 + 3 * J;
-    float* pp = st.template f<COEF>() + o;
-    float* mm = st.template f<COEF_M>() + o;
-    float* vv = st.template f<COEF_V>() + o;
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch)
-      float_adam(pp[ch], mm[ch], vv[ch], g[ch], J == 0 ? kDcRate : kRestRate,
-                 p.inv_bias1, p.inv_bias2);
-  } else {
-    float* pp = st.template f<COEF>() + gl * 48 + 3 * J;
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) sgd(pp[ch], g[ch]);
-  }
-}
-
-// One SH term of one Gaussian: coefficient gradient into the update, direction
-// adjoint into dd. Inactive terms (invisible Gaussian or above the degree)
-// still update the optimizer with a zero gradient.
-template <class C, int J>
-__device__ __forceinline__ void term_step(const StepParams& p,
-                                          const Stage<C>& st, int gl,
-                                          bool active, const Direction& d,
-                                          const float s[3], float dd[3]) {
-  float g[3] = {0.f, 0.f, 0.f};
+__device__ __forceinline__ void term_gradient(const Stage<C>& st, Scratch& sc,
+                                              int gl, bool active,
+                                              const Direction& d,
+                                              const float s[3], float dd[3]) {
+  float* g = sc.grad + grad_offset<C, J>(gl);
   dd[0] = dd[1] = dd[2] = 0.f;
   if (active) {
     float b, gx, gy, gz;
@@ -223,112 +253,210 @@ __device__ __forceinline__ void term_step(const StepParams& p,
     g[0] = b * s[0];
     g[1] = b * s[1];
     g[2] = b * s[2];
+  } else {
+    g[0] = g[1] = g[2] = 0.f;
   }
-  term_update<C, J>(p, st, gl, g);
 }
 
 template <class C, int R>
-__device__ __forceinline__ void sh_role(const StepParams& p, const Stage<C>& st,
-                                        int gl, bool visible, int nterms,
-                                        const Direction& d, const float s[3],
-                                        float part[3]) {
-  float t0[3], t1[3], t2[3], t3[3];
-  term_step<C, R>(p, st, gl, visible && R < nterms, d, s, t0);
-  term_step<C, R + 4>(p, st, gl, visible && R + 4 < nterms, d, s, t1);
-  term_step<C, R + 8>(p, st, gl, visible && R + 8 < nterms, d, s, t2);
-  term_step<C, R + 12>(p, st, gl, visible && R + 12 < nterms, d, s, t3);
+__device__ __forceinline__ void sh_role(const Stage<C>& st, Scratch& sc, int gl,
+                                        bool visible, int nterms,
+                                        const Direction& d, const float s[3]) {
+  float lo[3], hi[3];
+  term_gradient<C, R>(st, sc, gl, visible && R < nterms, d, s, lo);
+  term_gradient<C, R + 8>(st, sc, gl, visible && R + 8 < nterms, d, s, hi);
 #pragma unroll
-  for (int k = 0; k < 3; ++k) part[k] = (t0[k] + t2[k]) + (t1[k] + t3[k]);
+  for (int k = 0; k < 3; ++k) sc.partial[R][gl][k] = lo[k] + hi[k];
 }
 
 template <class C>
-__device__ __forceinline__ void process_tile(const StepParams& p,
-                                             const Stage<C>& st, int cnt,
-                                             int ct, float (*partial)[kTile][3],
-                                             const float cam[3]) {
+__device__ __forceinline__ void activation_gradients(const Stage<C>& st,
+                                                     Scratch& sc, int gl,
+                                                     int role) {
+  using R = Region<C>;
+  if (role == 0) {
+    const float* q = st.template f<ROT>() + 4 * gl;
+    const float* sq = st.template f<SEED_ROT>() + 4 * gl;
+    const float norm = st.template f<SAVED_NORM>()[gl];
+    float qr[4], sr[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      qr[k] = q[k];
+      sr[k] = sq[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      sc.grad[R::kRot + 4 * gl + k] = quaternion_vjp(qr, sr, norm, k);
+  } else if (role == 1) {
+    const float* ss = st.template f<SEED_SCL>() + 3 * gl;
+    const float* se = st.template f<SAVED_SCL>() + 3 * gl;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) sc.grad[R::kScl + 3 * gl + k] = se[k] * ss[k];
+  } else if (role == 2) {
+    const float a = st.template f<SAVED_OPA>()[gl];
+    sc.grad[R::kOpa + gl] = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
+  }
+}
+
+// Phase A. `ready` is false for a consumer whose stage wait timed out.
+template <class C>
+__device__ __forceinline__ void phase_gradients(const StepParams& p,
+                                                const Stage<C>& st, Scratch& sc,
+                                                int cnt, int ct,
+                                                const float cam[3], bool ready,
+                                                Direction& d, bool& visible) {
   const int cw = ct >> 5, lane = ct & 31;
-  const int gl = ((cw >> 2) << 5) + lane;  // local Gaussian of this thread
-  const int role = cw & 3;                 // warp-uniform
-  const bool valid = gl < cnt;
+  const int gl = ((cw >> 3) << 5) + lane;
+  const int role = cw & 7;  // warp-uniform
+  visible = false;
+  if (!ready || gl >= cnt) return;
   if constexpr (C::kSh != SH_NONE) {
-    float part[3] = {0.f, 0.f, 0.f};
-    bool visible = false;
-    Direction d{};
-    if (valid) {
-      visible = st.template i<RADII>()[gl] > 0;
-      if (C::kSh != SH_SGD || visible) {
-        float s[3] = {0.f, 0.f, 0.f};
-        if (visible) {
-          const float* m = st.template f<MEANS>() + 3 * gl;
-          d = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
-          const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
-          const float* sd = st.template f<SEED>() + 3 * gl;
+    visible = st.template i<RADII>()[gl] > 0;
+    float s[3] = {0.f, 0.f, 0.f};
+    if (visible) {
+      const float* m = st.template f<MEANS>() + 3 * gl;
+      d = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
+      const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
+      const float* sd = st.template f<SEED>() + 3 * gl;
 #pragma unroll
-          for (int ch = 0; ch < 3; ++ch) s[ch] = cl[ch] ? 0.f : sd[ch];
-        }
-        const int nterms = (p.degree + 1) * (p.degree + 1);
-        switch (role) {
-          case 0: sh_role<C, 0>(p, st, gl, visible, nterms, d, s, part); break;
-          case 1: sh_role<C, 1>(p, st, gl, visible, nterms, d, s, part); break;
-          case 2: sh_role<C, 2>(p, st, gl, visible, nterms, d, s, part); break;
-          default: sh_role<C, 3>(p, st, gl, visible, nterms, d, s, part); break;
-        }
-      }
+      for (int ch = 0; ch < 3; ++ch) s[ch] = cl[ch] ? 0.f : sd[ch];
     }
-    partial[role][gl][0] = part[0];
-    partial[role][gl][1] = part[1];
-    partial[role][gl][2] = part[2];
-    named_barrier(1, kConsumers);
-    if (role == 0 && valid && visible) {
-      float dd[3];
-#pragma unroll
-      for (int k = 0; k < 3; ++k)
-        dd[k] = (partial[0][gl][k] + partial[2][gl][k]) +
-                (partial[1][gl][k] + partial[3][gl][k]);
-      float o[3];
-      direction_vjp(d, dd[0], dd[1], dd[2], o[0], o[1], o[2]);
-      float* dm = st.template f<DM>() + 3 * gl;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
+    const int nterms = (p.degree + 1) * (p.degree + 1);
+    switch (role) {
+      case 0: sh_role<C, 0>(st, sc, gl, visible, nterms, d, s); break;
+      case 1: sh_role<C, 1>(st, sc, gl, visible, nterms, d, s); break;
+      case 2: sh_role<C, 2>(st, sc, gl, visible, nterms, d, s); break;
+      case 3: sh_role<C, 3>(st, sc, gl, visible, nterms, d, s); break;
+      case 4: sh_role<C, 4>(st, sc, gl, visible, nterms, d, s); break;
+      case 5: sh_role<C, 5>(st, sc, gl, visible, nterms, d, s); break;
+      case 6: sh_role<C, 6>(st, sc, gl, visible, nterms, d, s); break;
+      default: sh_role<C, 7>(st, sc, gl, visible, nterms, d, s); break;
     }
   }
-  if constexpr (C::kAct) {
-    if (valid) {
-      if (role == 1) {
-        float* q = st.template f<ROT>() + 4 * gl;
-        float* qm = st.template f<ROT_M>() + 4 * gl;
-        float* qv = st.template f<ROT_V>() + 4 * gl;
-        const float* sq = st.template f<SEED_ROT>() + 4 * gl;
-        const float norm = st.template f<SAVED_NORM>()[gl];
-        float qr[4], sr[4], g[4];
+  if constexpr (C::kAct) activation_gradients<C>(st, sc, gl, role);
+}
+
+// Position adjoint of the r = 0 warps, after phase A.
+template <class C>
+__device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
+                                                int cnt, int ct,
+                                                const Direction& d,
+                                                bool visible) {
+  if constexpr (C::kSh != SH_NONE) {
+    const int cw = ct >> 5;
+    const int gl = ((cw >> 3) << 5) + (ct & 31);
+    if ((cw & 7) != 0 || gl >= cnt || !visible) return;
+    float dd[3];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          qr[k] = q[k];
-          sr[k] = sq[k];
-        }
+    for (int k = 0; k < 3; ++k)
+      dd[k] = ((sc.partial[0][gl][k] + sc.partial[4][gl][k]) +
+               (sc.partial[2][gl][k] + sc.partial[6][gl][k])) +
+              ((sc.partial[1][gl][k] + sc.partial[5][gl][k]) +
+               (sc.partial[3][gl][k] + sc.partial[7][gl][k]));
+    float o[3];
+    direction_vjp(d, dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+    float* dm = st.template f<DM>() + 3 * gl;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) g[k] = quaternion_vjp(qr, sr, norm, k);
+    for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
+  }
+}
+
+// Phase B: one update per element of the parameter region. Slots past the
+// tile's Gaussian count are updated too and never stored.
+template <class C>
+__device__ __forceinline__ void update_element(const StepParams& p,
+                                               const Stage<C>& st, int e,
+                                               float& pe, float& me, float& ve,
+                                               float g) {
+  using R = Region<C>;
+  if constexpr (C::kSh == SH_SPLIT_TORCH || C::kSh == SH_NONE) {
+    float step = 0.f, bias2 = 1.f;
+    if constexpr (C::kSh == SH_SPLIT_TORCH) {
+      step = e < R::kRest ? p.sh_step_dc : p.sh_step_rest;
+      bias2 = p.sh_bias2;
+    }
+    if constexpr (C::kAct) {
+      if (C::kSh == SH_NONE || e >= R::kRot) {
+        const int group = e < R::kScl ? 0 : (e < R::kOpa ? 1 : 2);
+        step = p.act_step[group];
+        bias2 = p.act_bias2[group];
+      }
+    }
+    torch_adam(pe, me, ve, g, step, bias2);
+  } else if constexpr (C::kSh == SH_SPLIT_ADAM) {
+    float_adam(pe, me, ve, g, e < R::kRest ? kDcRate : kRestRate, p.inv_bias1,
+               p.inv_bias2);
+  } else if constexpr (C::kSh == SH_ADAM) {
+    float_adam(pe, me, ve, g, (e % 48) < 3 ? kDcRate : kRestRate, p.inv_bias1,
+               p.inv_bias2);
+  } else {
+    // SGD leaves invisible Gaussians untouched (SHGradientConsumer.cu:93).
+    if (st.template i<RADII>()[e / 48] > 0) sgd(pe, g);
+  }
+}
+
+template <class C>
+__device__ __forceinline__ void phase_update(const StepParams& p,
+                                             const Stage<C>& st,
+                                             const Scratch& sc, int ct) {
+  using R = Region<C>;
+  constexpr bool kMoments = C::kSh != SH_SGD;
+  float* P = st.template f<R::kParamArr>();
+  float* M = kMoments ? st.template f<R::kFirstArr>() : nullptr;
+  float* V = kMoments ? st.template f<R::kSecondArr>() : nullptr;
+  constexpr int kRounds = (R::kTotal + kConsumers - 1) / kConsumers;
+  constexpr bool kExact = R::kTotal % kConsumers == 0;
+  float pv[kRounds], mv[kRounds], vv[kRounds], gv[kRounds];
+  // All loads, then the arithmetic, then all stores: the elements are
+  // independent, which the compiler cannot prove through shared pointers.
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          torch_adam(q[k], qm[k], qv[k], g[k], p.act_step[0], p.act_bias2[0]);
-      } else if (role == 2) {
-        float* sc = st.template f<SCL>() + 3 * gl;
-        float* sm = st.template f<SCL_M>() + 3 * gl;
-        float* sv = st.template f<SCL_V>() + 3 * gl;
-        const float* ss = st.template f<SEED_SCL>() + 3 * gl;
-        const float* se = st.template f<SAVED_SCL>() + 3 * gl;
-#pragma unroll
-        for (int k = 0; k < 3; ++k)
-          torch_adam(sc[k], sm[k], sv[k], se[k] * ss[k], p.act_step[1],
-                     p.act_bias2[1]);
-      } else if (role == 3) {
-        const float a = st.template f<SAVED_OPA>()[gl];
-        const float g = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
-        torch_adam(st.template f<OPA>()[gl], st.template f<OPA_M>()[gl],
-                   st.template f<OPA_V>()[gl], g, p.act_step[2], p.act_bias2[2]);
+  for (int k = 0; k < kRounds; ++k) {
+    const int e = ct + k * kConsumers;
+    pv[k] = gv[k] = mv[k] = vv[k] = 0.f;
+    if (kExact || e < R::kTotal) {
+      pv[k] = P[e];
+      gv[k] = sc.grad[e];
+      if constexpr (kMoments) {
+        mv[k] = M[e];
+        vv[k] = V[e];
       }
     }
   }
+#pragma unroll
+  for (int k = 0; k < kRounds; ++k) {
+    const int e = ct + k * kConsumers;
+    if (kExact || e < R::kTotal)
+      update_element<C>(p, st, e, pv[k], mv[k], vv[k], gv[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < kRounds; ++k) {
+    const int e = ct + k * kConsumers;
+    if (kExact || e < R::kTotal) {
+      P[e] = pv[k];
+      if constexpr (kMoments) {
+        M[e] = mv[k];
+        V[e] = vv[k];
+      }
+    }
+  }
+}
+
+// Phases A and B with the barrier between them; returns false (on every
+// consumer) if some consumer's stage wait timed out.
+template <class C>
+__device__ __forceinline__ bool process_tile(const StepParams& p,
+                                             const Stage<C>& st, Scratch& sc,
+                                             int cnt, int ct,
+                                             const float cam[3], bool ready) {
+  Direction d{};
+  bool visible = false;
+  if (!ready) sc.abort = 1;
+  phase_gradients<C>(p, st, sc, cnt, ct, cam, ready, d, visible);
+  named_barrier(1, kConsumers);
+  if (sc.abort) return false;
+  finish_position<C>(st, sc, cnt, ct, d, visible);
+  phase_update<C>(p, st, sc, ct);
+  return true;
 }
 
 template <class C>
@@ -343,15 +471,14 @@ __device__ __forceinline__ void load_camera(const StepParams& p, float cam[3]) {
 }
 
 // ---------------------------------------------------------------------------
-// Persistent pipeline: warp 0 lane 0 produces, warps 1..8 consume.
+// Persistent pipeline: warp 0 lane 0 produces, warps 1..16 consume.
 template <class C>
 __global__ void __launch_bounds__(kPersistThreads, 1)
     stream_kernel(const StepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full_bar[C::stages];
   __shared__ __align__(8) uint64_t empty_bar[C::stages];
-  __shared__ float partial[4][kTile][3];
-  __shared__ int stage_ok;
+  __shared__ Scratch scratch;
   constexpr int S = C::stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -359,6 +486,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
+    scratch.abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -394,16 +522,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   int k = 0;
   for (long long t = first; t < p.tile_end; t += stride, ++k) {
     const int s = k % S;
-    const uint32_t parity = (k / S) & 1;
-    if (ct == 0) stage_ok = mbar_wait_bounded(&full_bar[s], parity) ? 1 : 0;
-    named_barrier(1, kConsumers);
-    if (!stage_ok) {
-      if (ct == 0) atomicOr(&g_fault_word, kFaultConsumerWait);
-      break;
-    }
-    (void)mbar_try_wait(&full_bar[s], parity);  // acquire for this thread
+    const bool ready = mbar_wait_bounded(&full_bar[s], (k / S) & 1);
+    if (!ready && ct == 0) atomicOr(&g_fault_word, kFaultConsumerWait);
     Stage<C> st{smem + size_t(s) * C::stage_bytes};
-    process_tile<C>(p, st, kTile, ct, partial, cam);
+    if (!process_tile<C>(p, st, scratch, kTile, ct, cam, ready)) break;
     fence_async_shared();
     named_barrier(1, kConsumers);
     if (ct == 0) {
@@ -431,11 +553,12 @@ template <class C>
 __global__ void __launch_bounds__(kConsumers)
     tile_kernel(const StepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ float partial[4][kTile][3];
+  __shared__ Scratch scratch;
   const long long tile = p.tile_begin + blockIdx.x;
   const long long g0 = tile * kTile;
   const int cnt = int(min((long long)kTile, p.n - g0));
   Stage<C> st{smem};
+  if (threadIdx.x == 0) scratch.abort = 0;
   for_each_arr([&](auto a_) {
     constexpr int a = decltype(a_)::value;
     if constexpr (C::has(a)) {
@@ -456,7 +579,7 @@ __global__ void __launch_bounds__(kConsumers)
   float cam[3];
   load_camera<C>(p, cam);
   __syncthreads();
-  process_tile<C>(p, st, cnt, threadIdx.x, partial, cam);
+  process_tile<C>(p, st, scratch, cnt, threadIdx.x, cam, true);
   __syncthreads();
   for_each_arr([&](auto a_) {
     constexpr int a = decltype(a_)::value;
@@ -553,6 +676,12 @@ cudaError_t run(StepParams p, cudaStream_t stream) {
   if (p.n <= 0) return cudaSuccess;
   cudaError_t e = configure_kernels<C>();
   if (e != cudaSuccess) return e;
+  // Every array this configuration stages must be given; never launch with a
+  // missing one.
+  for (int a = 0; a < NUM_ARR; ++a)
+    if (C::has(a) && p.ptr[a] == nullptr) return cudaErrorInvalidDevicePointer;
+  if constexpr (C::kSh != SH_NONE)
+    if (p.camera == nullptr) return cudaErrorInvalidDevicePointer;
   const long long tiles = (p.n + kTile - 1) / kTile;
   const long long full = p.n / kTile;
   bool aligned = true;
@@ -621,13 +750,17 @@ void set_activations(StepParams& p, float* const* parameters,
                      float* const* first, float* const* second,
                      const double* rates, const float* bias1,
                      const float* bias2) {
-  const int params[3] = {ROT, SCL, OPA};
+  constexpr int kParam[3] = {ROT, SCL, OPA};
+  constexpr int kFirst[3] = {ROT_M, SCL_M, OPA_M};
+  constexpr int kSecond[3] = {ROT_V, SCL_V, OPA_V};
+  constexpr int kSeed[3] = {SEED_ROT, SEED_SCL, SEED_OPA};
+  constexpr int kSaved[3] = {SAVED_NORM, SAVED_SCL, SAVED_OPA};
   for (int j = 0; j < 3; ++j) {
-    p.ptr[params[j]] = parameters[j];
-    p.ptr[params[j] + 1] = first[j];
-    p.ptr[params[j] + 2] = second[j];
-    p.ptr[SEED_ROT + j] = seeds[j];
-    p.ptr[SAVED_NORM + j] = saved[j];
+    p.ptr[kParam[j]] = parameters[j];
+    p.ptr[kFirst[j]] = first[j];
+    p.ptr[kSecond[j]] = second[j];
+    p.ptr[kSeed[j]] = seeds[j];
+    p.ptr[kSaved[j]] = saved[j];
     p.act_step[j] = float(rates[j] / double(bias1[j]));
     p.act_bias2[j] = bias2[j];
   }
