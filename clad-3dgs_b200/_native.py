@@ -54,6 +54,10 @@ _SIGNATURES = {
                                     + [_PP] * 5 + [POINTER(c_double), POINTER(c_float),
                                                    POINTER(c_float), _P, c_size_t, c_int64,
                                                    _P]),
+    "clad3dgs_gaussian_step_host_static": (c_int, [c_int64, c_int] + [_P] * 12
+                                           + [TorchAdamConfig] + [_PP] * 5
+                                           + [POINTER(c_double), POINTER(c_float),
+                                              POINTER(c_float), c_int64, _P]),
 }
 
 _lock = threading.Lock()

@@ -197,3 +197,134 @@ extern "C" int clad3dgs_gaussian_step_host(
   }
   return CLAD3DGS_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the staging set lives in a fixed device array.
+
+namespace {
+
+// One staging set plus the camera, for callers that cannot allocate.
+static __device__ __align__(256) unsigned char
+    g_static_staging[CLAD3DGS_STATIC_STAGING_BYTES];
+
+std::mutex g_static_lock;
+void* g_static_address[64] = {};  // device address of g_static_staging, per device
+
+// Largest multiple of 64 Gaussians whose staging set and camera fit the array.
+int64_t static_chunk_limit() {
+  int64_t chunk = (CLAD3DGS_STATIC_STAGING_BYTES / 1451) / 64 * 64;
+  while (chunk > 0 && set_bytes(chunk) + kAlign > CLAD3DGS_STATIC_STAGING_BYTES)
+    chunk -= 64;
+  return chunk;
+}
+
+}  // namespace
+
+extern "C" int clad3dgs_gaussian_step_host_static(
+    int64_t n, int degree, const float* means_host, const int* radii_host,
+    const bool* clamped_host, const float* camera_host, const float* seed_host,
+    float* dm_host, float* dc_host, float* rest_host, float* dc_first_host,
+    float* dc_second_host, float* rest_first_host, float* rest_second_host,
+    TorchAdamConfig sh_config, float* const* parameters_host,
+    const float* const* seeds_host, const float* const* saved_host,
+    float* const* first_host, float* const* second_host, const double* rates,
+    const float* bias1, const float* bias2, int64_t chunk_gaussians,
+    cudaStream_t stream) {
+  const int64_t limit = static_chunk_limit();
+  if (chunk_gaussians == 0) chunk_gaussians = limit;
+  if (chunk_gaussians < 0 || chunk_gaussians % 64 || chunk_gaussians > limit)
+    return clad3dgs::fail(
+        CLAD3DGS_INVALID_ARGUMENT,
+        "static host step: chunk of " + std::to_string(chunk_gaussians) +
+            " Gaussians does not fit the fixed staging area of " +
+            std::to_string(CLAD3DGS_STATIC_STAGING_BYTES) +
+            " bytes; use a multiple of 64 up to " + std::to_string(limit) +
+            " (or 0 for that maximum)");
+  if (degree < 0 || degree > 3)
+    return clad3dgs::fail(CLAD3DGS_INVALID_ARGUMENT,
+                          "SH degree must be between zero and three");
+  if (n <= 0) return CLAD3DGS_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return clad3dgs::fail(CLAD3DGS_CUDA_ERROR, cudaGetErrorString(e));
+  char* ws = nullptr;
+  {
+    // Set-up, once per device with that device current: the array's name is
+    // only a host-side handle; its device address comes from the runtime.
+    std::lock_guard<std::mutex> guard(g_static_lock);
+    void*& address = g_static_address[dev & 63];
+    if (address == nullptr) {
+      e = cudaGetSymbolAddress(&address, g_static_staging);
+      if (e != cudaSuccess) {
+        address = nullptr;
+        return clad3dgs::fail(CLAD3DGS_CUDA_ERROR,
+                              std::string("static staging address: ") +
+                                  cudaGetErrorString(e));
+      }
+    }
+    ws = static_cast<char*>(address);
+  }
+  const void* host[S_COUNT] = {
+      means_host,         radii_host,         clamped_host,
+      seed_host,          dm_host,            dc_host,
+      dc_first_host,      dc_second_host,     rest_host,
+      rest_first_host,    rest_second_host,   parameters_host[0],
+      first_host[0],      second_host[0],     parameters_host[1],
+      first_host[1],      second_host[1],     parameters_host[2],
+      first_host[2],      second_host[2],     seeds_host[0],
+      seeds_host[1],      seeds_host[2],      saved_host[0],
+      saved_host[1],      saved_host[2]};
+  char* dev_slot[S_COUNT];
+  char* cursor = ws;
+  for (int s = 0; s < S_COUNT; ++s) {
+    dev_slot[s] = cursor;
+    cursor += round_up(size_t(chunk_gaussians) * kSlotWidth[s] * slot_elem(s));
+  }
+  float* camera_dev = reinterpret_cast<float*>(cursor);
+  auto check = [&](cudaError_t err) {
+    if (err != cudaSuccess && e == cudaSuccess) e = err;
+  };
+  check(cudaMemcpyAsync(camera_dev, camera_host, 3 * sizeof(float),
+                        cudaMemcpyHostToDevice, stream));
+  const int64_t chunks = (n + chunk_gaussians - 1) / chunk_gaussians;
+  for (int64_t c = 0; c < chunks && e == cudaSuccess; ++c) {
+    // One staging set, one stream: chunk c's copy-in is ordered after chunk
+    // c-1's copy-out.
+    const int64_t g0 = c * chunk_gaussians;
+    const int64_t cnt = (n - g0) < chunk_gaussians ? (n - g0) : chunk_gaussians;
+    for (int s = 0; s < S_COUNT; ++s) {
+      const size_t row = kSlotWidth[s] * slot_elem(s);
+      check(cudaMemcpyAsync(dev_slot[s], static_cast<const char*>(host[s]) + g0 * row,
+                            size_t(cnt) * row, cudaMemcpyHostToDevice, stream));
+    }
+    if (e != cudaSuccess) break;
+    auto f = [&](int s) { return reinterpret_cast<float*>(dev_slot[s]); };
+    float* params[3] = {f(S_ROT), f(S_SCL), f(S_OPA)};
+    float* firsts[3] = {f(S_ROT_M), f(S_SCL_M), f(S_OPA_M)};
+    float* seconds[3] = {f(S_ROT_V), f(S_SCL_V), f(S_OPA_V)};
+    const float* seeds[3] = {f(S_SEED_ROT), f(S_SEED_SCL), f(S_SEED_OPA)};
+    const float* saved[3] = {f(S_NORM), f(S_EXPS), f(S_SIG)};
+    const int status = clad3dgs_gaussian_step(
+        cnt, degree, f(S_MEANS), reinterpret_cast<int*>(dev_slot[S_RADII]), nullptr,
+        reinterpret_cast<bool*>(dev_slot[S_CLAMPED]), camera_dev, f(S_SEED), f(S_DM),
+        f(S_DC), f(S_REST), f(S_DC_M), f(S_DC_V), f(S_REST_M), f(S_REST_V), sh_config,
+        params, seeds, saved, firsts, seconds, rates, bias1, bias2, stream);
+    if (status != CLAD3DGS_OK) {
+      cudaStreamSynchronize(stream);
+      return status;
+    }
+    for (int s = 0; s < S_COUNT; ++s) {
+      if (!kSlotOut[s]) continue;
+      const size_t row = kSlotWidth[s] * slot_elem(s);
+      check(cudaMemcpyAsync(static_cast<char*>(const_cast<void*>(host[s])) + g0 * row,
+                            dev_slot[s], size_t(cnt) * row, cudaMemcpyDeviceToHost,
+                            stream));
+    }
+  }
+  check(cudaStreamSynchronize(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return clad3dgs::fail(CLAD3DGS_CUDA_ERROR, cudaGetErrorString(e));
+  }
+  return CLAD3DGS_OK;
+}

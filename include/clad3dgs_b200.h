@@ -194,6 +194,40 @@ int clad3dgs_gaussian_step_host(
     const float* bias1, const float* bias2, void* workspace_dev,
     size_t workspace_bytes, int64_t chunk_gaussians, cudaStream_t stream);
 
+/* Size of the fixed device staging area used by
+ * clad3dgs_gaussian_step_host_static (bytes, on every GPU that loads this
+ * library, held until the process exits). */
+#define CLAD3DGS_STATIC_STAGING_BYTES (48u << 20)
+
+/* Host-buffer fused step that allocates nothing. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc, e.g. code
+ * embedded in a host application that owns all device memory through its own
+ * allocator or a fixed memory budget (where a library-side allocation can fail
+ * or break the host's accounting), and hot loops that must not pay for an
+ * allocation's implicit device synchronisation.
+ * Same arguments and results as clad3dgs_gaussian_step_host, without the
+ * workspace: chunks are staged in a file-scope device array of
+ * CLAD3DGS_STATIC_STAGING_BYTES bytes instead. chunk_gaussians = 0 picks the
+ * largest chunk that fits; a larger explicit chunk is rejected with
+ * CLAD3DGS_INVALID_ARGUMENT (the message gives the limit), as is a chunk that is
+ * not a multiple of 64. Copies and kernels run on `stream` only (no streams or
+ * events are created); the call returns when the results are in host memory.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. Every call
+ * on a device shares the one array, so calls that overlap on the GPU (from two
+ * host threads or two streams) race; nothing in it needs clearing, since each
+ * call copies in every staged byte it reads. */
+int clad3dgs_gaussian_step_host_static(
+    int64_t n, int degree, const float* means_host, const int* radii_host,
+    const bool* clamped_host, const float* camera_host, const float* seed_host,
+    float* dm_host, float* dc_host, float* rest_host, float* dc_first_host,
+    float* dc_second_host, float* rest_first_host, float* rest_second_host,
+    TorchAdamConfig sh_config, float* const* parameters_host,
+    const float* const* seeds_host, const float* const* saved_host,
+    float* const* first_host, float* const* second_host, const double* rates,
+    const float* bias1, const float* bias2, int64_t chunk_gaussians,
+    cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
