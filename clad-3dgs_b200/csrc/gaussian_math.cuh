@@ -162,14 +162,25 @@ constexpr double kOneMinusBeta1 = 1.0 - kBeta1;
 constexpr double kOneMinusBeta2 = 1.0 - kBeta2;
 
 // torch fused Adam: double beta arithmetic, float moments, float step size
-// (rate / bias1 rounded once), double epsilon added to the float ratio.
+// (rate / bias1 rounded once), double epsilon added to the float ratio
+// sqrt(v) / bias2.
+//
+// The division by the per-group constant bias2 is evaluated as
+// (float)(sqrt(v) * inv_bias2) with inv_bias2 = 1/(double)bias2 rounded to
+// double on the host. That is the correctly rounded float quotient: the exact
+// quotient of two floats is never a float midpoint and lies at least 2^-49
+// (relative) from one, while the double product is within 2^-52 of it, so
+// rounding to float lands on the same value (division by a constant known in
+// advance; Brisebarre, Muller, Raina, IEEE Trans. Computers 53(8), 2004). The
+// oracle divides directly; the bit-exact tests compare the two.
 __device__ __forceinline__ void torch_adam(float& p, float& m, float& v,
                                            float g, float step,
-                                           float bias2_sqrt) {
+                                           double inv_bias2) {
   const double gd = (double)g;
   m = (float)(kBeta1 * (double)m + kOneMinusBeta1 * gd);
   v = (float)(kBeta2 * (double)v + (kOneMinusBeta2 * gd) * gd);
-  const float denom = (float)((double)(sqrtf(v) / bias2_sqrt) + kEps);
+  const float ratio = (float)((double)sqrtf(v) * inv_bias2);
+  const float denom = (float)((double)ratio + kEps);
   p = p - (step * m) / denom;
 }
 
@@ -186,16 +197,24 @@ __device__ __forceinline__ void sgd(float& p, float g) { p = p - 1e-3f * g; }
 
 constexpr float kDcRate = 0.0025f, kRestRate = 0.000125f;
 
-// VJP of q / max(|q|, 1e-12) for one component k; the saved forward norm picks
-// the clamp branch and is used on both sides of it.
-__device__ __forceinline__ float quaternion_vjp(const float q[4],
-                                                const float s[4], float norm,
-                                                int k) {
-  if (norm < 1e-12f) return s[k] / 1e-12f;
+// VJP of q / max(|q|, 1e-12) for all four components; the saved forward norm
+// picks the clamp branch and is used on both sides of it.
+__device__ __forceinline__ void quaternion_vjp(const float q[4],
+                                               const float s[4], float norm,
+                                               float out[4]) {
+  if (norm < 1e-12f) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[k] = s[k] / 1e-12f;
+    return;
+  }
+  float qn[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qn[j] = q[j] / norm;
   float dot = 0.f;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) dot = dot + (q[j] / norm) * s[j];
-  return (s[k] - (q[k] / norm) * dot) / norm;
+  for (int j = 0; j < 4; ++j) dot = dot + qn[j] * s[j];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = (s[k] - qn[k] * dot) / norm;
 }
 
 }  // namespace clad3dgs

@@ -5,24 +5,22 @@
 // (normalization.cu:79-101) and the fused pass that does both. Data layout and
 // schedule:
 //
-//  * Gaussians are processed in tiles of kTile = 64. For each tile every array
+//  * Gaussians are processed in tiles of kTile = 32. For each tile every array
 //    the mode touches (means, radii, clamped, seeds, dm, dc/rest and their two
 //    moments, activation parameters/moments/seeds/saved values) is one
 //    contiguous byte range in HBM, so a tile is fetched with one 1D bulk copy
 //    (cp.async.bulk, the TMA engine) per array into shared memory and written
 //    back the same way. There are no per-lane 12-byte accesses.
-//  * The main kernel is persistent: one CTA per SM, a ring of stages in shared
-//    memory, one producer thread issuing bulk loads ahead and eight consumer
-//    warps doing the arithmetic. Stage reuse is gated by mbarriers, write-back
-//    by bulk-store groups, so HBM reads, compute and HBM writes overlap.
-//  * Inside a tile, warp w of the consumers owns SH terms {r, r+4, r+8, r+12}
-//    (r = w mod 4) for 32 consecutive Gaussians (lane = Gaussian). The term
-//    index is warp-uniform and compile-time after a 4-way dispatch, so there is
-//    no divergent 16-way switch. Shared-memory rows of 45 (rest) or 3 (dc)
-//    floats are odd strides, so these accesses are bank-conflict free.
-//  * The direction adjoint is reduced in the reference's order
-//    ((t_r + t_{r+8}) + (t_{r+4} + t_{r+12})) in registers, then
-//    (v0 + v2) + (v1 + v3) through shared memory (SHGradientConsumer.cu:203-207).
+//  * The main kernel is persistent: kCtasPerSm CTAs per SM, each with a ring of
+//    stages in shared memory, one producer thread issuing bulk loads ahead and
+//    sixteen consumer warps doing the arithmetic. Stage reuse is gated by
+//    mbarriers, write-back by bulk-store groups, so HBM reads, compute and HBM
+//    writes overlap, and one CTA's barrier waits overlap another's arithmetic.
+//  * Per tile: the view direction of each Gaussian is computed once (phase A0),
+//    warp j then owns SH term j for the 32 Gaussians of the tile (phase A1, lane
+//    = Gaussian, compile-time term, no divergent switch), and all consumers run
+//    one compact Adam update per parameter element (phase B). See "Arithmetic on
+//    one staged tile" below.
 //  * The tail tile and inputs that are not 16-byte aligned go through a plain
 //    one-tile-per-CTA kernel with the same arithmetic.
 #include <algorithm>
@@ -72,11 +70,25 @@ constexpr int elem_bytes(int a) { return a == CLAMPED ? 1 : 4; }
 
 enum ShMode : int { SH_NONE, SH_SGD, SH_ADAM, SH_SPLIT_ADAM, SH_SPLIT_TORCH };
 
-constexpr int kTile = 64;                 // Gaussians per tile
-constexpr int kConsumers = 512;           // 16 consumer warps
+// Tile size and resident persistent CTAs per SM. Several independent CTAs per
+// SM let one CTA's barrier waits overlap another's arithmetic.
+#ifndef CLAD3DGS_TILE
+#define CLAD3DGS_TILE 32
+#endif
+#ifndef CLAD3DGS_CTAS_PER_SM
+#define CLAD3DGS_CTAS_PER_SM 2
+#endif
+constexpr int kTile = CLAD3DGS_TILE;              // Gaussians per tile
+constexpr int kCtasPerSm = CLAD3DGS_CTAS_PER_SM;  // persistent CTAs per SM
+constexpr int kConsumers = 512;                  // 16 warps: one per SH term
 constexpr int kPersistThreads = kConsumers + 32;  // + 1 producer warp
 constexpr int kMaxStages = 8;
-constexpr uint32_t kStageBudget = 200u * 1024u;   // dynamic smem for stages
+static_assert(kTile == 32, "one lane per Gaussian of a tile");
+// Dynamic shared memory for the stages of one CTA: the SM's 228 KB shared
+// across kCtasPerSm CTAs, less each CTA's static scratch and reserve.
+constexpr uint32_t kStageBudget =
+    (226u * 1024u) / kCtasPerSm - (16u * kTile * 3u + 56u * kTile + 16u * kTile) * 4u -
+    1536u;
 
 constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
@@ -130,9 +142,11 @@ struct StepParams {
   long long tile_end;    // one past the last tile of this launch
   const float* camera;   // device, 3 floats
   int degree;
-  float sh_step_dc, sh_step_rest, sh_bias2;  // torch Adam on dc / rest
+  float sh_step_dc, sh_step_rest;            // torch Adam on dc / rest
+  double sh_inv_bias2;                       // 1 / bias2_sqrt, rounded to double
   float inv_bias1, inv_bias2;                // float Adam (AdamConfig)
-  float act_step[3], act_bias2[3];           // rotation, scaling, opacity
+  float act_step[3];                         // rotation, scaling, opacity
+  double act_inv_bias2[3];
 };
 
 template <class F, int... Is>
@@ -163,30 +177,31 @@ struct Stage {
 };
 
 // ---------------------------------------------------------------------------
-// Arithmetic on one staged tile, in two phases.
+// Arithmetic on one staged tile (kTile Gaussians, 16 consumer warps).
 //
-// Phase A (per Gaussian and SH term): consumer warp w owns terms {r, r+8}
-// (r = w mod 8) of 32 consecutive Gaussians (lane = Gaussian); it writes the
-// coefficient gradients b_j * seed into a gradient tile laid out like the
-// parameter region, and the direction adjoint of its two terms, t_r + t_{r+8},
-// into `partial`. Warps with r = 0..2 also write the rotation / scaling /
-// opacity VJPs. The term index is warp-uniform and compile-time after an
-// 8-way dispatch, so there is no divergent 16-way switch; rows of 45 (rest) or
-// 3 (dc) floats are odd strides, so these accesses are bank-conflict free.
-//
-// Phase B (per element): all consumers walk the parameter region of the tile
-// (dc, rest, rotation, scaling, opacity share one index with the moments and
-// the gradient tile) with one compact Adam update: independent elements,
-// unit-stride shared memory, 7 elements per thread for a full fused tile. The
-// position adjoint is finished by the r = 0 warps in the reference's
+// Phase A0: warp 0 (lane = Gaussian) computes each Gaussian's visibility, view
+// direction and masked colour seed once; warps 1-3 compute the rotation /
+// scaling / opacity VJPs meanwhile.
+// Phase A1: warp j owns SH term j of every Gaussian of the tile (lane =
+// Gaussian): it writes the coefficient gradient b_j * seed into a gradient tile
+// laid out like the parameter region and the term's direction adjoint t_j into
+// `partial`. The term index is warp-uniform and compile-time after a 16-way
+// dispatch, so there is no divergent switch; rows of 45 (rest) or 3 (dc)
+// floats are odd strides, so these accesses are bank-conflict free.
+// Phase B: warp 0 finishes the position adjoint with the reference's
 // shuffle-tree order ((t0+t8)+(t4+t12)) + ((t2+t10)+(t6+t14)) + ...
-// (SHGradientConsumer.cu:203-207).
+// (SHGradientConsumer.cu:203-207) while all consumers walk the parameter region
+// (dc, rest, rotation, scaling, opacity share one index with the moments and
+// the gradient tile) with one compact Adam update per element.
 
 // Per-CTA scratch shared by the consumers (one copy, reused every tile).
 struct Scratch {
-  float partial[8][kTile][3];  // t_r + t_{r+8} of every Gaussian
-  float grad[kTile * 56];      // gradients, laid out like the parameter region
-  int abort;                   // set by a consumer whose wait timed out
+  float partial[16][kTile][3];  // direction adjoint of every term
+  float grad[kTile * 56];       // gradients, laid out like the parameter region
+  Direction dir[kTile];         // view direction of every Gaussian
+  float seed[kTile][3];         // clamped-masked colour seed
+  int visible[kTile];
+  int abort;                    // set by a consumer whose wait timed out
 };
 
 template <class C>
@@ -232,129 +247,130 @@ __device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
   }
 }
 
-// One SH term of one Gaussian: coefficient gradient into the gradient tile,
-// direction adjoint into dd. Inactive terms (invisible Gaussian or above the
-// degree) get a zero gradient, which still advances Adam.
+// Phase A1 for term J of local Gaussian gl. Inactive terms (invisible
+// Gaussian or above the degree) get a zero gradient, which still advances Adam.
 template <class C, int J>
 __device__ __forceinline__ void term_gradient(const Stage<C>& st, Scratch& sc,
-                                              int gl, bool active,
-                                              const Direction& d,
-                                              const float s[3], float dd[3]) {
+                                              int gl, int nterms) {
   float* g = sc.grad + grad_offset<C, J>(gl);
-  dd[0] = dd[1] = dd[2] = 0.f;
-  if (active) {
+  float* t = sc.partial[J][gl];
+  if (sc.visible[gl] && J < nterms) {
+    const Direction& d = sc.dir[gl];
+    const float* s = sc.seed[gl];
     float b, gx, gy, gz;
     sh_basis<J>(d, b, gx, gy, gz);
     const float* c = term_coefficients<C, J>(st, gl);
     const float dot = (c[0] * s[0] + c[1] * s[1]) + c[2] * s[2];
-    dd[0] = gx * dot;
-    dd[1] = gy * dot;
-    dd[2] = gz * dot;
+    t[0] = gx * dot;
+    t[1] = gy * dot;
+    t[2] = gz * dot;
     g[0] = b * s[0];
     g[1] = b * s[1];
     g[2] = b * s[2];
   } else {
+    t[0] = t[1] = t[2] = 0.f;
     g[0] = g[1] = g[2] = 0.f;
   }
 }
 
-template <class C, int R>
-__device__ __forceinline__ void sh_role(const Stage<C>& st, Scratch& sc, int gl,
-                                        bool visible, int nterms,
-                                        const Direction& d, const float s[3]) {
-  float lo[3], hi[3];
-  term_gradient<C, R>(st, sc, gl, visible && R < nterms, d, s, lo);
-  term_gradient<C, R + 8>(st, sc, gl, visible && R + 8 < nterms, d, s, hi);
-#pragma unroll
-  for (int k = 0; k < 3; ++k) sc.partial[R][gl][k] = lo[k] + hi[k];
-}
-
+// Phase A0. Returns nothing; `ready` is false for a consumer whose stage wait
+// timed out (it then only joins the barriers).
 template <class C>
-__device__ __forceinline__ void activation_gradients(const Stage<C>& st,
-                                                     Scratch& sc, int gl,
-                                                     int role) {
+__device__ __forceinline__ void phase_directions(const Stage<C>& st, Scratch& sc,
+                                                 int cnt, int ct,
+                                                 const float cam[3]) {
   using R = Region<C>;
-  if (role == 0) {
-    const float* q = st.template f<ROT>() + 4 * gl;
-    const float* sq = st.template f<SEED_ROT>() + 4 * gl;
-    const float norm = st.template f<SAVED_NORM>()[gl];
-    float qr[4], sr[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      qr[k] = q[k];
-      sr[k] = sq[k];
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      sc.grad[R::kRot + 4 * gl + k] = quaternion_vjp(qr, sr, norm, k);
-  } else if (role == 1) {
-    const float* ss = st.template f<SEED_SCL>() + 3 * gl;
-    const float* se = st.template f<SAVED_SCL>() + 3 * gl;
-#pragma unroll
-    for (int k = 0; k < 3; ++k) sc.grad[R::kScl + 3 * gl + k] = se[k] * ss[k];
-  } else if (role == 2) {
-    const float a = st.template f<SAVED_OPA>()[gl];
-    sc.grad[R::kOpa + gl] = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
-  }
-}
-
-// Phase A. `ready` is false for a consumer whose stage wait timed out.
-template <class C>
-__device__ __forceinline__ void phase_gradients(const StepParams& p,
-                                                const Stage<C>& st, Scratch& sc,
-                                                int cnt, int ct,
-                                                const float cam[3], bool ready,
-                                                Direction& d, bool& visible) {
-  const int cw = ct >> 5, lane = ct & 31;
-  const int gl = ((cw >> 3) << 5) + lane;
-  const int role = cw & 7;  // warp-uniform
-  visible = false;
-  if (!ready || gl >= cnt) return;
+  const int cw = ct >> 5, gl = ct & 31;
+  if (gl >= cnt) return;
   if constexpr (C::kSh != SH_NONE) {
-    visible = st.template i<RADII>()[gl] > 0;
-    float s[3] = {0.f, 0.f, 0.f};
-    if (visible) {
-      const float* m = st.template f<MEANS>() + 3 * gl;
-      d = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
-      const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
-      const float* sd = st.template f<SEED>() + 3 * gl;
+    if (cw == 0) {
+      const bool visible = st.template i<RADII>()[gl] > 0;
+      sc.visible[gl] = visible;
+      if (visible) {
+        const float* m = st.template f<MEANS>() + 3 * gl;
+        sc.dir[gl] = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
+        const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
+        const float* sd = st.template f<SEED>() + 3 * gl;
 #pragma unroll
-      for (int ch = 0; ch < 3; ++ch) s[ch] = cl[ch] ? 0.f : sd[ch];
-    }
-    const int nterms = (p.degree + 1) * (p.degree + 1);
-    switch (role) {
-      case 0: sh_role<C, 0>(st, sc, gl, visible, nterms, d, s); break;
-      case 1: sh_role<C, 1>(st, sc, gl, visible, nterms, d, s); break;
-      case 2: sh_role<C, 2>(st, sc, gl, visible, nterms, d, s); break;
-      case 3: sh_role<C, 3>(st, sc, gl, visible, nterms, d, s); break;
-      case 4: sh_role<C, 4>(st, sc, gl, visible, nterms, d, s); break;
-      case 5: sh_role<C, 5>(st, sc, gl, visible, nterms, d, s); break;
-      case 6: sh_role<C, 6>(st, sc, gl, visible, nterms, d, s); break;
-      default: sh_role<C, 7>(st, sc, gl, visible, nterms, d, s); break;
+        for (int ch = 0; ch < 3; ++ch) sc.seed[gl][ch] = cl[ch] ? 0.f : sd[ch];
+      }
     }
   }
-  if constexpr (C::kAct) activation_gradients<C>(st, sc, gl, role);
+  if constexpr (C::kAct) {
+    if (cw == 1) {
+      const float* q = st.template f<ROT>() + 4 * gl;
+      const float* sq = st.template f<SEED_ROT>() + 4 * gl;
+      float qr[4], sr[4], out[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        qr[k] = q[k];
+        sr[k] = sq[k];
+      }
+      quaternion_vjp(qr, sr, st.template f<SAVED_NORM>()[gl], out);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sc.grad[R::kRot + 4 * gl + k] = out[k];
+    } else if (cw == 2) {
+      const float* ss = st.template f<SEED_SCL>() + 3 * gl;
+      const float* se = st.template f<SAVED_SCL>() + 3 * gl;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) sc.grad[R::kScl + 3 * gl + k] = se[k] * ss[k];
+    } else if (cw == 3) {
+      const float a = st.template f<SAVED_OPA>()[gl];
+      sc.grad[R::kOpa + gl] = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
+    }
+  }
 }
 
-// Position adjoint of the r = 0 warps, after phase A.
+// Phase A1.
+template <class C>
+__device__ __forceinline__ void phase_terms(const StepParams& p,
+                                            const Stage<C>& st, Scratch& sc,
+                                            int cnt, int ct) {
+  if constexpr (C::kSh != SH_NONE) {
+    const int term = ct >> 5, gl = ct & 31;  // term is warp-uniform
+    if (gl >= cnt) return;
+    if (C::kSh == SH_SGD && !sc.visible[gl]) return;  // SGD skips invisible
+    const int nterms = (p.degree + 1) * (p.degree + 1);
+    switch (term) {
+      case 0: term_gradient<C, 0>(st, sc, gl, nterms); break;
+      case 1: term_gradient<C, 1>(st, sc, gl, nterms); break;
+      case 2: term_gradient<C, 2>(st, sc, gl, nterms); break;
+      case 3: term_gradient<C, 3>(st, sc, gl, nterms); break;
+      case 4: term_gradient<C, 4>(st, sc, gl, nterms); break;
+      case 5: term_gradient<C, 5>(st, sc, gl, nterms); break;
+      case 6: term_gradient<C, 6>(st, sc, gl, nterms); break;
+      case 7: term_gradient<C, 7>(st, sc, gl, nterms); break;
+      case 8: term_gradient<C, 8>(st, sc, gl, nterms); break;
+      case 9: term_gradient<C, 9>(st, sc, gl, nterms); break;
+      case 10: term_gradient<C, 10>(st, sc, gl, nterms); break;
+      case 11: term_gradient<C, 11>(st, sc, gl, nterms); break;
+      case 12: term_gradient<C, 12>(st, sc, gl, nterms); break;
+      case 13: term_gradient<C, 13>(st, sc, gl, nterms); break;
+      case 14: term_gradient<C, 14>(st, sc, gl, nterms); break;
+      default: term_gradient<C, 15>(st, sc, gl, nterms); break;
+    }
+  }
+}
+
+// Position adjoint (warp 0, lane = Gaussian), after phase A1.
 template <class C>
 __device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
-                                                int cnt, int ct,
-                                                const Direction& d,
-                                                bool visible) {
+                                                int cnt, int ct) {
   if constexpr (C::kSh != SH_NONE) {
-    const int cw = ct >> 5;
-    const int gl = ((cw >> 3) << 5) + (ct & 31);
-    if ((cw & 7) != 0 || gl >= cnt || !visible) return;
+    const int gl = ct & 31;
+    if ((ct >> 5) != 0 || gl >= cnt || !sc.visible[gl]) return;
     float dd[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k)
-      dd[k] = ((sc.partial[0][gl][k] + sc.partial[4][gl][k]) +
-               (sc.partial[2][gl][k] + sc.partial[6][gl][k])) +
-              ((sc.partial[1][gl][k] + sc.partial[5][gl][k]) +
-               (sc.partial[3][gl][k] + sc.partial[7][gl][k]));
+    for (int k = 0; k < 3; ++k) {
+      float v[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        v[r] = (sc.partial[r][gl][k] + sc.partial[r + 8][gl][k]) +
+               (sc.partial[r + 4][gl][k] + sc.partial[r + 12][gl][k]);
+      dd[k] = (v[0] + v[2]) + (v[1] + v[3]);
+    }
     float o[3];
-    direction_vjp(d, dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+    direction_vjp(sc.dir[gl], dd[0], dd[1], dd[2], o[0], o[1], o[2]);
     float* dm = st.template f<DM>() + 3 * gl;
 #pragma unroll
     for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
@@ -370,19 +386,20 @@ __device__ __forceinline__ void update_element(const StepParams& p,
                                                float g) {
   using R = Region<C>;
   if constexpr (C::kSh == SH_SPLIT_TORCH || C::kSh == SH_NONE) {
-    float step = 0.f, bias2 = 1.f;
+    float step = 0.f;
+    double inv_bias2 = 1.0;
     if constexpr (C::kSh == SH_SPLIT_TORCH) {
       step = e < R::kRest ? p.sh_step_dc : p.sh_step_rest;
-      bias2 = p.sh_bias2;
+      inv_bias2 = p.sh_inv_bias2;
     }
     if constexpr (C::kAct) {
       if (C::kSh == SH_NONE || e >= R::kRot) {
         const int group = e < R::kScl ? 0 : (e < R::kOpa ? 1 : 2);
         step = p.act_step[group];
-        bias2 = p.act_bias2[group];
+        inv_bias2 = p.act_inv_bias2[group];
       }
     }
-    torch_adam(pe, me, ve, g, step, bias2);
+    torch_adam(pe, me, ve, g, step, inv_bias2);
   } else if constexpr (C::kSh == SH_SPLIT_ADAM) {
     float_adam(pe, me, ve, g, e < R::kRest ? kDcRate : kRestRate, p.inv_bias1,
                p.inv_bias2);
@@ -441,20 +458,20 @@ __device__ __forceinline__ void phase_update(const StepParams& p,
   }
 }
 
-// Phases A and B with the barrier between them; returns false (on every
+// Phases A0, A1 and B with barriers between them; returns false (on every
 // consumer) if some consumer's stage wait timed out.
 template <class C>
 __device__ __forceinline__ bool process_tile(const StepParams& p,
                                              const Stage<C>& st, Scratch& sc,
                                              int cnt, int ct,
                                              const float cam[3], bool ready) {
-  Direction d{};
-  bool visible = false;
   if (!ready) sc.abort = 1;
-  phase_gradients<C>(p, st, sc, cnt, ct, cam, ready, d, visible);
+  else phase_directions<C>(st, sc, cnt, ct, cam);
   named_barrier(1, kConsumers);
   if (sc.abort) return false;
-  finish_position<C>(st, sc, cnt, ct, d, visible);
+  phase_terms<C>(p, st, sc, cnt, ct);
+  if constexpr (C::kSh != SH_NONE) named_barrier(1, kConsumers);
+  finish_position<C>(st, sc, cnt, ct);
   phase_update<C>(p, st, sc, ct);
   return true;
 }
@@ -471,9 +488,9 @@ __device__ __forceinline__ void load_camera(const StepParams& p, float cam[3]) {
 }
 
 // ---------------------------------------------------------------------------
-// Persistent pipeline: warp 0 lane 0 produces, warps 1..16 consume.
+// Persistent pipeline: warp 0 lane 0 produces, the other warps consume.
 template <class C>
-__global__ void __launch_bounds__(kPersistThreads, 1)
+__global__ void __launch_bounds__(kPersistThreads, kCtasPerSm)
     stream_kernel(const StepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full_bar[C::stages];
@@ -617,8 +634,7 @@ __global__ void quaternion_kernel(long long n, const float* __restrict__ q,
       }
     }
     const float norm = norms[i];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r[k] = quaternion_vjp(qv, sv, norm, k);
+    quaternion_vjp(qv, sv, norm, r);
     if constexpr (Vec) {
       reinterpret_cast<float4*>(out)[i] = make_float4(r[0], r[1], r[2], r[3]);
     } else {
@@ -691,7 +707,7 @@ cudaError_t run(StepParams p, cudaStream_t stream) {
   long long generic_begin = 0;
   if (aligned && full > 0) {
     const long long grid =
-        std::min<long long>(full, (long long)device_info().sm_count);
+        std::min<long long>(full, (long long)device_info().sm_count * kCtasPerSm);
     p.tile_begin = 0;
     p.tile_end = full;
     stream_kernel<C><<<unsigned(grid), kPersistThreads, persist_smem<C>(),
@@ -742,7 +758,7 @@ void set_torch_config(StepParams& p, TorchAdamConfig c) {
   // rate / bias1 in double, rounded once to float, as torch fused Adam does.
   p.sh_step_dc = float(0.0025 / double(c.bias1));
   p.sh_step_rest = float(0.000125 / double(c.bias1));
-  p.sh_bias2 = c.bias2_sqrt;
+  p.sh_inv_bias2 = 1.0 / double(c.bias2_sqrt);
 }
 
 void set_activations(StepParams& p, float* const* parameters,
@@ -762,7 +778,7 @@ void set_activations(StepParams& p, float* const* parameters,
     p.ptr[kSeed[j]] = seeds[j];
     p.ptr[kSaved[j]] = saved[j];
     p.act_step[j] = float(rates[j] / double(bias1[j]));
-    p.act_bias2[j] = bias2[j];
+    p.act_inv_bias2[j] = 1.0 / double(bias2[j]);
   }
 }
 
