@@ -15,9 +15,11 @@ enum FaultCode : unsigned {
   kFaultConsumerWait = 2u,   // consumers timed out waiting for a full stage
 };
 
-// try_wait suspends for a bounded, hardware-defined time per attempt; this many
-// attempts is far longer (seconds) than any launch here and still terminates.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every wait is bounded: a try_wait sleeps at most kSuspendHintNs (it wakes
+// as soon as the phase completes), and a wait gives up after kSpinLimit tries,
+// i.e. after at most about five seconds, far longer than any launch here.
+constexpr uint32_t kSuspendHintNs = 20000;
+constexpr uint32_t kSpinLimit = 1u << 18;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,10 +54,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }

@@ -180,7 +180,10 @@ __device__ __forceinline__ void torch_adam(float& p, float& m, float& v,
   m = (float)(kBeta1 * (double)m + kOneMinusBeta1 * gd);
   v = (float)(kBeta2 * (double)v + (kOneMinusBeta2 * gd) * gd);
   const float ratio = (float)((double)sqrtf(v) * inv_bias2);
-  const float denom = (float)((double)ratio + kEps);
+  // fl32(ratio + 1e-15) equals ratio whenever ratio >= 2^-25: half an ulp of
+  // such a ratio is at least 2^-49 (about 1.78e-15), more than 1e-15, even after
+  // the intermediate rounding to double. Only smaller ratios need the sum.
+  const float denom = ratio >= 0x1p-25f ? ratio : (float)((double)ratio + kEps);
   p = p - (step * m) / denom;
 }
 

@@ -11,7 +11,7 @@
 //    contiguous byte range in HBM, so a tile is fetched with one 1D bulk copy
 //    (cp.async.bulk, the TMA engine) per array into shared memory and written
 //    back the same way. There are no per-lane 12-byte accesses.
-//  * The main kernel is persistent: kCtasPerSm CTAs per SM, each with a ring of
+//  * The main kernel is persistent: up to three CTAs per SM, each with a ring of
 //    stages in shared memory, one producer thread issuing bulk loads ahead and
 //    sixteen consumer warps doing the arithmetic. Stage reuse is gated by
 //    mbarriers, write-back by bulk-store groups, so HBM reads, compute and HBM
@@ -79,17 +79,17 @@ enum ShMode : int { SH_NONE, SH_SGD, SH_ADAM, SH_SPLIT_ADAM, SH_SPLIT_TORCH };
 #define CLAD3DGS_CTAS_PER_SM 2
 #endif
 constexpr int kTile = CLAD3DGS_TILE;              // Gaussians per tile
-constexpr int kCtasPerSm = CLAD3DGS_CTAS_PER_SM;  // persistent CTAs per SM
+constexpr int kMaxCtasPerSm = CLAD3DGS_CTAS_PER_SM;  // cap on persistent CTAs per SM
 constexpr int kConsumers = 512;                  // 16 warps: one per SH term
 constexpr int kPersistThreads = kConsumers + 32;  // + 1 producer warp
 constexpr int kMaxStages = 8;
 static_assert(kTile == 32, "one lane per Gaussian of a tile");
-// Dynamic shared memory for the stages of one CTA: the SM's 228 KB shared
-// across kCtasPerSm CTAs, less each CTA's static scratch and reserve.
-constexpr uint32_t kStageBudget =
-    (226u * 1024u) / kCtasPerSm - (16u * kTile * 3u + 56u * kTile + 16u * kTile) * 4u -
-    1536u;
-
+// Dynamic shared memory for the stages of one CTA when `ctas` CTAs share an
+// SM's 226 KB: less each CTA's static scratch and a reserve.
+constexpr uint32_t stage_budget(int ctas) {
+  return (226u * 1024u) / ctas -
+         (16u * kTile * 3u + 56u * kTile + 16u * kTile) * 4u - 1536u;
+}
 constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 template <int Sh, bool Act, bool Snap>
@@ -128,9 +128,16 @@ struct Cfg {
       if (has(a)) s += tile_bytes(a);
     return s;
   }
+  // As many CTAs per SM (up to the cap) as still get two stages each, then as
+  // many stages per CTA as fit.
+  static constexpr int ctas_fitting(int c) {
+    return (c <= 1 || stage_budget(c) / stage_bytes >= 2) ? c : ctas_fitting(c - 1);
+  }
+  static constexpr int ctas = ctas_fitting(kMaxCtasPerSm);
   static constexpr int stages =
-      (kStageBudget / stage_bytes) > kMaxStages ? kMaxStages
-                                                : int(kStageBudget / stage_bytes);
+      (stage_budget(ctas) / stage_bytes) > kMaxStages
+          ? kMaxStages
+          : int(stage_budget(ctas) / stage_bytes);
   static_assert(stages >= 2, "stage does not fit twice in shared memory");
 };
 
@@ -195,10 +202,11 @@ struct Stage {
 // the gradient tile) with one compact Adam update per element.
 
 // Per-CTA scratch shared by the consumers (one copy, reused every tile).
-struct Scratch {
+struct __align__(16) Scratch {
   float partial[16][kTile][3];  // direction adjoint of every term
-  float grad[kTile * 56];       // gradients, laid out like the parameter region
-  Direction dir[kTile];         // view direction of every Gaussian
+  __align__(16) float grad[kTile * 56];  // gradients, laid out like the parameters
+  float dir[10][kTile];         // view direction of every Gaussian (x, y, z,
+                                // r, xx, yy, zz, xy, yz, xz), one row per field
   float seed[kTile][3];         // clamped-masked colour seed
   int visible[kTile];
   int abort;                    // set by a consumer whose wait timed out
@@ -247,6 +255,22 @@ __device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
   }
 }
 
+__device__ __forceinline__ void store_direction(Scratch& sc, int gl,
+                                                const Direction& d) {
+  const float f[10] = {d.x, d.y, d.z, d.r, d.xx, d.yy, d.zz, d.xy, d.yz, d.xz};
+#pragma unroll
+  for (int k = 0; k < 10; ++k) sc.dir[k][gl] = f[k];
+}
+
+__device__ __forceinline__ Direction load_direction(const Scratch& sc, int gl) {
+  Direction d;
+  d.x = sc.dir[0][gl]; d.y = sc.dir[1][gl]; d.z = sc.dir[2][gl];
+  d.r = sc.dir[3][gl]; d.xx = sc.dir[4][gl]; d.yy = sc.dir[5][gl];
+  d.zz = sc.dir[6][gl]; d.xy = sc.dir[7][gl]; d.yz = sc.dir[8][gl];
+  d.xz = sc.dir[9][gl];
+  return d;
+}
+
 // Phase A1 for term J of local Gaussian gl. Inactive terms (invisible
 // Gaussian or above the degree) get a zero gradient, which still advances Adam.
 template <class C, int J>
@@ -255,7 +279,7 @@ __device__ __forceinline__ void term_gradient(const Stage<C>& st, Scratch& sc,
   float* g = sc.grad + grad_offset<C, J>(gl);
   float* t = sc.partial[J][gl];
   if (sc.visible[gl] && J < nterms) {
-    const Direction& d = sc.dir[gl];
+    const Direction d = load_direction(sc, gl);
     const float* s = sc.seed[gl];
     float b, gx, gy, gz;
     sh_basis<J>(d, b, gx, gy, gz);
@@ -288,7 +312,7 @@ __device__ __forceinline__ void phase_directions(const Stage<C>& st, Scratch& sc
       sc.visible[gl] = visible;
       if (visible) {
         const float* m = st.template f<MEANS>() + 3 * gl;
-        sc.dir[gl] = make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]);
+        store_direction(sc, gl, make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]));
         const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
         const float* sd = st.template f<SEED>() + 3 * gl;
 #pragma unroll
@@ -370,7 +394,7 @@ __device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
       dd[k] = (v[0] + v[2]) + (v[1] + v[3]);
     }
     float o[3];
-    direction_vjp(sc.dir[gl], dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+    direction_vjp(load_direction(sc, gl), dd[0], dd[1], dd[2], o[0], o[1], o[2]);
     float* dm = st.template f<DM>() + 3 * gl;
 #pragma unroll
     for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
@@ -379,11 +403,13 @@ __device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
 
 // Phase B: one update per element of the parameter region. Slots past the
 // tile's Gaussian count are updated too and never stored.
+// Per-element updates of one float4 group; the group's region fixes the step
+// size (every region is a multiple of four elements long).
 template <class C>
-__device__ __forceinline__ void update_element(const StepParams& p,
-                                               const Stage<C>& st, int e,
-                                               float& pe, float& me, float& ve,
-                                               float g) {
+__device__ __forceinline__ void update_group(const StepParams& p,
+                                             const Stage<C>& st, int e,
+                                             float4& pv, float4& mv, float4& vv,
+                                             const float4& gv) {
   using R = Region<C>;
   if constexpr (C::kSh == SH_SPLIT_TORCH || C::kSh == SH_NONE) {
     float step = 0.f;
@@ -399,61 +425,64 @@ __device__ __forceinline__ void update_element(const StepParams& p,
         inv_bias2 = p.act_inv_bias2[group];
       }
     }
-    torch_adam(pe, me, ve, g, step, inv_bias2);
+    torch_adam(pv.x, mv.x, vv.x, gv.x, step, inv_bias2);
+    torch_adam(pv.y, mv.y, vv.y, gv.y, step, inv_bias2);
+    torch_adam(pv.z, mv.z, vv.z, gv.z, step, inv_bias2);
+    torch_adam(pv.w, mv.w, vv.w, gv.w, step, inv_bias2);
   } else if constexpr (C::kSh == SH_SPLIT_ADAM) {
-    float_adam(pe, me, ve, g, e < R::kRest ? kDcRate : kRestRate, p.inv_bias1,
-               p.inv_bias2);
+    const float rate = e < R::kRest ? kDcRate : kRestRate;
+    float_adam(pv.x, mv.x, vv.x, gv.x, rate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.y, mv.y, vv.y, gv.y, rate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.z, mv.z, vv.z, gv.z, rate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.w, mv.w, vv.w, gv.w, rate, p.inv_bias1, p.inv_bias2);
   } else if constexpr (C::kSh == SH_ADAM) {
-    float_adam(pe, me, ve, g, (e % 48) < 3 ? kDcRate : kRestRate, p.inv_bias1,
-               p.inv_bias2);
+    // Packed rows: term 0 (elements 0..2 of a Gaussian's 48) is dc.
+    const int col = e % 48;
+    float_adam(pv.x, mv.x, vv.x, gv.x, col < 3 ? kDcRate : kRestRate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.y, mv.y, vv.y, gv.y, col + 1 < 3 ? kDcRate : kRestRate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.z, mv.z, vv.z, gv.z, col + 2 < 3 ? kDcRate : kRestRate, p.inv_bias1, p.inv_bias2);
+    float_adam(pv.w, mv.w, vv.w, gv.w, kRestRate, p.inv_bias1, p.inv_bias2);
   } else {
-    // SGD leaves invisible Gaussians untouched (SHGradientConsumer.cu:93).
-    if (st.template i<RADII>()[e / 48] > 0) sgd(pe, g);
+    // SGD leaves invisible Gaussians untouched (SHGradientConsumer.cu:93); the
+    // four elements belong to one Gaussian (48 is a multiple of 4).
+    if (st.template i<RADII>()[e / 48] > 0) {
+      sgd(pv.x, gv.x);
+      sgd(pv.y, gv.y);
+      sgd(pv.z, gv.z);
+      sgd(pv.w, gv.w);
+    }
   }
 }
 
+// Each consumer updates four consecutive elements with 128-bit shared-memory
+// accesses; every group's region is a multiple of four elements long, so the
+// four share one group (one step size).
 template <class C>
 __device__ __forceinline__ void phase_update(const StepParams& p,
                                              const Stage<C>& st,
                                              const Scratch& sc, int ct) {
   using R = Region<C>;
+  static_assert(R::kTotal % 4 == 0 && R::kRest % 4 == 0 && R::kRot % 4 == 0 &&
+                    R::kScl % 4 == 0 && R::kOpa % 4 == 0,
+                "group regions must be float4-aligned");
   constexpr bool kMoments = C::kSh != SH_SGD;
-  float* P = st.template f<R::kParamArr>();
-  float* M = kMoments ? st.template f<R::kFirstArr>() : nullptr;
-  float* V = kMoments ? st.template f<R::kSecondArr>() : nullptr;
-  constexpr int kRounds = (R::kTotal + kConsumers - 1) / kConsumers;
-  constexpr bool kExact = R::kTotal % kConsumers == 0;
-  float pv[kRounds], mv[kRounds], vv[kRounds], gv[kRounds];
-  // All loads, then the arithmetic, then all stores: the elements are
-  // independent, which the compiler cannot prove through shared pointers.
-#pragma unroll
-  for (int k = 0; k < kRounds; ++k) {
-    const int e = ct + k * kConsumers;
-    pv[k] = gv[k] = mv[k] = vv[k] = 0.f;
-    if (kExact || e < R::kTotal) {
-      pv[k] = P[e];
-      gv[k] = sc.grad[e];
-      if constexpr (kMoments) {
-        mv[k] = M[e];
-        vv[k] = V[e];
-      }
+  float4* P = reinterpret_cast<float4*>(st.template f<R::kParamArr>());
+  float4* M = kMoments ? reinterpret_cast<float4*>(st.template f<R::kFirstArr>()) : nullptr;
+  float4* V = kMoments ? reinterpret_cast<float4*>(st.template f<R::kSecondArr>()) : nullptr;
+  const float4* G = reinterpret_cast<const float4*>(sc.grad);
+  for (int q = ct; q < R::kTotal / 4; q += kConsumers) {
+    const int e = 4 * q;
+    float4 pv = P[q], gv = G[q];
+    float4 mv = make_float4(0.f, 0.f, 0.f, 0.f), vv = mv;
+    if constexpr (kMoments) {
+      mv = M[q];
+      vv = V[q];
     }
-  }
-#pragma unroll
-  for (int k = 0; k < kRounds; ++k) {
-    const int e = ct + k * kConsumers;
-    if (kExact || e < R::kTotal)
-      update_element<C>(p, st, e, pv[k], mv[k], vv[k], gv[k]);
-  }
-#pragma unroll
-  for (int k = 0; k < kRounds; ++k) {
-    const int e = ct + k * kConsumers;
-    if (kExact || e < R::kTotal) {
-      P[e] = pv[k];
-      if constexpr (kMoments) {
-        M[e] = mv[k];
-        V[e] = vv[k];
-      }
+    update_group<C>(p, st, e, pv, mv, vv, gv);
+    P[q] = pv;
+    if constexpr (kMoments) {
+      M[q] = mv;
+      V[q] = vv;
     }
   }
 }
@@ -487,10 +516,32 @@ __device__ __forceinline__ void load_camera(const StepParams& p, float cam[3]) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// Persistent pipeline: warp 0 lane 0 produces, the other warps consume.
+// Staging facts of array `lane` (one lane per array, NUM_ARR <= 32).
 template <class C>
-__global__ void __launch_bounds__(kPersistThreads, kCtasPerSm)
+__device__ __forceinline__ void lane_array(int lane, bool& present, bool& written,
+                                           uint32_t& offset, uint32_t& bytes) {
+  present = written = false;
+  offset = bytes = 0;
+  for_each_arr([&](auto a_) {
+    constexpr int a = decltype(a_)::value;
+    if constexpr (C::has(a)) {
+      constexpr bool kWrites = kWritten[a];
+      constexpr uint32_t kOffset = C::offset(a), kBytes = C::tile_bytes(a);
+      if (lane == a) {
+        present = true;
+        written = kWrites;
+        offset = kOffset;
+        bytes = kBytes;
+      }
+    }
+  });
+}
+static_assert(NUM_ARR <= 32, "one producer lane per staged array");
+
+// ---------------------------------------------------------------------------
+// Persistent pipeline: warp 0 produces, the other warps consume.
+template <class C>
+__global__ void __launch_bounds__(kPersistThreads, C::ctas)
     stream_kernel(const StepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full_bar[C::stages];
@@ -511,24 +562,29 @@ __global__ void __launch_bounds__(kPersistThreads, kCtasPerSm)
   const long long stride = gridDim.x;
 
   if (warp == 0) {
-    if (lane != 0) return;
+    // Lane a issues the bulk load of staged array a (one warp instruction per
+    // tile instead of one per array); lane 0 owns the barriers.
+    bool present, written;
+    uint32_t off, bytes;
+    lane_array<C>(lane, present, written, off, bytes);
+    const char* base = present ? static_cast<const char*>(p.ptr[lane]) : nullptr;
     int k = 0;
     for (long long t = first; t < p.tile_end; t += stride, ++k) {
       const int s = k % S;
-      if (k >= S && !mbar_wait_bounded(&empty_bar[s], ((k / S) - 1) & 1)) {
-        atomicOr(&g_fault_word, kFaultProducerWait);
+      int ok = 1;
+      if (k >= S) {
+        if (lane == 0) ok = mbar_wait_bounded(&empty_bar[s], ((k / S) - 1) & 1) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+      if (!ok) {
+        if (lane == 0) atomicOr(&g_fault_word, kFaultProducerWait);
         return;
       }
-      mbar_arrive_expect_tx(&full_bar[s], C::load_bytes());
-      unsigned char* st = smem + size_t(s) * C::stage_bytes;
-      for_each_arr([&](auto a_) {
-        constexpr int a = decltype(a_)::value;
-        if constexpr (C::has(a)) {
-          const char* src = static_cast<const char*>(p.ptr[a]) +
-                            t * (long long)C::tile_bytes(a);
-          bulk_load(st + C::offset(a), src, C::tile_bytes(a), &full_bar[s]);
-        }
-      });
+      if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], C::load_bytes());
+      __syncwarp();
+      if (present)
+        bulk_load(smem + size_t(s) * C::stage_bytes + off, base + t * (long long)bytes,
+                  bytes, &full_bar[s]);
     }
     return;
   }
@@ -536,32 +592,45 @@ __global__ void __launch_bounds__(kPersistThreads, kCtasPerSm)
   const int ct = threadIdx.x - 32;
   float cam[3];
   load_camera<C>(p, cam);
+  bool store_present = false, store_written = false;
+  uint32_t store_off = 0, store_bytes = 0;
+  char* out_base = nullptr;
+  if (ct < 32) {
+    lane_array<C>(ct, store_present, store_written, store_off, store_bytes);
+    if (store_present && store_written)
+      out_base = static_cast<char*>(const_cast<void*>(p.ptr[ct]));
+  }
   int k = 0;
   for (long long t = first; t < p.tile_end; t += stride, ++k) {
     const int s = k % S;
-    const bool ready = mbar_wait_bounded(&full_bar[s], (k / S) & 1);
-    if (!ready && ct == 0) atomicOr(&g_fault_word, kFaultConsumerWait);
+    // Warps 0-3 read the stage in phase A0 and wait for it; the others first
+    // touch it after the barrier that follows A0, which orders them after the
+    // waiters' acquire.
+    bool ready = true;
+    if (ct < 128) {
+      ready = mbar_wait_bounded(&full_bar[s], (k / S) & 1);
+      if (!ready) atomicOr(&g_fault_word, kFaultConsumerWait);
+    }
     Stage<C> st{smem + size_t(s) * C::stage_bytes};
     if (!process_tile<C>(p, st, scratch, kTile, ct, cam, ready)) break;
     fence_async_shared();
     named_barrier(1, kConsumers);
-    if (ct == 0) {
-      for_each_arr([&](auto a_) {
-        constexpr int a = decltype(a_)::value;
-        if constexpr (C::has(a) && kWritten[a]) {
-          char* dst = static_cast<char*>(const_cast<void*>(p.ptr[a])) +
-                      t * (long long)C::tile_bytes(a);
-          bulk_store(dst, st.base + C::offset(a), C::tile_bytes(a));
-        }
-      });
-      bulk_commit();
+    if (ct < 32) {
+      // Lane a stores written array a and tracks its own bulk groups; the
+      // previous tile's stage is released once every lane's older stores have
+      // finished reading shared memory.
+      if (store_present && store_written) {
+        bulk_store(out_base + t * (long long)store_bytes, st.base + store_off, store_bytes);
+        bulk_commit();
+      }
       if (k > 0) {
         bulk_wait_read<1>();
-        mbar_arrive(&empty_bar[(k - 1) % S]);
+        __syncwarp();
+        if (ct == 0) mbar_arrive(&empty_bar[(k - 1) % S]);
       }
     }
   }
-  if (ct == 0) bulk_wait_read<0>();
+  if (ct < 32) bulk_wait_read<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -707,7 +776,7 @@ cudaError_t run(StepParams p, cudaStream_t stream) {
   long long generic_begin = 0;
   if (aligned && full > 0) {
     const long long grid =
-        std::min<long long>(full, (long long)device_info().sm_count * kCtasPerSm);
+        std::min<long long>(full, (long long)device_info().sm_count * C::ctas);
     p.tile_begin = 0;
     p.tile_end = full;
     stream_kernel<C><<<unsigned(grid), kPersistThreads, persist_smem<C>(),

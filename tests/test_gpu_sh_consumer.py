@@ -234,3 +234,25 @@ def test_full_size_bit_exact(cuda):
     assert_identical(run_kernel(p, 3, 7, cuda), run_oracle(p, 3, 7), "1.1M")
     import _native as native
     assert native.fault_status() == 0
+
+
+def test_adam_ratio_threshold_bit_exact(cuda):
+    """sqrt(v)/bias2 swept densely across 2^-25, where the kernel skips the
+    double-precision epsilon add that cannot change the float result; zero
+    gradients (invisible Gaussians) keep v under control."""
+    n = 8192
+    p = cases.sh_problem(n, seed=99, invisible=1.0, moments=True)
+    b1, b2 = cases.bias(3)
+    rng = np.random.default_rng(5)
+    # v_new = 0.999 v; pick v so sqrt(v_new)/b2 covers [2^-27, 2^-23].
+    exponent = rng.uniform(-27.0, -23.0, (n, 45))
+    ratio = np.exp2(exponent)
+    v = ((ratio * b2) ** 2 / 0.999).astype(np.float32)
+    # also hit exact float neighbours of the threshold
+    edge = np.float32(2.0 ** -25)
+    around = np.array([np.nextafter(edge, np.float32(0)), edge, np.nextafter(edge, np.float32(1))],
+                      np.float32)
+    v[:3, :3] = ((around.astype(np.float64)[None, :] * b2) ** 2 / 0.999).astype(np.float32)
+    p["rest_second"] = v
+    p["dc_second"] = v[:, :3].copy()
+    assert_identical(run_kernel(p, 3, 3, cuda), run_oracle(p, 3, 3), "ratio sweep")
