@@ -1,0 +1,998 @@
+// Tile-based Gaussian rasterizer for B200: projection, binning, forward
+// compositing, and the backward pass whose pixel stage accumulates per-Gaussian
+// adjoints with warp reductions before the global atomics.
+//
+// Pipeline (forward): preprocess (one thread per Gaussian: camera transform,
+// 3D covariance from scale and rotation, EWA screen covariance, conic, radius,
+// tiles touched, SH colour and its clamp flags) -> inclusive scan of tiles
+// touched -> one (tile << 32 | depth) key per touched tile -> radix sort ->
+// per-tile ranges -> compositing (one 16x16 CTA per tile, Gaussians staged in
+// shared memory in batches of 256).
+//
+// Pixel backward: the same traversal back to front. Every pixel contributes
+// ten adjoints per Gaussian (RGB, screen mean x/y, conic a/b/c, opacity,
+// inverse depth). Accumulation modes:
+//   0  one atomic per contributing lane and adjoint (the unpatched renderer);
+//   1  the reference's WarpAccumulation.cuh: a shuffle reduction and one
+//      atomic per adjoint when all 32 lanes contribute to the same Gaussian,
+//      per-lane atomics otherwise (WarpAccumulation.cuh:9-29);
+//   2  (default) all lanes stay converged on each Gaussian, lanes that do not
+//      contribute add zeros, and a transposing butterfly (16 shuffles instead
+//      of 10 x 5) leaves each of the ten sums in one lane pair, so a warp
+//      issues a single 10-lane atomic instruction per Gaussian it touches,
+//      partial warps included.
+// All three give the same gradients up to floating-point summation order.
+//
+// Geometry backward (one thread per Gaussian): conic -> screen covariance ->
+// 3D covariance (and the mean through the projection Jacobian), covariance ->
+// scale and rotation, screen mean and inverse depth -> 3D mean, and SH colour
+// -> coefficients and view direction, unless the SH adjoint is consumed by the
+// fused SH + Adam kernel instead (see gaussian_step.cu).
+#include <cub/cub.cuh>
+
+#include <cstdint>
+#include <string>
+
+#include "clad3dgs_b200.h"
+#include "gaussian_math.cuh"
+#include "raster_math.cuh"
+
+namespace clad3dgs {
+int fail(int code, const std::string& message);  // gaussian_step.cu
+}
+
+namespace clad3dgs {
+namespace raster {
+
+constexpr int kBatch = kTilePixels;
+
+template <class T>
+__host__ __device__ inline size_t aligned(size_t v) {
+  return (v + 127) & ~size_t(127);
+}
+
+// ---------------------------------------------------------------------------
+// Buffer layouts carved out of caller-provided memory.
+
+struct GeomState {
+  float* depth;          // camera z
+  bool* clamped;         // [P][3]
+  int* radii;            // internal copy
+  float2* mean2d;        // pixel coordinates
+  float* cov3d;          // [P][6]
+  float4* conic_opacity; // conic (a, b, c), opacity x antialias factor
+  float* rgb;            // [P][3]
+  uint32_t* tiles;       // tiles touched
+  uint32_t* offsets;     // inclusive scan of tiles
+  void* scan_tmp;
+  size_t scan_bytes;
+};
+
+size_t scan_temp_bytes(int P) {
+  size_t bytes = 0;
+  cub::DeviceScan::InclusiveSum(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr, P);
+  return bytes;
+}
+
+size_t geom_bytes(int P) {
+  size_t s = 0;
+  s += aligned<float>(sizeof(float) * P);
+  s += aligned<bool>(3 * P);
+  s += aligned<int>(sizeof(int) * P);
+  s += aligned<float2>(sizeof(float2) * P);
+  s += aligned<float>(sizeof(float) * 6 * P);
+  s += aligned<float4>(sizeof(float4) * P);
+  s += aligned<float>(sizeof(float) * 3 * P);
+  s += aligned<uint32_t>(sizeof(uint32_t) * P);
+  s += aligned<uint32_t>(sizeof(uint32_t) * P);
+  s += aligned<char>(scan_temp_bytes(P));
+  return s + 128;
+}
+
+GeomState geom_from(char* base, int P) {
+  GeomState g;
+  char* c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 127) & ~uintptr_t(127));
+  auto take = [&](size_t bytes) {
+    char* r = c;
+    c += aligned<char>(bytes);
+    return r;
+  };
+  g.depth = reinterpret_cast<float*>(take(sizeof(float) * P));
+  g.clamped = reinterpret_cast<bool*>(take(3 * P));
+  g.radii = reinterpret_cast<int*>(take(sizeof(int) * P));
+  g.mean2d = reinterpret_cast<float2*>(take(sizeof(float2) * P));
+  g.cov3d = reinterpret_cast<float*>(take(sizeof(float) * 6 * P));
+  g.conic_opacity = reinterpret_cast<float4*>(take(sizeof(float4) * P));
+  g.rgb = reinterpret_cast<float*>(take(sizeof(float) * 3 * P));
+  g.tiles = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.offsets = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.scan_bytes = scan_temp_bytes(P);
+  g.scan_tmp = take(g.scan_bytes);
+  return g;
+}
+
+struct ImageState {
+  uint2* ranges;        // per tile
+  uint32_t* n_contrib;  // per pixel
+  float* final_t;       // per pixel
+};
+
+size_t image_bytes(int pixels, int tiles) {
+  return aligned<uint2>(sizeof(uint2) * tiles) + aligned<uint32_t>(4 * size_t(pixels)) +
+         aligned<float>(4 * size_t(pixels)) + 128;
+}
+
+ImageState image_from(char* base, int pixels, int tiles) {
+  ImageState s;
+  char* c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 127) & ~uintptr_t(127));
+  s.ranges = reinterpret_cast<uint2*>(c);
+  c += aligned<uint2>(sizeof(uint2) * tiles);
+  s.n_contrib = reinterpret_cast<uint32_t*>(c);
+  c += aligned<uint32_t>(4 * size_t(pixels));
+  s.final_t = reinterpret_cast<float*>(c);
+  return s;
+}
+
+struct BinningState {
+  uint64_t* keys_unsorted;
+  uint32_t* values_unsorted;
+  uint64_t* keys;
+  uint32_t* values;
+  void* sort_tmp;
+  size_t sort_bytes;
+};
+
+size_t sort_temp_bytes(int n, int end_bit) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint64_t*)nullptr, (uint64_t*)nullptr,
+                                  (uint32_t*)nullptr, (uint32_t*)nullptr, n, 0, end_bit);
+  return bytes;
+}
+
+size_t binning_bytes(int n) {
+  return 2 * aligned<uint64_t>(8 * size_t(n)) + 2 * aligned<uint32_t>(4 * size_t(n)) +
+         aligned<char>(sort_temp_bytes(n, 64)) + 128;
+}
+
+BinningState binning_from(char* base, int n) {
+  BinningState b;
+  char* c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 127) & ~uintptr_t(127));
+  b.keys_unsorted = reinterpret_cast<uint64_t*>(c);
+  c += aligned<uint64_t>(8 * size_t(n));
+  b.keys = reinterpret_cast<uint64_t*>(c);
+  c += aligned<uint64_t>(8 * size_t(n));
+  b.values_unsorted = reinterpret_cast<uint32_t*>(c);
+  c += aligned<uint32_t>(4 * size_t(n));
+  b.values = reinterpret_cast<uint32_t*>(c);
+  c += aligned<uint32_t>(4 * size_t(n));
+  b.sort_tmp = c;
+  b.sort_bytes = sort_temp_bytes(n, 64);
+  return b;
+}
+
+// ---------------------------------------------------------------------------
+// SH colour access for packed [P][16][3] or split dc [P][3] + rest [P][45].
+
+struct ShSource {
+  const float* packed;
+  const float* dc;
+  const float* rest;
+  __device__ __forceinline__ const float* term(int i, int j) const {
+    if (packed) return packed + 48 * size_t(i) + 3 * j;
+    return j == 0 ? dc + 3 * size_t(i) : rest + 45 * size_t(i) + 3 * (j - 1);
+  }
+};
+
+template <int J>
+__device__ __forceinline__ void colour_terms(const Direction& d, const ShSource& sh, int i,
+                                             int nterms, float rgb[3]) {
+  if constexpr (J < 16) {
+    if (J < nterms) {
+      float b, gx, gy, gz;
+      sh_basis<J>(d, b, gx, gy, gz);
+      const float* c = sh.term(i, J);
+      rgb[0] += b * c[0];
+      rgb[1] += b * c[1];
+      rgb[2] += b * c[2];
+      colour_terms<J + 1>(d, sh, i, nterms, rgb);
+    }
+  }
+}
+
+// SH backward for one Gaussian: d colour / d coefficients (optional) and the
+// adjoint of the view direction.
+template <int J>
+__device__ __forceinline__ void colour_adjoint_terms(const Direction& d, const ShSource& sh,
+                                                     int i, int nterms, const float g[3],
+                                                     float* dsh, float dd[3]) {
+  if constexpr (J < 16) {
+    float b, gx, gy, gz;
+    sh_basis<J>(d, b, gx, gy, gz);
+    if (J < nterms) {
+      const float* c = sh.term(i, J);
+      const float dot = c[0] * g[0] + c[1] * g[1] + c[2] * g[2];
+      dd[0] += gx * dot;
+      dd[1] += gy * dot;
+      dd[2] += gz * dot;
+      if (dsh) {
+        dsh[3 * J] = b * g[0];
+        dsh[3 * J + 1] = b * g[1];
+        dsh[3 * J + 2] = b * g[2];
+      }
+    } else if (dsh) {
+      dsh[3 * J] = dsh[3 * J + 1] = dsh[3 * J + 2] = 0.f;
+    }
+    colour_adjoint_terms<J + 1>(d, sh, i, nterms, g, dsh, dd);
+  }
+}
+
+struct Camera {
+  const float* view;  // column-major 4x4
+  const float* proj;  // column-major 4x4 (full projection)
+  const float* campos;
+  float tan_x, tan_y, fx, fy;
+  int width, height, grid_x, grid_y;
+};
+
+// ---------------------------------------------------------------------------
+// Forward kernels.
+
+__global__ void preprocess_kernel(int P, int degree, const float* __restrict__ means,
+                                  const float* __restrict__ scales, float scale_modifier,
+                                  const float* __restrict__ rotations,
+                                  const float* __restrict__ opacities,
+                                  const float* __restrict__ colors_precomp,
+                                  const float* __restrict__ cov3d_precomp, ShSource sh,
+                                  Camera cam, bool antialiasing, GeomState g,
+                                  int* __restrict__ radii_out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  g.radii[i] = 0;
+  g.tiles[i] = 0;
+  radii_out[i] = 0;
+  const Vec3 p{means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+  const Vec3 t = affine3(cam.view, p);
+  if (t.z <= kNearPlane) return;
+  float cov[6];
+  if (cov3d_precomp) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) cov[k] = cov3d_precomp[6 * i + k];
+  } else {
+    const float s[3] = {scale_modifier * scales[3 * i], scale_modifier * scales[3 * i + 1],
+                        scale_modifier * scales[3 * i + 2]};
+    const float q[4] = {rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
+                        rotations[4 * i + 3]};
+    covariance3d(s, q, cov);
+  }
+#pragma unroll
+  for (int k = 0; k < 6; ++k) g.cov3d[6 * i + k] = cov[k];
+  const Projection2 J = screen_jacobian(t, cam.fx, cam.fy, cam.tan_x, cam.tan_y, cam.view);
+  float a, b, c;
+  covariance2d(J, cov, a, b, c);
+  const float det0 = a * c - b * b;
+  a += kLowPass;
+  c += kLowPass;
+  const float det = a * c - b * b;
+  float aa = 1.f;
+  if (antialiasing) aa = sqrtf(fmaxf(0.000025f, det0 / det));
+  if (det == 0.f) return;
+  const float inv = 1.f / det;
+  const float mid = 0.5f * (a + c);
+  const float disc = sqrtf(fmaxf(0.1f, mid * mid - det));
+  const float lambda = fmaxf(mid + disc, mid - disc);
+  const int radius = (int)ceilf(3.f * sqrtf(lambda));
+  const float hw = affine_w(cam.proj, p);
+  const Vec3 h = affine3(cam.proj, p);
+  const float iw = 1.f / (hw + 0.0000001f);
+  const float px = ndc_to_pixel(h.x * iw, cam.width), py = ndc_to_pixel(h.y * iw, cam.height);
+  int x0, y0, x1, y1;
+  tile_rect(px, py, radius, cam.grid_x, cam.grid_y, x0, y0, x1, y1);
+  const int touched = (x1 - x0) * (y1 - y0);
+  if (touched == 0) return;
+  if (colors_precomp) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) g.rgb[3 * i + k] = colors_precomp[3 * i + k];
+  } else {
+    const Direction d = make_direction(p.x, p.y, p.z, cam.campos[0], cam.campos[1],
+                                       cam.campos[2]);
+    float rgb[3] = {0.f, 0.f, 0.f};
+    colour_terms<0>(d, sh, i, (degree + 1) * (degree + 1), rgb);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float v = rgb[k] + 0.5f;
+      g.clamped[3 * i + k] = v < 0.f;
+      g.rgb[3 * i + k] = fmaxf(v, 0.f);
+    }
+  }
+  g.depth[i] = t.z;
+  g.radii[i] = radius;
+  radii_out[i] = radius;
+  g.mean2d[i] = make_float2(px, py);
+  g.conic_opacity[i] = make_float4(c * inv, -b * inv, a * inv, opacities[i] * aa);
+  g.tiles[i] = touched;
+}
+
+__global__ void duplicate_kernel(int P, GeomState g, Camera cam, uint64_t* keys,
+                                 uint32_t* values) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P || g.radii[i] <= 0) return;
+  uint32_t out = i == 0 ? 0 : g.offsets[i - 1];
+  int x0, y0, x1, y1;
+  const float2 m = g.mean2d[i];
+  tile_rect(m.x, m.y, g.radii[i], cam.grid_x, cam.grid_y, x0, y0, x1, y1);
+  const uint32_t depth_bits = __float_as_uint(g.depth[i]);
+  for (int y = y0; y < y1; ++y)
+    for (int x = x0; x < x1; ++x) {
+      keys[out] = (uint64_t(uint32_t(y * cam.grid_x + x)) << 32) | depth_bits;
+      values[out] = i;
+      ++out;
+    }
+}
+
+__global__ void ranges_kernel(int n, const uint64_t* keys, uint2* ranges) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t tile = uint32_t(keys[i] >> 32);
+  if (i == 0) ranges[tile].x = 0;
+  else {
+    const uint32_t prev = uint32_t(keys[i - 1] >> 32);
+    if (tile != prev) {
+      ranges[prev].y = i;
+      ranges[tile].x = i;
+    }
+  }
+  if (i == n - 1) ranges[tile].y = n;
+}
+
+__global__ void __launch_bounds__(kTilePixels)
+    render_forward_kernel(const uint2* __restrict__ ranges,
+                          const uint32_t* __restrict__ point_list, int width, int height,
+                          int grid_x, const float2* __restrict__ mean2d,
+                          const float* __restrict__ rgb,
+                          const float4* __restrict__ conic_opacity,
+                          const float* __restrict__ depth, const float* __restrict__ bg,
+                          float* __restrict__ final_t, uint32_t* __restrict__ n_contrib,
+                          float* __restrict__ out_color, float* __restrict__ out_invdepth) {
+  const int tile = blockIdx.y * grid_x + blockIdx.x;
+  const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
+  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;
+  const bool inside = px < width && py < height;
+  const int pix = py * width + px;
+  const float fx = (float)px, fy = (float)py;
+  const uint2 range = ranges[tile];
+  __shared__ float2 s_xy[kBatch];
+  __shared__ float4 s_co[kBatch];
+  __shared__ float s_rgb[3 * kBatch];
+  __shared__ float s_inv[kBatch];
+  bool done = !inside;
+  float T = 1.f, C[3] = {0.f, 0.f, 0.f}, D = 0.f;
+  uint32_t contributor = 0, last = 0;
+  const int todo = int(range.y - range.x);
+  for (int base = 0; base < todo; base += kBatch) {
+    if (__syncthreads_count(done) == kTilePixels) break;
+    const int k = base + threadIdx.x;
+    if (k < todo) {
+      const uint32_t id = point_list[range.x + k];
+      s_xy[threadIdx.x] = mean2d[id];
+      s_co[threadIdx.x] = conic_opacity[id];
+      s_rgb[3 * threadIdx.x] = rgb[3 * id];
+      s_rgb[3 * threadIdx.x + 1] = rgb[3 * id + 1];
+      s_rgb[3 * threadIdx.x + 2] = rgb[3 * id + 2];
+      s_inv[threadIdx.x] = 1.f / depth[id];
+    }
+    __syncthreads();
+    const int count = min(kBatch, todo - base);
+    for (int j = 0; !done && j < count; ++j) {
+      ++contributor;
+      const float dx = s_xy[j].x - fx, dy = s_xy[j].y - fy;
+      const float4 co = s_co[j];
+      const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
+      if (power > 0.f) continue;
+      const float alpha = fminf(kMaxAlpha, co.w * __expf(power));
+      if (alpha < kMinAlpha) continue;
+      const float test_t = T * (1.f - alpha);
+      if (test_t < kMinTransmittance) {
+        done = true;
+        continue;
+      }
+      const float w = alpha * T;
+      C[0] += s_rgb[3 * j] * w;
+      C[1] += s_rgb[3 * j + 1] * w;
+      C[2] += s_rgb[3 * j + 2] * w;
+      D += s_inv[j] * w;
+      T = test_t;
+      last = contributor;
+    }
+  }
+  if (inside) {
+    final_t[pix] = T;
+    n_contrib[pix] = last;
+    const int hw = width * height;
+    out_color[pix] = C[0] + T * bg[0];
+    out_color[hw + pix] = C[1] + T * bg[1];
+    out_color[2 * hw + pix] = C[2] + T * bg[2];
+    if (out_invdepth) out_invdepth[pix] = D;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pixel backward.
+
+struct PixelGrads {
+  float* dmean2d;    // [P][3]
+  float* dconic;     // [P][4] (a, b, -, c)
+  float* dopacity;   // [P]
+  float* dcolor;     // [P][3]
+  float* dinvdepth;  // [P] or null
+};
+
+// Address of adjoint field f (0-2 RGB, 3-4 mean x/y, 5-7 conic a/b/c,
+// 8 opacity, 9 inverse depth) of Gaussian id.
+__device__ __forceinline__ float* field_address(const PixelGrads& o, uint32_t id, int f) {
+  switch (f) {
+    case 0: case 1: case 2: return o.dcolor + 3 * size_t(id) + f;
+    case 3: case 4: return o.dmean2d + 3 * size_t(id) + (f - 3);
+    case 5: return o.dconic + 4 * size_t(id);
+    case 6: return o.dconic + 4 * size_t(id) + 1;
+    case 7: return o.dconic + 4 * size_t(id) + 3;
+    case 8: return o.dopacity + id;
+    default: return o.dinvdepth + id;
+  }
+}
+
+// Sums v[0..9] over the warp; afterwards lane L holds the total of field
+// (L >> 1) & 15 (lanes L and L ^ 1 hold the same value). Each butterfly step
+// halves the number of fields a lane keeps, so 16 shuffles cover 10 fields.
+__device__ __forceinline__ float transpose_reduce(float v[16], int lane) {
+#pragma unroll
+  for (int step = 0; step < 4; ++step) {
+    const int half = 8 >> step;          // fields kept after this step
+    const int mask = 16 >> step;         // lane bit that picks the half
+    const bool upper = lane & mask;
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      const float send = upper ? v[k] : v[k + half];
+      const float keep = upper ? v[k + half] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+template <int Mode>
+__global__ void __launch_bounds__(kTilePixels)
+    render_backward_kernel(const uint2* __restrict__ ranges,
+                           const uint32_t* __restrict__ point_list, int width, int height,
+                           int grid_x, const float* __restrict__ bg,
+                           const float2* __restrict__ mean2d,
+                           const float4* __restrict__ conic_opacity,
+                           const float* __restrict__ rgb, const float* __restrict__ depth,
+                           const float* __restrict__ final_t,
+                           const uint32_t* __restrict__ n_contrib,
+                           const float* __restrict__ dpixels,
+                           const float* __restrict__ dinvdepth_pixels, PixelGrads out) {
+  const int tile = blockIdx.y * grid_x + blockIdx.x;
+  const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
+  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;
+  const bool inside = px < width && py < height;
+  const int pix = py * width + px;
+  const int lane = threadIdx.x & 31;
+  const float fx = (float)px, fy = (float)py;
+  const uint2 range = ranges[tile];
+  const int todo = int(range.y - range.x);
+  __shared__ uint32_t s_id[kBatch];
+  __shared__ float2 s_xy[kBatch];
+  __shared__ float4 s_co[kBatch];
+  __shared__ float s_rgb[3 * kBatch];
+  __shared__ float s_inv[kBatch];
+  const int hw = width * height;
+  const float T_final = inside ? final_t[pix] : 0.f;
+  float T = T_final;
+  uint32_t contributor = todo;
+  const uint32_t last = inside ? n_contrib[pix] : 0;
+  float dpix[3] = {0.f, 0.f, 0.f}, dinv = 0.f;
+  if (inside) {
+    dpix[0] = dpixels[pix];
+    dpix[1] = dpixels[hw + pix];
+    dpix[2] = dpixels[2 * hw + pix];
+    if (dinvdepth_pixels) dinv = dinvdepth_pixels[pix];
+  }
+  const float bg_dot = bg[0] * dpix[0] + bg[1] * dpix[1] + bg[2] * dpix[2];
+  float acc[3] = {0.f, 0.f, 0.f}, acc_inv = 0.f;
+  float last_alpha = 0.f, last_rgb[3] = {0.f, 0.f, 0.f}, last_inv = 0.f;
+  const float ddx = 0.5f * width, ddy = 0.5f * height;
+  for (int base = 0; base < todo; base += kBatch) {
+    __syncthreads();
+    const int k = base + threadIdx.x;
+    if (k < todo) {
+      const uint32_t id = point_list[range.y - k - 1];
+      s_id[threadIdx.x] = id;
+      s_xy[threadIdx.x] = mean2d[id];
+      s_co[threadIdx.x] = conic_opacity[id];
+      s_rgb[3 * threadIdx.x] = rgb[3 * id];
+      s_rgb[3 * threadIdx.x + 1] = rgb[3 * id + 1];
+      s_rgb[3 * threadIdx.x + 2] = rgb[3 * id + 2];
+      s_inv[threadIdx.x] = 1.f / depth[id];
+    }
+    __syncthreads();
+    const int count = min(kBatch, todo - base);
+    for (int j = 0; j < count; ++j) {
+      --contributor;
+      bool contrib = inside && contributor < last;
+      const float4 co = s_co[j];
+      const float dx = s_xy[j].x - fx, dy = s_xy[j].y - fy;
+      const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
+      contrib = contrib && power <= 0.f;
+      const float G = __expf(power);
+      const float alpha = fminf(kMaxAlpha, co.w * G);
+      contrib = contrib && alpha >= kMinAlpha;
+      float f[16];
+      if constexpr (Mode == 2) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) f[q] = 0.f;
+      } else {
+        if (!contrib) continue;
+      }
+      if (contrib) {
+        T = T / (1.f - alpha);
+        const float w = alpha * T;
+        float dl_dalpha = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+          const float cc = s_rgb[3 * j + ch];
+          acc[ch] = last_alpha * last_rgb[ch] + (1.f - last_alpha) * acc[ch];
+          last_rgb[ch] = cc;
+          dl_dalpha += (cc - acc[ch]) * dpix[ch];
+          f[ch] = w * dpix[ch];
+        }
+        const float inv = s_inv[j];
+        acc_inv = last_alpha * last_inv + (1.f - last_alpha) * acc_inv;
+        last_inv = inv;
+        dl_dalpha += (inv - acc_inv) * dinv;
+        f[9] = w * dinv;
+        dl_dalpha *= T;
+        last_alpha = alpha;
+        dl_dalpha += (-T_final / (1.f - alpha)) * bg_dot;
+        const float dl_dg = co.w * dl_dalpha;
+        const float gdx = G * dx, gdy = G * dy;
+        const float dg_ddx = -gdx * co.x - gdy * co.y;
+        const float dg_ddy = -gdy * co.z - gdx * co.y;
+        f[3] = dl_dg * dg_ddx * ddx;
+        f[4] = dl_dg * dg_ddy * ddy;
+        f[5] = -0.5f * gdx * dx * dl_dg;
+        f[6] = -0.5f * gdx * dy * dl_dg;
+        f[7] = -0.5f * gdy * dy * dl_dg;
+        f[8] = G * dl_dalpha;
+      }
+      const uint32_t id = s_id[j];
+      const int nf = out.dinvdepth ? 10 : 9;
+      if constexpr (Mode == 0) {
+        atomicAdd(out.dcolor + 3 * size_t(id), f[0]);
+        atomicAdd(out.dcolor + 3 * size_t(id) + 1, f[1]);
+        atomicAdd(out.dcolor + 3 * size_t(id) + 2, f[2]);
+        atomicAdd(out.dmean2d + 3 * size_t(id), f[3]);
+        atomicAdd(out.dmean2d + 3 * size_t(id) + 1, f[4]);
+        atomicAdd(out.dconic + 4 * size_t(id), f[5]);
+        atomicAdd(out.dconic + 4 * size_t(id) + 1, f[6]);
+        atomicAdd(out.dconic + 4 * size_t(id) + 3, f[7]);
+        atomicAdd(out.dopacity + id, f[8]);
+        if (out.dinvdepth) atomicAdd(out.dinvdepth + id, f[9]);
+      } else if constexpr (Mode == 1) {
+        // The reference's helper: whole warp on one Gaussian -> reduce, else
+        // per-lane atomics.
+        const bool full = __match_any_sync(__activemask(), id) == 0xffffffffu;
+        for (int q = 0; q < nf; ++q) {
+          float v = f[q];
+          if (full) {
+#pragma unroll
+            for (int off = 16; off; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+            if (lane == 0) atomicAdd(field_address(out, id, q), v);
+          } else {
+            atomicAdd(field_address(out, id, q), v);
+          }
+        }
+      } else {
+        if (!__any_sync(0xffffffffu, contrib)) continue;
+        const float total = transpose_reduce(f, lane);
+        const int q = (lane >> 1) & 15;
+        if ((lane & 1) == 0 && q < nf) atomicAdd(field_address(out, id, q), total);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Geometry backward: one thread per Gaussian.
+
+struct GeomGrads {
+  const float* dmean2d;    // [P][3]
+  const float* dconic;     // [P][4]
+  float* dopacity;         // [P] in: w.r.t. scaled opacity; out: w.r.t. opacity
+  const float* dcolor;     // [P][3]
+  const float* dinvdepth;  // [P] or null
+  float* dmeans;           // [P][3] out
+  float* dcov3d;           // [P][6] out
+  float* dsh;              // [P][16][3] out or null (SH adjoint consumed elsewhere)
+  float* dscales;          // [P][3] out
+  float* drotations;       // [P][4] out
+};
+
+__global__ void preprocess_backward_kernel(
+    int P, int degree, const float* __restrict__ means, const float* __restrict__ scales,
+    float scale_modifier, const float* __restrict__ rotations,
+    const float* __restrict__ opacities, const float* __restrict__ cov3d_precomp,
+    ShSource sh, Camera cam, bool antialiasing, const int* __restrict__ radii,
+    GeomState g, bool colours_from_sh, GeomGrads o) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  if (radii[i] <= 0) {
+    return;
+  }
+  const Vec3 p{means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+  const Vec3 t = affine3(cam.view, p);
+  const float* cov = g.cov3d + 6 * i;
+  const Projection2 J = screen_jacobian(t, cam.fx, cam.fy, cam.tan_x, cam.tan_y, cam.view);
+  float a0, b, c0;
+  covariance2d(J, cov, a0, b, c0);
+  const float a = a0 + kLowPass, c = c0 + kLowPass;
+  const float det0 = a0 * c0 - b * b;
+  const float det = a * c - b * b;
+  // Opacity: the renderer used opacity * s with s = sqrt(max(2.5e-5, det0/det)).
+  float dl_da = 0.f, dl_db = 0.f, dl_dc = 0.f;
+  const float dop_scaled = o.dopacity[i];
+  if (antialiasing) {
+    const float r = det0 / det;
+    const float s = sqrtf(fmaxf(0.000025f, r));
+    o.dopacity[i] = dop_scaled * s;
+    if (r > 0.000025f) {
+      const float dl_ds = dop_scaled * opacities[i];
+      const float dl_dr = dl_ds * 0.5f / s;
+      const float id2 = 1.f / (det * det);
+      // r = det0 / det; d det0 = (c0, -2b, a0), d det = (c, -2b, a) wrt (a0, b, c0)
+      dl_da += dl_dr * (c0 * det - det0 * c) * id2;
+      dl_db += dl_dr * (-2.f * b * det + 2.f * b * det0) * id2;
+      dl_dc += dl_dr * (a0 * det - det0 * a) * id2;
+    }
+  }
+  // Conic = inverse of [[a, b], [b, c]]; dconic.y holds half the adjoint of the
+  // off-diagonal value (each symmetric entry receives it).
+  const float* dq = o.dconic + 4 * i;
+  const float gx = dq[0], gy2 = dq[1], gz = dq[3];
+  const float id2 = 1.f / (det * det + 0.0000001f);
+  if (id2 != 0.f) {
+    dl_da += id2 * (-c * c * gx + 2.f * b * c * gy2 + (det - a * c) * gz);
+    dl_dc += id2 * (-a * a * gz + 2.f * a * b * gy2 + (det - a * c) * gx);
+    dl_db += id2 * 2.f * (b * c * gx - (det + 2.f * b * b) * gy2 + a * b * gz);
+  }
+  // Screen covariance A Sigma A^T -> Sigma (six unique entries).
+  const float* A0 = J.A;
+  const float* A1 = J.A + 3;
+  float dcov[6];
+  {
+    int k = 0;
+    for (int r = 0; r < 3; ++r)
+      for (int s = r; s < 3; ++s, ++k) {
+        const float mul = r == s ? 1.f : 2.f;
+        const float sym_b = r == s ? A0[r] * A1[r] : A0[r] * A1[s] + A0[s] * A1[r];
+        dcov[k] = mul * (A0[r] * A0[s] * dl_da + A1[r] * A1[s] * dl_dc) + sym_b * dl_db;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < 6; ++k) o.dcov3d[6 * i + k] = dcov[k];
+  // Through the projection Jacobian to the camera-space mean.
+  const float S[9] = {cov[0], cov[1], cov[2], cov[1], cov[3], cov[4], cov[2], cov[4], cov[5]};
+  float sa0[3], sa1[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    sa0[k] = S[3 * k] * A0[0] + S[3 * k + 1] * A0[1] + S[3 * k + 2] * A0[2];
+    sa1[k] = S[3 * k] * A1[0] + S[3 * k + 1] * A1[1] + S[3 * k + 2] * A1[2];
+  }
+  float dA0[3], dA1[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    dA0[k] = 2.f * dl_da * sa0[k] + dl_db * sa1[k];
+    dA1[k] = dl_db * sa0[k] + 2.f * dl_dc * sa1[k];
+  }
+  // A = J W: dJ = dA W^T; J00 = fx/z, J02 = -fx tx/z^2, J11 = fy/z, J12 = -fy ty/z^2.
+  float dJ00 = 0.f, dJ02 = 0.f, dJ11 = 0.f, dJ12 = 0.f;
+#pragma unroll
+  for (int col = 0; col < 3; ++col) {
+    dJ00 += dA0[col] * cam.view[4 * col + 0];
+    dJ02 += dA0[col] * cam.view[4 * col + 2];
+    dJ11 += dA1[col] * cam.view[4 * col + 1];
+    dJ12 += dA1[col] * cam.view[4 * col + 2];
+  }
+  const float iz = 1.f / J.tz, iz2 = iz * iz, iz3 = iz2 * iz;
+  const float dtx = (J.clamp_x ? 0.f : 1.f) * -cam.fx * iz2 * dJ02;
+  const float dty = (J.clamp_y ? 0.f : 1.f) * -cam.fy * iz2 * dJ12;
+  float dtz = -cam.fx * iz2 * dJ00 - cam.fy * iz2 * dJ11 + 2.f * cam.fx * J.tx * iz3 * dJ02 +
+              2.f * cam.fy * J.ty * iz3 * dJ12;
+  if (o.dinvdepth) dtz += -o.dinvdepth[i] * iz2;
+  // Camera-space -> world: t = W p + b, so dp = W^T dt.
+  float dm[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    dm[k] = cam.view[4 * k + 0] * dtx + cam.view[4 * k + 1] * dty + cam.view[4 * k + 2] * dtz;
+  // Screen mean (NDC adjoint) -> world mean through the projective divide.
+  {
+    const float hw = affine_w(cam.proj, p);
+    const Vec3 h = affine3(cam.proj, p);
+    const float iw = 1.f / (hw + 0.0000001f);
+    const float gxn = o.dmean2d[3 * i], gyn = o.dmean2d[3 * i + 1];
+    const float mx = h.x * iw * iw, my = h.y * iw * iw;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float pk3 = cam.proj[4 * k + 3];
+      dm[k] += (cam.proj[4 * k + 0] * iw - pk3 * mx) * gxn +
+               (cam.proj[4 * k + 1] * iw - pk3 * my) * gyn;
+    }
+  }
+  // SH colour -> coefficients and the view direction.
+  if (colours_from_sh) {
+    const Direction d = make_direction(p.x, p.y, p.z, cam.campos[0], cam.campos[1],
+                                       cam.campos[2]);
+    float gcol[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) gcol[k] = g.clamped[3 * i + k] ? 0.f : o.dcolor[3 * i + k];
+    float dd[3] = {0.f, 0.f, 0.f};
+    colour_adjoint_terms<0>(d, sh, i, (degree + 1) * (degree + 1), gcol,
+                            o.dsh ? o.dsh + 48 * size_t(i) : nullptr, dd);
+    float om[3];
+    direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
+    dm[0] += om[0];
+    dm[1] += om[1];
+    dm[2] += om[2];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) o.dmeans[3 * i + k] += dm[k];
+  // Sigma = M M^T, M = R diag(s): dM = 2 G M with G the symmetric adjoint.
+  if (!cov3d_precomp) {
+    const float G[9] = {dcov[0], 0.5f * dcov[1], 0.5f * dcov[2], 0.5f * dcov[1], dcov[3],
+                        0.5f * dcov[4], 0.5f * dcov[2], 0.5f * dcov[4], dcov[5]};
+    const float s[3] = {scale_modifier * scales[3 * i], scale_modifier * scales[3 * i + 1],
+                        scale_modifier * scales[3 * i + 2]};
+    const float q[4] = {rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
+                        rotations[4 * i + 3]};
+    float R[9];
+    rotation(q, R);
+    float M[9], dM[9];
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int col = 0; col < 3; ++col) M[3 * r + col] = R[3 * r + col] * s[col];
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int col = 0; col < 3; ++col)
+        dM[3 * r + col] =
+            2.f * (G[3 * r] * M[col] + G[3 * r + 1] * M[3 + col] + G[3 * r + 2] * M[6 + col]);
+    // M_rc = R_rc s_c
+#pragma unroll
+    for (int col = 0; col < 3; ++col)
+      o.dscales[3 * i + col] =
+          scale_modifier * (dM[col] * R[col] + dM[3 + col] * R[3 + col] + dM[6 + col] * R[6 + col]);
+    float dR[9];
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int col = 0; col < 3; ++col) dR[3 * r + col] = dM[3 * r + col] * s[col];
+    const float w = q[0], x = q[1], y = q[2], z = q[3];
+    // dR/dq for R(w, x, y, z) of the rotation() above.
+    o.drotations[4 * i + 0] = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] -
+                                     y * dR[6] + x * dR[7]);
+    o.drotations[4 * i + 1] = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] -
+                                     w * dR[5] + z * dR[6] + w * dR[7] - 2.f * x * dR[8]);
+    o.drotations[4 * i + 2] = 2.f * (-2.f * y * dR[0] + x * dR[1] + w * dR[2] + x * dR[3] +
+                                     z * dR[5] - w * dR[6] + z * dR[7] - 2.f * y * dR[8]);
+    o.drotations[4 * i + 3] = 2.f * (-2.f * z * dR[0] - w * dR[1] + x * dR[2] + w * dR[3] -
+                                     2.f * z * dR[4] + y * dR[5] + x * dR[6] + y * dR[7]);
+  }
+}
+
+}  // namespace raster
+}  // namespace clad3dgs
+
+// ===========================================================================
+// C ABI.
+
+using namespace clad3dgs;
+using namespace clad3dgs::raster;
+
+namespace {
+
+int status_of(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return CLAD3DGS_OK;
+  cudaGetLastError();
+  return fail(CLAD3DGS_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int bits_for(uint32_t v) {
+  int b = 0;
+  while (b < 32 && (v >> b) != 0) ++b;
+  return b;
+}
+
+Camera make_camera(const float* view, const float* proj, const float* campos, int width,
+                   int height, float tan_x, float tan_y) {
+  Camera c;
+  c.view = view;
+  c.proj = proj;
+  c.campos = campos;
+  c.tan_x = tan_x;
+  c.tan_y = tan_y;
+  c.fx = width / (2.f * tan_x);
+  c.fy = height / (2.f * tan_y);
+  c.width = width;
+  c.height = height;
+  c.grid_x = (width + kTileX - 1) / kTileX;
+  c.grid_y = (height + kTileY - 1) / kTileY;
+  return c;
+}
+
+}  // namespace
+
+extern "C" size_t clad3dgs_raster_geom_bytes(int P) { return P > 0 ? geom_bytes(P) : 0; }
+extern "C" size_t clad3dgs_raster_image_bytes(int width, int height) {
+  const int tiles = ((width + kTileX - 1) / kTileX) * ((height + kTileY - 1) / kTileY);
+  return image_bytes(width * height, tiles);
+}
+extern "C" size_t clad3dgs_raster_binning_bytes(int instances) {
+  return instances > 0 ? binning_bytes(instances) : 0;
+}
+
+// Forward. The view-space / projection matrices, campos and bg are device
+// pointers; the three buffers are requested from the caller through `alloc`
+// (geom first, then image, then binning once the number of tile instances is
+// known), as the renderer's resizable buffers are.
+extern "C" int clad3dgs_raster_forward(
+    int P, int degree, const float* bg, const float* means, const float* colors_precomp,
+    const float* opacities, const float* scales, float scale_modifier,
+    const float* rotations, const float* cov3d_precomp, const float* view,
+    const float* proj, float tan_x, float tan_y, int height, int width,
+    const float* sh_packed, const float* sh_dc, const float* sh_rest, const float* campos,
+    int antialiasing, clad3dgs_alloc_fn alloc, void* alloc_ctx, float* out_color,
+    float* out_invdepth, int* radii, int* num_rendered, cudaStream_t stream) {
+  *num_rendered = 0;
+  if (degree < 0 || degree > 3)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
+  if (width <= 0 || height <= 0)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "image size must be positive");
+  const Camera cam = make_camera(view, proj, campos, width, height, tan_x, tan_y);
+  const int tiles = cam.grid_x * cam.grid_y;
+  char* image_base = alloc(alloc_ctx, 1, image_bytes(width * height, tiles));
+  if (!image_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "image buffer allocation failed");
+  ImageState img = image_from(image_base, width * height, tiles);
+  cudaError_t e = cudaMemsetAsync(img.ranges, 0, sizeof(uint2) * tiles, stream);
+  if (e != cudaSuccess) return status_of(e, "clearing tile ranges");
+  if (P > 0) {
+    char* geom_base = alloc(alloc_ctx, 0, geom_bytes(P));
+    if (!geom_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "geometry buffer allocation failed");
+    GeomState g = geom_from(geom_base, P);
+    const ShSource sh{sh_packed, sh_dc, sh_rest};
+    preprocess_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
+        P, degree, means, scales, scale_modifier, rotations, opacities, colors_precomp,
+        cov3d_precomp, sh, cam, antialiasing != 0, g, radii);
+    e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.tiles, g.offsets, P, stream);
+    if (e != cudaSuccess) return status_of(e, "tile scan");
+    uint32_t total = 0;
+    e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                        stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return status_of(e, "reading the instance count");
+    *num_rendered = int(total);
+    if (total > 0) {
+      char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
+      if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
+      BinningState b = binning_from(bin_base, int(total));
+      duplicate_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, cam, b.keys_unsorted,
+                                                           b.values_unsorted);
+      const int end_bit = 32 + bits_for(uint32_t(tiles));
+      e = cub::DeviceRadixSort::SortPairs(b.sort_tmp, b.sort_bytes, b.keys_unsorted, b.keys,
+                                          b.values_unsorted, b.values, int(total), 0,
+                                          end_bit, stream);
+      if (e != cudaSuccess) return status_of(e, "tile sort");
+      ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+      render_forward_kernel<<<dim3(cam.grid_x, cam.grid_y), kTilePixels, 0, stream>>>(
+          img.ranges, b.values, width, height, cam.grid_x, g.mean2d, g.rgb,
+          g.conic_opacity, g.depth, bg, img.final_t, img.n_contrib, out_color, out_invdepth);
+      return status_of(cudaPeekAtLastError(), "forward kernels");
+    }
+  }
+  // Nothing to draw: background everywhere.
+  render_forward_kernel<<<dim3(cam.grid_x, cam.grid_y), kTilePixels, 0, stream>>>(
+      img.ranges, nullptr, width, height, cam.grid_x, nullptr, nullptr, nullptr, nullptr, bg,
+      img.final_t, img.n_contrib, out_color, out_invdepth);
+  return status_of(cudaPeekAtLastError(), "forward kernels");
+}
+
+// Pixel backward only (used by the 2D benchmark and tests). dmean2d [P][3],
+// dconic [P][4], dopacity [P], dcolor [P][3], dinvdepth [P] (nullable) are
+// accumulated into (callers zero them).
+extern "C" int clad3dgs_raster_render_backward(
+    int P, int width, int height, const float* bg, const void* geom_buffer,
+    const void* binning_buffer, int num_rendered, const void* image_buffer,
+    const float* dpixels, const float* dinvdepth_pixels, float* dmean2d, float* dconic,
+    float* dopacity, float* dcolor, float* dinvdepth, int mode, cudaStream_t stream) {
+  if (mode < 0 || mode > 2)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "accumulation mode must be 0, 1 or 2");
+  if (P <= 0 || num_rendered <= 0) return CLAD3DGS_OK;
+  const int gx = (width + kTileX - 1) / kTileX, gy = (height + kTileY - 1) / kTileY;
+  GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
+  ImageState img = image_from(static_cast<char*>(const_cast<void*>(image_buffer)),
+                              width * height, gx * gy);
+  BinningState b = binning_from(static_cast<char*>(const_cast<void*>(binning_buffer)),
+                                num_rendered);
+  PixelGrads o{dmean2d, dconic, dopacity, dcolor, dinvdepth};
+  const dim3 grid(gx, gy);
+  if (mode == 0)
+    render_backward_kernel<0><<<grid, kTilePixels, 0, stream>>>(
+        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
+  else if (mode == 1)
+    render_backward_kernel<1><<<grid, kTilePixels, 0, stream>>>(
+        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
+  else
+    render_backward_kernel<2><<<grid, kTilePixels, 0, stream>>>(
+        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
+  return status_of(cudaPeekAtLastError(), "pixel backward");
+}
+
+// Full backward. Outputs (zeroed by the caller): dmean2d [P][3], dcolor [P][3],
+// dopacity [P], dmeans [P][3], dcov3d [P][6], dsh [P][16][3] (null when
+// consume_sh), dscales [P][3], drotations [P][4]. With consume_sh, the SH
+// adjoint is not written: dcolor (masked by the clamp flags) feeds the fused
+// SH + Adam kernel, which updates dc/rest and both moments in place and adds
+// the direction adjoint into dmeans (sh_consumer_split_torch_adam semantics).
+extern "C" int clad3dgs_raster_backward(
+    int P, int degree, const float* bg, const float* means, const int* radii,
+    const float* colors_precomp, const float* opacities, const float* scales,
+    float scale_modifier, const float* rotations, const float* cov3d_precomp,
+    const float* view, const float* proj, float tan_x, float tan_y, int height, int width,
+    const float* dpixels, const float* dinvdepth_pixels, const float* sh_packed,
+    const float* sh_dc, const float* sh_rest, const float* campos, const void* geom_buffer,
+    int num_rendered, const void* binning_buffer, const void* image_buffer,
+    int antialiasing, float* dmean2d, float* dcolor, float* dopacity, float* dmeans,
+    float* dcov3d, float* dsh, float* dscales, float* drotations, float* dconic_scratch,
+    float* dinvdepth_scratch, int mode, int consume_sh, float* dc, float* rest,
+    float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig config, cudaStream_t stream) {
+  if (degree < 0 || degree > 3)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
+  if (P <= 0) return CLAD3DGS_OK;
+  int status = clad3dgs_raster_render_backward(
+      P, width, height, bg, geom_buffer, binning_buffer, num_rendered, image_buffer, dpixels,
+      dinvdepth_pixels, dmean2d, dconic_scratch, dopacity, dcolor,
+      dinvdepth_pixels ? dinvdepth_scratch : nullptr, mode, stream);
+  if (status != CLAD3DGS_OK) return status;
+  const Camera cam = make_camera(view, proj, campos, width, height, tan_x, tan_y);
+  GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
+  const ShSource sh{sh_packed, sh_dc, sh_rest};
+  GeomGrads o{dmean2d, dconic_scratch, dopacity, dcolor,
+              dinvdepth_pixels ? dinvdepth_scratch : nullptr,
+              dmeans, dcov3d, consume_sh ? nullptr : dsh, dscales, drotations};
+  const bool from_sh = colors_precomp == nullptr && !consume_sh;
+  preprocess_backward_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
+      P, degree, means, scales, scale_modifier, rotations, opacities, cov3d_precomp, sh, cam,
+      antialiasing != 0, radii, g, from_sh, o);
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return status_of(e, "geometry backward");
+  if (consume_sh && colors_precomp == nullptr)
+    return clad3dgs_sh_consume_split_torch_adam(
+        P, degree, means, radii, sh_packed, g.clamped, campos, dcolor, dmeans, dc, rest,
+        dc_first, dc_second, rest_first, rest_second, config, stream);
+  return CLAD3DGS_OK;
+}
+
+// Binning + forward compositing of already projected 2D Gaussians (the pixel
+// stage alone, for the 2D benchmark configuration). Inputs: mean2d [P][2]
+// pixels, conic_opacity [P][4], rgb [P][3], depth [P], radii [P]. The geom
+// buffer is filled from them so clad3dgs_raster_render_backward can follow.
+extern "C" int clad3dgs_raster_forward_2d(int P, const float* mean2d,
+                                          const float* conic_opacity, const float* rgb,
+                                          const float* depth, const int* radii, int width,
+                                          int height, const float* bg,
+                                          clad3dgs_alloc_fn alloc, void* alloc_ctx,
+                                          float* out_color, float* out_invdepth,
+                                          int* num_rendered, cudaStream_t stream);
