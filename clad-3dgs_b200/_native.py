@@ -28,6 +28,8 @@ class TorchAdamConfig(ctypes.Structure):
 
 _P = c_void_p
 _PP = POINTER(c_void_p)
+# char* (*)(void* ctx, int which, size_t bytes): device buffer for the rasterizer.
+ALLOC_FN = ctypes.CFUNCTYPE(c_void_p, c_void_p, c_int, c_size_t)
 _SIGNATURES = {
     "sh_consumer_sgd": (None, [c_int, c_int, _P, _P, _P, _P, _P, _P, _P]),
     "sh_consumer_adam": (None, [c_int, c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, AdamConfig]),
@@ -54,6 +56,20 @@ _SIGNATURES = {
                                     + [_PP] * 5 + [POINTER(c_double), POINTER(c_float),
                                                    POINTER(c_float), _P, c_size_t, c_int64,
                                                    _P]),
+    "clad3dgs_raster_geom_bytes": (c_size_t, [c_int]),
+    "clad3dgs_raster_image_bytes": (c_size_t, [c_int, c_int]),
+    "clad3dgs_raster_binning_bytes": (c_size_t, [c_int]),
+    "clad3dgs_raster_forward": (c_int, [c_int, c_int] + [_P] * 5 + [c_float] + [_P] * 4
+                                + [c_float, c_float, c_int, c_int] + [_P] * 4
+                                + [c_int, _P, _P, _P, _P, _P, POINTER(c_int), _P]),
+    "clad3dgs_raster_render_backward": (c_int, [c_int, c_int, c_int] + [_P] * 3 + [c_int]
+                                        + [_P] * 8 + [c_int, _P]),
+    "clad3dgs_raster_backward": (c_int, [c_int, c_int] + [_P] * 6 + [c_float] + [_P] * 4
+                                 + [c_float, c_float, c_int, c_int] + [_P] * 7 + [c_int]
+                                 + [_P] * 2 + [c_int] + [_P] * 10 + [c_int, c_int]
+                                 + [_P] * 6 + [TorchAdamConfig, _P]),
+    "clad3dgs_raster_forward_2d": (c_int, [c_int] + [_P] * 5 + [c_int, c_int, _P, _P, _P,
+                                                               _P, _P, POINTER(c_int), _P]),
     "clad3dgs_gaussian_step_host_static": (c_int, [c_int64, c_int] + [_P] * 12
                                            + [TorchAdamConfig] + [_PP] * 5
                                            + [POINTER(c_double), POINTER(c_float),

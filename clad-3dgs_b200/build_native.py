@@ -33,6 +33,7 @@ COMMON = ARCH + [
 FLAGS = {
     "gaussian_step.cu": ["-fmad=false"],
     "host_step.cu": [],
+    "rasterizer.cu": [],
 }
 
 

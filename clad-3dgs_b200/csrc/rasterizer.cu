@@ -985,6 +985,32 @@ extern "C" int clad3dgs_raster_backward(
   return CLAD3DGS_OK;
 }
 
+namespace clad3dgs {
+namespace raster {
+__global__ void fill_2d_kernel(int P, const float* __restrict__ mean2d,
+                               const float* __restrict__ conic_opacity,
+                               const float* __restrict__ rgb, const float* __restrict__ depth,
+                               const int* __restrict__ radii, int grid_x, int grid_y,
+                               GeomState g) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  const float px = mean2d[2 * i], py = mean2d[2 * i + 1];
+  const int r = radii[i];
+  g.mean2d[i] = make_float2(px, py);
+  g.conic_opacity[i] = make_float4(conic_opacity[4 * i], conic_opacity[4 * i + 1],
+                                   conic_opacity[4 * i + 2], conic_opacity[4 * i + 3]);
+  g.rgb[3 * i] = rgb[3 * i];
+  g.rgb[3 * i + 1] = rgb[3 * i + 1];
+  g.rgb[3 * i + 2] = rgb[3 * i + 2];
+  g.depth[i] = depth[i];
+  g.radii[i] = r;
+  int x0, y0, x1, y1;
+  tile_rect(px, py, r, grid_x, grid_y, x0, y0, x1, y1);
+  g.tiles[i] = r > 0 ? uint32_t((x1 - x0) * (y1 - y0)) : 0u;
+}
+}  // namespace raster
+}  // namespace clad3dgs
+
 // Binning + forward compositing of already projected 2D Gaussians (the pixel
 // stage alone, for the 2D benchmark configuration). Inputs: mean2d [P][2]
 // pixels, conic_opacity [P][4], rgb [P][3], depth [P], radii [P]. The geom
@@ -995,4 +1021,45 @@ extern "C" int clad3dgs_raster_forward_2d(int P, const float* mean2d,
                                           int height, const float* bg,
                                           clad3dgs_alloc_fn alloc, void* alloc_ctx,
                                           float* out_color, float* out_invdepth,
-                                          int* num_rendered, cudaStream_t stream);
+                                          int* num_rendered, cudaStream_t stream) {
+  *num_rendered = 0;
+  if (P <= 0 || width <= 0 || height <= 0)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "need Gaussians and a positive image size");
+  const int gx = (width + kTileX - 1) / kTileX, gy = (height + kTileY - 1) / kTileY;
+  char* image_base = alloc(alloc_ctx, 1, image_bytes(width * height, gx * gy));
+  char* geom_base = alloc(alloc_ctx, 0, geom_bytes(P));
+  if (!image_base || !geom_base)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "buffer allocation failed");
+  ImageState img = image_from(image_base, width * height, gx * gy);
+  GeomState g = geom_from(geom_base, P);
+  cudaError_t e = cudaMemsetAsync(img.ranges, 0, sizeof(uint2) * gx * gy, stream);
+  if (e != cudaSuccess) return status_of(e, "clearing tile ranges");
+  fill_2d_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, mean2d, conic_opacity, rgb, depth,
+                                                      radii, gx, gy, g);
+  e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.tiles, g.offsets, P, stream);
+  if (e != cudaSuccess) return status_of(e, "tile scan");
+  uint32_t total = 0;
+  e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                      stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return status_of(e, "reading the instance count");
+  *num_rendered = int(total);
+  if (total == 0) return CLAD3DGS_OK;
+  char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
+  if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
+  BinningState b = binning_from(bin_base, int(total));
+  Camera cam{};
+  cam.grid_x = gx;
+  cam.grid_y = gy;
+  duplicate_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, cam, b.keys_unsorted,
+                                                       b.values_unsorted);
+  e = cub::DeviceRadixSort::SortPairs(b.sort_tmp, b.sort_bytes, b.keys_unsorted, b.keys,
+                                      b.values_unsorted, b.values, int(total), 0,
+                                      32 + bits_for(uint32_t(gx * gy)), stream);
+  if (e != cudaSuccess) return status_of(e, "tile sort");
+  ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+  render_forward_kernel<<<dim3(gx, gy), kTilePixels, 0, stream>>>(
+      img.ranges, b.values, width, height, gx, g.mean2d, g.rgb, g.conic_opacity, g.depth, bg,
+      img.final_t, img.n_contrib, out_color, out_invdepth);
+  return status_of(cudaPeekAtLastError(), "forward kernels");
+}

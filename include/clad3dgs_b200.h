@@ -194,6 +194,73 @@ int clad3dgs_gaussian_step_host(
     const float* bias1, const float* bias2, void* workspace_dev,
     size_t workspace_bytes, int64_t chunk_gaussians, cudaStream_t stream);
 
+/* ============================ rasterizer ============================ */
+
+/* Caller-provided buffer allocation: returns device memory of `bytes` for
+ * buffer `which` (0 geometry, 1 image, 2 binning), valid until the matching
+ * backward call (the renderer's resizable geom/image/binning buffers). */
+typedef char* (*clad3dgs_alloc_fn)(void* ctx, int which, size_t bytes);
+
+size_t clad3dgs_raster_geom_bytes(int P);
+size_t clad3dgs_raster_image_bytes(int width, int height);
+size_t clad3dgs_raster_binning_bytes(int instances);
+
+/* Forward rasterization of P Gaussians (the renderer's
+ * rasterize_gaussians, called at adapter.py:45-48 and check.py:768-774):
+ * projection, binning, sort and front-to-back compositing. SH colours come from
+ * sh_packed [P][16][3] or, when it is NULL, sh_dc [P][3] + sh_rest [P][45]
+ * (direct inputs, direct_inputs.py:6-34); colors_precomp [P][3] overrides both.
+ * view/proj are column-major 4x4, campos [3], bg [3]; out_color [3][H][W],
+ * out_invdepth [H][W] (nullable), radii [P]. num_rendered receives the number
+ * of tile instances. */
+int clad3dgs_raster_forward(
+    int P, int degree, const float* bg, const float* means, const float* colors_precomp,
+    const float* opacities, const float* scales, float scale_modifier,
+    const float* rotations, const float* cov3d_precomp, const float* view,
+    const float* proj, float tan_x, float tan_y, int height, int width,
+    const float* sh_packed, const float* sh_dc, const float* sh_rest, const float* campos,
+    int antialiasing, clad3dgs_alloc_fn alloc, void* alloc_ctx, float* out_color,
+    float* out_invdepth, int* radii, int* num_rendered, cudaStream_t stream);
+
+/* Pixel backward alone (accumulates into zeroed outputs): mode 0 per-lane
+ * atomics (the unpatched renderer), 1 the reference's full-warp accumulation
+ * (WarpAccumulation.cuh:9-29, injected by prepare_native.py:8-29), 2 converged
+ * warps with a transposing reduction (partial warps included). */
+int clad3dgs_raster_render_backward(
+    int P, int width, int height, const float* bg, const void* geom_buffer,
+    const void* binning_buffer, int num_rendered, const void* image_buffer,
+    const float* dpixels, const float* dinvdepth_pixels, float* dmean2d, float* dconic,
+    float* dopacity, float* dcolor, float* dinvdepth, int mode, cudaStream_t stream);
+
+/* Full backward (the renderer's rasterize_gaussians_backward, adapter.py:67-97)
+ * or, with consume_sh, the consumed variant (prepare_native.py:32-93,
+ * direct_inputs.py:151-171): the SH adjoint is applied by the fused SH + Adam
+ * kernel to dc/rest and both moments in place instead of being written to dsh.
+ * Outputs are accumulated into zeroed tensors; dconic_scratch [P][4] and
+ * dinvdepth_scratch [P] are zeroed scratch. */
+int clad3dgs_raster_backward(
+    int P, int degree, const float* bg, const float* means, const int* radii,
+    const float* colors_precomp, const float* opacities, const float* scales,
+    float scale_modifier, const float* rotations, const float* cov3d_precomp,
+    const float* view, const float* proj, float tan_x, float tan_y, int height, int width,
+    const float* dpixels, const float* dinvdepth_pixels, const float* sh_packed,
+    const float* sh_dc, const float* sh_rest, const float* campos, const void* geom_buffer,
+    int num_rendered, const void* binning_buffer, const void* image_buffer,
+    int antialiasing, float* dmean2d, float* dcolor, float* dopacity, float* dmeans,
+    float* dcov3d, float* dsh, float* dscales, float* drotations, float* dconic_scratch,
+    float* dinvdepth_scratch, int mode, int consume_sh, float* dc, float* rest,
+    float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig config, cudaStream_t stream);
+
+/* Binning + compositing of already projected 2D Gaussians (mean2d [P][2] px,
+ * conic_opacity [P][4], rgb [P][3], depth [P], radii [P]); fills the buffers
+ * clad3dgs_raster_render_backward consumes. */
+int clad3dgs_raster_forward_2d(int P, const float* mean2d, const float* conic_opacity,
+                               const float* rgb, const float* depth, const int* radii,
+                               int width, int height, const float* bg,
+                               clad3dgs_alloc_fn alloc, void* alloc_ctx, float* out_color,
+                               float* out_invdepth, int* num_rendered, cudaStream_t stream);
+
 /* Size of the fixed device staging area used by
  * clad3dgs_gaussian_step_host_static (bytes, on every GPU that loads this
  * library, held until the process exits). */

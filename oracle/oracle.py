@@ -203,3 +203,106 @@ def run_fixture_mode(fx, degree, mode, snapshot=True):
                inv_bias1=fx["adam"][0], inv_bias2=fx["adam"][1])
     join = lambda a, b: np.concatenate([a, b], axis=1)
     return dm, join(dc, rest), join(m_dc, m_rest), join(v_dc, v_rest)
+
+
+# --------------------------------------------------------------------------
+# Rasterizer oracle (raster_oracle.c), double precision.
+
+def _d(a):
+    return None if a is None else np.ascontiguousarray(a, np.float64)
+
+
+def _dp(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _scene_args(scene):
+    s = {k: _d(v) if isinstance(v, np.ndarray) else v for k, v in scene.items()}
+    return s, (ctypes.c_int(s["P"]), ctypes.c_int(s["degree"]), _dp(s["bg"]), _dp(s["means"]),
+               _dp(s["opacities"]), _dp(s["scales"]), ctypes.c_double(s["scale_modifier"]),
+               _dp(s["rotations"]), _dp(s["view"]), _dp(s["proj"]), ctypes.c_double(s["tanx"]),
+               ctypes.c_double(s["tany"]), ctypes.c_int(s["H"]), ctypes.c_int(s["W"]),
+               _dp(s["sh"]), _dp(s["campos"]), ctypes.c_int(int(s["antialiasing"])))
+
+
+def raster_forward(scene):
+    """-> (color [3,H,W], invdepth [H,W], radii [P])."""
+    s, args = _scene_args(scene)
+    color = np.zeros((3, s["H"], s["W"]))
+    inv = np.zeros((s["H"], s["W"]))
+    radii = np.zeros(s["P"], np.int32)
+    lib().oracle_raster_forward(*args, _dp(color), _dp(inv), radii.ctypes.data_as(ctypes.c_void_p))
+    return color, inv, radii
+
+
+def raster_backward(scene, dpix, dinv):
+    s, args = _scene_args(scene)
+    P = s["P"]
+    out = dict(dmean2d=np.zeros((P, 3)), dconic=np.zeros((P, 4)), dopacity=np.zeros(P),
+               dcolor=np.zeros((P, 3)), dinvdepth=np.zeros(P), dmeans=np.zeros((P, 3)),
+               dcov3d=np.zeros((P, 6)), dsh=np.zeros((P, 48)), dscales=np.zeros((P, 3)),
+               drots=np.zeros((P, 4)))
+    dpix, dinv = _d(dpix), _d(dinv)
+    lib().oracle_raster_backward(*args, _dp(dpix), _dp(dinv),
+                                 *[_dp(out[k]) for k in ("dmean2d", "dconic", "dopacity",
+                                                         "dcolor", "dinvdepth", "dmeans",
+                                                         "dcov3d", "dsh", "dscales", "drots")])
+    return out
+
+
+def raster_loss(scene, dpix, dinv):
+    s, args = _scene_args(scene)
+    dpix, dinv = _d(dpix), _d(dinv)
+    f = lib().oracle_raster_loss
+    f.restype = ctypes.c_double
+    return f(*args, _dp(dpix), _dp(dinv))
+
+
+def projection_matrix(znear, zfar, tanx, tany):
+    """OpenGL-style perspective (row-major) with z mapped to [0, 1] depth,
+    the convention of the 3DGS renderer's camera model."""
+    top, right = tany * znear, tanx * znear
+    P = np.zeros((4, 4))
+    P[0, 0] = 2 * znear / (2 * right)
+    P[1, 1] = 2 * znear / (2 * top)
+    P[3, 2] = 1.0
+    P[2, 2] = zfar / (zfar - znear)
+    P[2, 3] = -(zfar * znear) / (zfar - znear)
+    return P
+
+
+def raster_scene(P, H, W, seed=0, degree=3, antialiasing=False, spread=0.6, depth=(2.0, 4.0),
+                 scale=(0.02, 0.08), rotation=None):
+    """Random Gaussians in front of a camera; matrices in the renderer's
+    column-major convention (viewmatrix = world-to-camera transposed,
+    projmatrix = (proj @ world-to-camera) transposed)."""
+    rng = np.random.default_rng(seed)
+    tanx = tany = 0.5
+    ang = rng.uniform(-0.1, 0.1, 3) if rotation is None else rotation
+    cx, cy, cz = np.cos(ang)
+    sx, sy, sz = np.sin(ang)
+    Rx = np.array([[1, 0, 0], [0, cx, -sx], [0, sx, cx]])
+    Ry = np.array([[cy, 0, sy], [0, 1, 0], [-sy, 0, cy]])
+    Rz = np.array([[cz, -sz, 0], [sz, cz, 0], [0, 0, 1]])
+    R = Rz @ Ry @ Rx
+    t = rng.uniform(-0.1, 0.1, 3)
+    w2c = np.eye(4)
+    w2c[:3, :3] = R
+    w2c[:3, 3] = t
+    c2w = np.linalg.inv(w2c)
+    campos = c2w[:3, 3]
+    # Gaussians: place them in camera space, then map to world.
+    zc = rng.uniform(*depth, P)
+    xc = rng.uniform(-spread, spread, P) * zc * tanx
+    yc = rng.uniform(-spread, spread, P) * zc * tany
+    cam_pts = np.stack([xc, yc, zc, np.ones(P)], 1)
+    means = (c2w @ cam_pts.T).T[:, :3]
+    q = rng.standard_normal((P, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    proj = projection_matrix(0.01, 100.0, tanx, tany)
+    return dict(P=P, degree=degree, bg=np.array([0.1, 0.2, 0.3]), means=means,
+                opacities=rng.uniform(0.05, 0.99, P), scales=rng.uniform(*scale, (P, 3)),
+                scale_modifier=1.0, rotations=q, view=w2c.T.copy(),
+                proj=(proj @ w2c).T.copy(), tanx=tanx, tany=tany, H=H, W=W,
+                sh=rng.standard_normal((P, 48)) * 0.2, campos=campos,
+                antialiasing=antialiasing)

@@ -1,0 +1,476 @@
+/*
+ * CPU oracle of the Gaussian rasterizer (forward compositing and backward).
+ *
+ * TEST INFRASTRUCTURE ONLY: tests compare the CUDA rasterizer with it; the
+ * product never loads it.
+ *
+ * The reference patches a third-party renderer (graphdeco-inria/
+ * diff-gaussian-rasterization @ 9c5c2028, not vendored in the reference) whose
+ * arithmetic is therefore restated here from the published algorithms it
+ * implements: 3D Gaussian Splatting (Kerbl et al. 2023) and EWA splatting
+ * (Zwicker et al. 2001), with the conventions visible at the reference's call
+ * sites (adapter.py:21-117, check.py:743-1052, prepare_native.py:8-29):
+ * column-major view/projection matrices, quaternion (w, x, y, z), 0.3 px^2
+ * screen low-pass with the optional opacity compensation, 3-sigma radius,
+ * 16x16 tiles, alpha in [1/255, 0.99], stop below transmittance 1e-4, inverse
+ * depth output, colour = SH + 0.5 clamped at 0.
+ *
+ * Everything is double precision. The pixel order per tile is the sort order
+ * of the renderer: tile, then depth, then Gaussian index.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define TILE 16
+
+typedef struct {
+  double x, y, z;
+} v3;
+
+static v3 affine(const double* m, v3 p) {
+  v3 r = {m[0] * p.x + m[4] * p.y + m[8] * p.z + m[12],
+          m[1] * p.x + m[5] * p.y + m[9] * p.z + m[13],
+          m[2] * p.x + m[6] * p.y + m[10] * p.z + m[14]};
+  return r;
+}
+
+static double affine_w(const double* m, v3 p) {
+  return m[3] * p.x + m[7] * p.y + m[11] * p.z + m[15];
+}
+
+/* Standard rotation matrix of q = (w, x, y, z), row-major. */
+static void rot(const double* q, double R[9]) {
+  double w = q[0], x = q[1], y = q[2], z = q[3];
+  R[0] = 1 - 2 * (y * y + z * z); R[1] = 2 * (x * y - w * z); R[2] = 2 * (x * z + w * y);
+  R[3] = 2 * (x * y + w * z); R[4] = 1 - 2 * (x * x + z * z); R[5] = 2 * (y * z - w * x);
+  R[6] = 2 * (x * z - w * y); R[7] = 2 * (y * z + w * x); R[8] = 1 - 2 * (x * x + y * y);
+}
+
+static const double SH_C0 = 0.28209479177387814, SH_C1 = 0.4886025119029199;
+static const double SH_C2[5] = {1.0925484305920792, -1.0925484305920792, 0.31539156525252005,
+                                -1.0925484305920792, 0.5462742152960396};
+static const double SH_C3[7] = {-0.5900435899266435, 2.890611442640554, -0.4570457994644658,
+                                0.3731763325901154, -0.4570457994644658, 1.445305721320277,
+                                -0.5900435899266435};
+
+/* Basis values b[16] and their gradients g[16][3] wrt the unit direction. */
+static void sh_basis(double x, double y, double z, double b[16], double g[16][3]) {
+  double xx = x * x, yy = y * y, zz = z * z;
+  memset(g, 0, sizeof(double) * 48);
+  b[0] = SH_C0;
+  b[1] = -SH_C1 * y; g[1][1] = -SH_C1;
+  b[2] = SH_C1 * z; g[2][2] = SH_C1;
+  b[3] = -SH_C1 * x; g[3][0] = -SH_C1;
+  b[4] = SH_C2[0] * x * y; g[4][0] = SH_C2[0] * y; g[4][1] = SH_C2[0] * x;
+  b[5] = SH_C2[1] * y * z; g[5][1] = SH_C2[1] * z; g[5][2] = SH_C2[1] * y;
+  b[6] = SH_C2[2] * (2 * zz - xx - yy);
+  g[6][0] = -2 * SH_C2[2] * x; g[6][1] = -2 * SH_C2[2] * y; g[6][2] = 4 * SH_C2[2] * z;
+  b[7] = SH_C2[3] * x * z; g[7][0] = SH_C2[3] * z; g[7][2] = SH_C2[3] * x;
+  b[8] = SH_C2[4] * (xx - yy); g[8][0] = 2 * SH_C2[4] * x; g[8][1] = -2 * SH_C2[4] * y;
+  b[9] = SH_C3[0] * y * (3 * xx - yy);
+  g[9][0] = 6 * SH_C3[0] * x * y; g[9][1] = 3 * SH_C3[0] * (xx - yy);
+  b[10] = SH_C3[1] * x * y * z;
+  g[10][0] = SH_C3[1] * y * z; g[10][1] = SH_C3[1] * x * z; g[10][2] = SH_C3[1] * x * y;
+  b[11] = SH_C3[2] * y * (4 * zz - xx - yy);
+  g[11][0] = -2 * SH_C3[2] * x * y; g[11][1] = SH_C3[2] * (4 * zz - xx - 3 * yy);
+  g[11][2] = 8 * SH_C3[2] * y * z;
+  b[12] = SH_C3[3] * z * (2 * zz - 3 * xx - 3 * yy);
+  g[12][0] = -6 * SH_C3[3] * x * z; g[12][1] = -6 * SH_C3[3] * y * z;
+  g[12][2] = SH_C3[3] * (6 * zz - 3 * xx - 3 * yy);
+  b[13] = SH_C3[4] * x * (4 * zz - xx - yy);
+  g[13][0] = SH_C3[4] * (4 * zz - 3 * xx - yy); g[13][1] = -2 * SH_C3[4] * x * y;
+  g[13][2] = 8 * SH_C3[4] * x * z;
+  b[14] = SH_C3[5] * z * (xx - yy);
+  g[14][0] = 2 * SH_C3[5] * x * z; g[14][1] = -2 * SH_C3[5] * y * z; g[14][2] = SH_C3[5] * (xx - yy);
+  b[15] = SH_C3[6] * x * (xx - 3 * yy);
+  g[15][0] = 3 * SH_C3[6] * (xx - yy); g[15][1] = -6 * SH_C3[6] * x * y;
+}
+
+typedef struct {
+  int P, degree, H, W, antialias;
+  const double *bg, *means, *opacities, *scales, *rots, *view, *proj, *sh, *campos;
+  double mod, tanx, tany;
+} scene_t;
+
+typedef struct {
+  int visible, radius;
+  double px, py, depth, conic[3], opacity, aa, rgb[3], cov3[6], A[6];
+  double a0, b, c0;  /* screen covariance before the low-pass */
+  int clampx, clampy, clamped[3];
+  double tx, ty, tz, dir[3], dist;
+} proj_t;
+
+static void project(const scene_t* s, int i, proj_t* o) {
+  memset(o, 0, sizeof(*o));
+  v3 p = {s->means[3 * i], s->means[3 * i + 1], s->means[3 * i + 2]};
+  v3 t = affine(s->view, p);
+  if (t.z <= 0.2) return;
+  double sc[3] = {s->mod * s->scales[3 * i], s->mod * s->scales[3 * i + 1],
+                  s->mod * s->scales[3 * i + 2]};
+  double R[9];
+  rot(s->rots + 4 * i, R);
+  /* Sigma = R diag(s^2) R^T */
+  for (int r = 0, k = 0; r < 3; ++r)
+    for (int c = r; c < 3; ++c, ++k) {
+      double acc = 0;
+      for (int j = 0; j < 3; ++j) acc += R[3 * r + j] * sc[j] * sc[j] * R[3 * c + j];
+      o->cov3[k] = acc;
+    }
+  double W = s->W, H = s->H;
+  double fx = W / (2 * s->tanx), fy = H / (2 * s->tany);
+  double limx = 1.3 * s->tanx, limy = 1.3 * s->tany;
+  double rx = t.x / t.z, ry = t.y / t.z;
+  o->clampx = rx < -limx || rx > limx;
+  o->clampy = ry < -limy || ry > limy;
+  o->tx = fmin(limx, fmax(-limx, rx)) * t.z;
+  o->ty = fmin(limy, fmax(-limy, ry)) * t.z;
+  o->tz = t.z;
+  double J00 = fx / t.z, J02 = -fx * o->tx / (t.z * t.z);
+  double J11 = fy / t.z, J12 = -fy * o->ty / (t.z * t.z);
+  for (int c = 0; c < 3; ++c) {
+    /* camera rotation row r, column c = view[4c + r] */
+    o->A[c] = J00 * s->view[4 * c] + J02 * s->view[4 * c + 2];
+    o->A[3 + c] = J11 * s->view[4 * c + 1] + J12 * s->view[4 * c + 2];
+  }
+  double S[9] = {o->cov3[0], o->cov3[1], o->cov3[2], o->cov3[1], o->cov3[3], o->cov3[4],
+                 o->cov3[2], o->cov3[4], o->cov3[5]};
+  double q[2][2] = {{0, 0}, {0, 0}};
+  for (int r = 0; r < 2; ++r)
+    for (int c = 0; c < 2; ++c)
+      for (int k = 0; k < 3; ++k)
+        for (int l = 0; l < 3; ++l) q[r][c] += o->A[3 * r + k] * S[3 * k + l] * o->A[3 * c + l];
+  o->a0 = q[0][0]; o->b = q[0][1]; o->c0 = q[1][1];
+  double a = o->a0 + 0.3, c = o->c0 + 0.3;
+  double det0 = o->a0 * o->c0 - o->b * o->b, det = a * c - o->b * o->b;
+  o->aa = s->antialias ? sqrt(fmax(0.000025, det0 / det)) : 1.0;
+  if (det == 0) return;
+  double mid = 0.5 * (a + c), disc = sqrt(fmax(0.1, mid * mid - det));
+  o->radius = (int)ceil(3 * sqrt(fmax(mid + disc, mid - disc)));
+  double hw = affine_w(s->proj, p);
+  v3 h = affine(s->proj, p);
+  double iw = 1 / (hw + 0.0000001);
+  o->px = ((h.x * iw + 1) * W - 1) * 0.5;
+  o->py = ((h.y * iw + 1) * H - 1) * 0.5;
+  int gx = (s->W + TILE - 1) / TILE, gy = (s->H + TILE - 1) / TILE;
+  int x0 = (int)fmin(gx, fmax(0, (int)((o->px - o->radius) / TILE)));
+  int y0 = (int)fmin(gy, fmax(0, (int)((o->py - o->radius) / TILE)));
+  int x1 = (int)fmin(gx, fmax(0, (int)((o->px + o->radius + TILE - 1) / TILE)));
+  int y1 = (int)fmin(gy, fmax(0, (int)((o->py + o->radius + TILE - 1) / TILE)));
+  if ((x1 - x0) * (y1 - y0) == 0) { o->radius = 0; return; }
+  o->conic[0] = c / det; o->conic[1] = -o->b / det; o->conic[2] = a / det;
+  o->opacity = s->opacities[i] * o->aa;
+  double d[3] = {p.x - s->campos[0], p.y - s->campos[1], p.z - s->campos[2]};
+  o->dist = sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  for (int k = 0; k < 3; ++k) o->dir[k] = d[k] / o->dist;
+  double bb[16], gg[16][3];
+  sh_basis(o->dir[0], o->dir[1], o->dir[2], bb, gg);
+  int nt = (s->degree + 1) * (s->degree + 1);
+  for (int ch = 0; ch < 3; ++ch) {
+    double v = 0;
+    for (int j = 0; j < nt; ++j) v += bb[j] * s->sh[48 * i + 3 * j + ch];
+    v += 0.5;
+    o->clamped[ch] = v < 0;
+    o->rgb[ch] = fmax(v, 0);
+  }
+  o->depth = t.z;
+  o->visible = 1;
+}
+
+static int in_tile(const scene_t* s, const proj_t* g, int tx, int ty) {
+  int gx = (s->W + TILE - 1) / TILE, gy = (s->H + TILE - 1) / TILE;
+  int x0 = (int)fmin(gx, fmax(0, (int)((g->px - g->radius) / TILE)));
+  int y0 = (int)fmin(gy, fmax(0, (int)((g->py - g->radius) / TILE)));
+  int x1 = (int)fmin(gx, fmax(0, (int)((g->px + g->radius + TILE - 1) / TILE)));
+  int y1 = (int)fmin(gy, fmax(0, (int)((g->py + g->radius + TILE - 1) / TILE)));
+  return tx >= x0 && tx < x1 && ty >= y0 && ty < y1;
+}
+
+static const proj_t* g_sort_base;
+static int by_depth(const void* a, const void* b) {
+  int i = *(const int*)a, j = *(const int*)b;
+  float di = (float)g_sort_base[i].depth, dj = (float)g_sort_base[j].depth;
+  if (di != dj) return di < dj ? -1 : 1;
+  return i < j ? -1 : (i > j);
+}
+
+/* Forward + (when dpix != NULL) backward of the whole image.
+ * Gradient outputs (may be NULL in forward-only use) are accumulated. */
+static void render(const scene_t* s, double* color, double* invdepth, int* radii,
+                   const double* dpix, const double* dinv, double* dmean2d, double* dconic,
+                   double* dop_scaled, double* dcolor, double* dinvdepth) {
+  proj_t* g = calloc((size_t)s->P, sizeof(proj_t));
+  for (int i = 0; i < s->P; ++i) {
+    project(s, i, &g[i]);
+    if (radii) radii[i] = g[i].visible ? g[i].radius : 0;
+  }
+  int gx = (s->W + TILE - 1) / TILE, gy = (s->H + TILE - 1) / TILE;
+  int* list = malloc(sizeof(int) * (size_t)(s->P > 0 ? s->P : 1));
+  double* alpha_buf = malloc(sizeof(double) * (size_t)(s->P > 0 ? s->P : 1));
+  int* used = malloc(sizeof(int) * (size_t)(s->P > 0 ? s->P : 1));
+  for (int ty = 0; ty < gy; ++ty)
+    for (int tx = 0; tx < gx; ++tx) {
+      int n = 0;
+      for (int i = 0; i < s->P; ++i)
+        if (g[i].visible && g[i].radius > 0 && in_tile(s, &g[i], tx, ty)) list[n++] = i;
+      g_sort_base = g;
+      qsort(list, (size_t)n, sizeof(int), by_depth);
+      for (int py = ty * TILE; py < (ty + 1) * TILE && py < s->H; ++py)
+        for (int px = tx * TILE; px < (tx + 1) * TILE && px < s->W; ++px) {
+          int pix = py * s->W + px, m = 0;
+          double T = 1, C[3] = {0, 0, 0}, D = 0;
+          for (int k = 0; k < n; ++k) {
+            const proj_t* q = &g[list[k]];
+            double dx = q->px - px, dy = q->py - py;
+            double power = -0.5 * (q->conic[0] * dx * dx + q->conic[2] * dy * dy) -
+                           q->conic[1] * dx * dy;
+            if (power > 0) continue;
+            double alpha = fmin(0.99, q->opacity * exp(power));
+            if (alpha < 1.0 / 255.0) continue;
+            double tt = T * (1 - alpha);
+            if (tt < 0.0001) break;
+            for (int ch = 0; ch < 3; ++ch) C[ch] += q->rgb[ch] * alpha * T;
+            D += (1.0 / q->depth) * alpha * T;
+            T = tt;
+            used[m] = list[k];
+            alpha_buf[m] = alpha;
+            ++m;
+          }
+          int hw = s->H * s->W;
+          for (int ch = 0; ch < 3; ++ch) color[ch * hw + pix] = C[ch] + T * s->bg[ch];
+          if (invdepth) invdepth[pix] = D;
+          if (!dpix) continue;
+          /* Backward: walk the contributors back to front. */
+          double dp[3] = {dpix[pix], dpix[hw + pix], dpix[2 * hw + pix]};
+          double di = dinv ? dinv[pix] : 0;
+          double Tf = T, Tc = T, acc[3] = {0, 0, 0}, acc_i = 0, last_a = 0, last_c[3] = {0, 0, 0},
+                 last_i = 0;
+          double bgdot = s->bg[0] * dp[0] + s->bg[1] * dp[1] + s->bg[2] * dp[2];
+          for (int k = m - 1; k >= 0; --k) {
+            int id = used[k];
+            const proj_t* q = &g[id];
+            double alpha = alpha_buf[k];
+            double dx = q->px - px, dy = q->py - py;
+            double power = -0.5 * (q->conic[0] * dx * dx + q->conic[2] * dy * dy) -
+                           q->conic[1] * dx * dy;
+            double G = exp(power);
+            Tc = Tc / (1 - alpha);
+            double w = alpha * Tc, dl_dalpha = 0;
+            for (int ch = 0; ch < 3; ++ch) {
+              acc[ch] = last_a * last_c[ch] + (1 - last_a) * acc[ch];
+              last_c[ch] = q->rgb[ch];
+              dl_dalpha += (q->rgb[ch] - acc[ch]) * dp[ch];
+              dcolor[3 * id + ch] += w * dp[ch];
+            }
+            double inv = 1.0 / q->depth;
+            acc_i = last_a * last_i + (1 - last_a) * acc_i;
+            last_i = inv;
+            dl_dalpha += (inv - acc_i) * di;
+            if (dinvdepth) dinvdepth[id] += w * di;
+            dl_dalpha *= Tc;
+            last_a = alpha;
+            dl_dalpha += (-Tf / (1 - alpha)) * bgdot;
+            /* alpha = opacity * G below the 0.99 cap */
+            double dl_dg = q->opacity * dl_dalpha;
+            double gdx = G * dx, gdy = G * dy;
+            dmean2d[3 * id] += dl_dg * (-gdx * q->conic[0] - gdy * q->conic[1]) * 0.5 * s->W;
+            dmean2d[3 * id + 1] += dl_dg * (-gdy * q->conic[2] - gdx * q->conic[1]) * 0.5 * s->H;
+            dconic[4 * id] += -0.5 * gdx * dx * dl_dg;
+            dconic[4 * id + 1] += -0.5 * gdx * dy * dl_dg;
+            dconic[4 * id + 3] += -0.5 * gdy * dy * dl_dg;
+            dop_scaled[id] += G * dl_dalpha;
+          }
+        }
+    }
+  free(list);
+  free(alpha_buf);
+  free(used);
+  free(g);
+}
+
+static scene_t make_scene(int P, int degree, const double* bg, const double* means,
+                          const double* opacities, const double* scales, double mod,
+                          const double* rots, const double* view, const double* proj,
+                          double tanx, double tany, int H, int W, const double* sh,
+                          const double* campos, int antialias) {
+  scene_t s = {P, degree, H, W, antialias, bg, means, opacities, scales, rots, view, proj, sh,
+               campos, mod, tanx, tany};
+  return s;
+}
+
+void oracle_raster_forward(int P, int degree, const double* bg, const double* means,
+                           const double* opacities, const double* scales, double mod,
+                           const double* rots, const double* view, const double* proj,
+                           double tanx, double tany, int H, int W, const double* sh,
+                           const double* campos, int antialias, double* color,
+                           double* invdepth, int* radii) {
+  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                         tany, H, W, sh, campos, antialias);
+  render(&s, color, invdepth, radii, NULL, NULL, NULL, NULL, NULL, NULL, NULL);
+}
+
+/* Full backward. Outputs (zero-initialised by the caller, P-major like the
+ * renderer's): dmean2d [P][3], dconic [P][4], dopacity [P], dcolor [P][3],
+ * dinvdepth [P], dmeans [P][3], dcov3d [P][6], dsh [P][48], dscales [P][3],
+ * drots [P][4]. */
+void oracle_raster_backward(int P, int degree, const double* bg, const double* means,
+                            const double* opacities, const double* scales, double mod,
+                            const double* rots, const double* view, const double* proj,
+                            double tanx, double tany, int H, int W, const double* sh,
+                            const double* campos, int antialias, const double* dpix,
+                            const double* dinv, double* dmean2d, double* dconic,
+                            double* dopacity, double* dcolor, double* dinvdepth,
+                            double* dmeans, double* dcov3d, double* dsh, double* dscales,
+                            double* drots) {
+  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                         tany, H, W, sh, campos, antialias);
+  double* color = malloc(sizeof(double) * 3 * (size_t)H * W);
+  double* dop_scaled = calloc((size_t)(P > 0 ? P : 1), sizeof(double));
+  render(&s, color, NULL, NULL, dpix, dinv, dmean2d, dconic, dop_scaled, dcolor, dinvdepth);
+  free(color);
+  for (int i = 0; i < P; ++i) {
+    proj_t q;
+    project(&s, i, &q);
+    if (!q.visible) continue;
+    v3 p = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+    double a0 = q.a0, b = q.b, c0 = q.c0, a = a0 + 0.3, c = c0 + 0.3;
+    double det0 = a0 * c0 - b * b, det = a * c - b * b;
+    double dl_da = 0, dl_db = 0, dl_dc = 0;
+    double dop = dop_scaled[i];
+    dopacity[i] = dop * q.aa;
+    if (antialias) {
+      double r = det0 / det;
+      if (r > 0.000025) {
+        double dl_dr = dop * opacities[i] * 0.5 / sqrt(r);
+        dl_da += dl_dr * (c0 * det - det0 * c) / (det * det);
+        dl_db += dl_dr * (-2 * b * det + 2 * b * det0) / (det * det);
+        dl_dc += dl_dr * (a0 * det - det0 * a) / (det * det);
+      }
+    }
+    /* conic = inverse([[a, b], [b, c]]); dconic[1] is half the off-diagonal adjoint */
+    double gx = dconic[4 * i], gy = 2 * dconic[4 * i + 1], gz = dconic[4 * i + 3];
+    double d2 = det * det;
+    dl_da += (-c * c * gx + b * c * gy + (det - a * c) * gz) / d2;
+    dl_dc += ((det - a * c) * gx + a * b * gy - a * a * gz) / d2;
+    dl_db += (2 * b * c * gx - (det + 2 * b * b) * gy + 2 * a * b * gz) / d2;
+    /* screen covariance q = A S A^T: symmetric S, unique entries */
+    double S[9] = {q.cov3[0], q.cov3[1], q.cov3[2], q.cov3[1], q.cov3[3], q.cov3[4],
+                   q.cov3[2], q.cov3[4], q.cov3[5]};
+    const double *A0 = q.A, *A1 = q.A + 3;
+    int k = 0;
+    for (int r = 0; r < 3; ++r)
+      for (int cc = r; cc < 3; ++cc, ++k) {
+        double f = r == cc ? 1 : 2;
+        double sb = r == cc ? A0[r] * A1[r] : A0[r] * A1[cc] + A0[cc] * A1[r];
+        dcov3d[6 * i + k] += f * (A0[r] * A0[cc] * dl_da + A1[r] * A1[cc] * dl_dc) + sb * dl_db;
+      }
+    /* through A = J W to the camera-space mean */
+    double dA0[3], dA1[3];
+    for (int kk = 0; kk < 3; ++kk) {
+      double s0 = 0, s1 = 0;
+      for (int l = 0; l < 3; ++l) { s0 += S[3 * kk + l] * A0[l]; s1 += S[3 * kk + l] * A1[l]; }
+      dA0[kk] = 2 * dl_da * s0 + dl_db * s1;
+      dA1[kk] = dl_db * s0 + 2 * dl_dc * s1;
+    }
+    double dJ00 = 0, dJ02 = 0, dJ11 = 0, dJ12 = 0;
+    for (int col = 0; col < 3; ++col) {
+      dJ00 += dA0[col] * view[4 * col]; dJ02 += dA0[col] * view[4 * col + 2];
+      dJ11 += dA1[col] * view[4 * col + 1]; dJ12 += dA1[col] * view[4 * col + 2];
+    }
+    double fx = W / (2 * tanx), fy = H / (2 * tany), z = q.tz;
+    double dtx = (q.clampx ? 0 : 1) * -fx / (z * z) * dJ02;
+    double dty = (q.clampy ? 0 : 1) * -fy / (z * z) * dJ12;
+    double dtz = -fx / (z * z) * dJ00 - fy / (z * z) * dJ11 + 2 * fx * q.tx / (z * z * z) * dJ02 +
+                 2 * fy * q.ty / (z * z * z) * dJ12;
+    dtz += -dinvdepth[i] / (z * z);
+    double dm[3];
+    for (int kk = 0; kk < 3; ++kk)
+      dm[kk] = view[4 * kk] * dtx + view[4 * kk + 1] * dty + view[4 * kk + 2] * dtz;
+    /* projective divide: ndc = h.xy / (h.w + 1e-7) */
+    {
+      double hw = affine_w(proj, p) + 0.0000001;
+      v3 h = affine(proj, p);
+      for (int kk = 0; kk < 3; ++kk) {
+        dm[kk] += (proj[4 * kk] / hw - proj[4 * kk + 3] * h.x / (hw * hw)) * dmean2d[3 * i] +
+                  (proj[4 * kk + 1] / hw - proj[4 * kk + 3] * h.y / (hw * hw)) * dmean2d[3 * i + 1];
+      }
+    }
+    /* SH colour */
+    {
+      double bb[16], gg[16][3];
+      sh_basis(q.dir[0], q.dir[1], q.dir[2], bb, gg);
+      int nt = (degree + 1) * (degree + 1);
+      double gc[3], dd[3] = {0, 0, 0};
+      for (int ch = 0; ch < 3; ++ch) gc[ch] = q.clamped[ch] ? 0 : dcolor[3 * i + ch];
+      for (int j = 0; j < nt; ++j) {
+        double dot = 0;
+        for (int ch = 0; ch < 3; ++ch) {
+          dsh[48 * i + 3 * j + ch] += bb[j] * gc[ch];
+          dot += sh[48 * i + 3 * j + ch] * gc[ch];
+        }
+        for (int kk = 0; kk < 3; ++kk) dd[kk] += gg[j][kk] * dot;
+      }
+      double ds = q.dir[0] * dd[0] + q.dir[1] * dd[1] + q.dir[2] * dd[2];
+      for (int kk = 0; kk < 3; ++kk) dm[kk] += (dd[kk] - q.dir[kk] * ds) / q.dist;
+    }
+    for (int kk = 0; kk < 3; ++kk) dmeans[3 * i + kk] += dm[kk];
+    /* Sigma = R diag(s^2) R^T -> scale and rotation */
+    {
+      double G[9] = {dcov3d[6 * i], 0.5 * dcov3d[6 * i + 1], 0.5 * dcov3d[6 * i + 2],
+                     0.5 * dcov3d[6 * i + 1], dcov3d[6 * i + 3], 0.5 * dcov3d[6 * i + 4],
+                     0.5 * dcov3d[6 * i + 2], 0.5 * dcov3d[6 * i + 4], dcov3d[6 * i + 5]};
+      double sc[3] = {mod * scales[3 * i], mod * scales[3 * i + 1], mod * scales[3 * i + 2]};
+      double R[9], M[9], dM[9], dR[9];
+      rot(rots + 4 * i, R);
+      for (int r = 0; r < 3; ++r)
+        for (int cc = 0; cc < 3; ++cc) M[3 * r + cc] = R[3 * r + cc] * sc[cc];
+      for (int r = 0; r < 3; ++r)
+        for (int cc = 0; cc < 3; ++cc) {
+          double acc = 0;
+          for (int l = 0; l < 3; ++l) acc += G[3 * r + l] * M[3 * l + cc];
+          dM[3 * r + cc] = 2 * acc;
+        }
+      for (int cc = 0; cc < 3; ++cc)
+        dscales[3 * i + cc] += mod * (dM[cc] * R[cc] + dM[3 + cc] * R[3 + cc] + dM[6 + cc] * R[6 + cc]);
+      for (int r = 0; r < 3; ++r)
+        for (int cc = 0; cc < 3; ++cc) dR[3 * r + cc] = dM[3 * r + cc] * sc[cc];
+      /* dR/dq: numerically exact central difference of the polynomial map
+       * (degree 2, so the central difference is exact up to rounding). */
+      double qv[4] = {rots[4 * i], rots[4 * i + 1], rots[4 * i + 2], rots[4 * i + 3]};
+      for (int kq = 0; kq < 4; ++kq) {
+        double qp[4], qm[4], Rp[9], Rm[9], h = 1e-3, acc = 0;
+        memcpy(qp, qv, sizeof qp);
+        memcpy(qm, qv, sizeof qm);
+        qp[kq] += h;
+        qm[kq] -= h;
+        rot(qp, Rp);
+        rot(qm, Rm);
+        for (int l = 0; l < 9; ++l) acc += dR[l] * (Rp[l] - Rm[l]) / (2 * h);
+        drots[4 * i + kq] += acc;
+      }
+    }
+  }
+  free(dop_scaled);
+}
+
+/* The scalar loss sum(dpix * colour) + sum(dinv * inverse depth), for
+ * finite-difference checks of the backward. */
+double oracle_raster_loss(int P, int degree, const double* bg, const double* means,
+                          const double* opacities, const double* scales, double mod,
+                          const double* rots, const double* view, const double* proj,
+                          double tanx, double tany, int H, int W, const double* sh,
+                          const double* campos, int antialias, const double* dpix,
+                          const double* dinv) {
+  double* color = malloc(sizeof(double) * 3 * (size_t)H * W);
+  double* inv = malloc(sizeof(double) * (size_t)H * W);
+  oracle_raster_forward(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                        tany, H, W, sh, campos, antialias, color, inv, NULL);
+  double L = 0;
+  for (int k = 0; k < 3 * H * W; ++k) L += dpix[k] * color[k];
+  if (dinv)
+    for (int k = 0; k < H * W; ++k) L += dinv[k] * inv[k];
+  free(color);
+  free(inv);
+  return L;
+}

@@ -1,0 +1,197 @@
+"""CUDA rasterizer vs the double-precision oracle, warp-accumulation modes vs
+each other, and the consumed SH backward vs native SH gradients + torch fused
+Adam.
+
+Tolerances: forward colours within 1e-5 absolute; backward adjoints within the
+path's 1e-4 relative bound for atomically accumulated gradients, measured
+against each tensor's scale (|d| <= 1e-4 |ref| + 1e-4 max|ref|); the three
+pixel-accumulation modes agree within the reference's own warp-vs-native
+tolerance (check.py:815, rtol 5e-5, atol 2e-6) with bit-identical forwards.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, device, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype, device=device)
+
+
+def _render(scene, device, mode=2, dpix=None, dinv=None):
+    import rasterizer
+
+    rasterizer.pixel_accumulation = mode
+    P, H, W = scene["P"], scene["H"], scene["W"]
+    args = dict(
+        bg=_t(scene["bg"], device), means=_t(scene["means"], device).reshape(P, 3),
+        opacity=_t(scene["opacities"], device).reshape(P, 1),
+        scales=_t(scene["scales"], device).reshape(P, 3),
+        rotations=_t(scene["rotations"], device).reshape(P, 4),
+        view=_t(scene["view"], device), proj=_t(scene["proj"], device),
+        sh=_t(scene["sh"], device).reshape(P, 16, 3), campos=_t(scene["campos"], device))
+    empty = torch.empty(0, device=device)
+    out = rasterizer.rasterize_gaussians(
+        args["bg"], args["means"], empty, args["opacity"], args["scales"], args["rotations"],
+        scene["scale_modifier"], empty, args["view"], args["proj"], scene["tanx"],
+        scene["tany"], H, W, args["sh"], scene["degree"], args["campos"], False,
+        scene["antialiasing"], False)
+    num, color, radii, geom, binning, image, invdepth = out
+    grads = None
+    if dpix is not None:
+        grads = rasterizer.rasterize_gaussians_backward(
+            args["bg"], args["means"], radii, empty, args["opacity"], args["scales"],
+            args["rotations"], scene["scale_modifier"], empty, args["view"], args["proj"],
+            scene["tanx"], scene["tany"], _t(dpix, device), _t(dinv, device).reshape(1, H, W),
+            args["sh"], scene["degree"], args["campos"], geom, num, binning, image,
+            scene["antialiasing"], False)
+    torch.cuda.synchronize()
+    return num, color, radii, invdepth, grads
+
+
+def _close(got, ref, what, rel=1e-4):
+    got = np.asarray(got, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    scale = np.abs(ref).max() if ref.size else 0.0
+    bad = np.abs(got - ref) > rel * np.abs(ref) + rel * scale + 1e-12
+    assert not bad.any(), (what, int(bad.sum()), got[bad][:4], ref[bad][:4])
+
+
+@pytest.mark.parametrize("antialiasing", [False, True])
+@pytest.mark.parametrize("degree", [0, 3])
+@pytest.mark.parametrize("P,H,W", [(40, 48, 64), (300, 97, 131)])
+def test_rasterizer_matches_oracle(cuda, P, H, W, degree, antialiasing):
+    scene = oracle.raster_scene(P, H, W, seed=P + degree, degree=degree,
+                                antialiasing=antialiasing)
+    rng = np.random.default_rng(2)
+    dpix = rng.standard_normal((3, H, W)) * 0.1
+    dinv = rng.standard_normal((H, W)) * 0.01
+    num, color, radii, invdepth, grads = _render(scene, cuda, 2, dpix, dinv)
+    ocolor, oinv, oradii = oracle.raster_forward(scene)
+    assert np.array_equal(radii.cpu().numpy(), oradii)
+    assert np.abs(color.cpu().numpy() - ocolor).max() < 1e-5
+    assert np.abs(invdepth.cpu().numpy()[0] - oinv).max() < 1e-5 * max(1.0, np.abs(oinv).max())
+    ref = oracle.raster_backward(scene, dpix, dinv)
+    g2d, gcol, gop, gmean, gcov, gsh, gscale, grot = [g.cpu().numpy() for g in grads]
+    _close(g2d[:, :2], ref["dmean2d"][:, :2], "dL/dmean2D")
+    _close(gcol, ref["dcolor"], "dL/dcolors")
+    _close(gop.reshape(-1), ref["dopacity"], "dL/dopacity")
+    _close(gmean, ref["dmeans"], "dL/dmeans3D")
+    _close(gcov, ref["dcov3d"], "dL/dcov3D")
+    _close(gsh.reshape(P, 48), ref["dsh"], "dL/dsh")
+    _close(gscale, ref["dscales"], "dL/dscales")
+    _close(grot, ref["drots"], "dL/drotations")
+
+
+def _reference_fixture(name, n, H, W, scale, opacity, antialiasing):
+    """The reference's raster fixtures (check.py:745-767), restated."""
+    torch.manual_seed(42)
+    means = (torch.randn(n, 3) * .08)
+    means[:, 2] = torch.linspace(2., 3., n)
+    sh = torch.randn(n, 16, 3) * .02
+    proj = torch.tensor([[1., 0, 0, 0], [0, 1., 0, 0], [0, 0, 100 / 99.99, -1 / 99.99],
+                         [0, 0, 1., 0]]).T.contiguous()
+    rotations = torch.zeros(n, 4)
+    rotations[:, 0] = 1
+    return dict(P=n, degree=3, bg=np.array([.1, .2, .3]), means=means.numpy(),
+                opacities=np.full(n, opacity), scales=np.full((n, 3), scale),
+                scale_modifier=1.0, rotations=rotations.numpy(), view=np.eye(4),
+                proj=proj.numpy(), tanx=1.0, tany=1.0, H=H, W=W,
+                sh=sh.reshape(n, 48).numpy(), campos=np.zeros(3), antialiasing=antialiasing)
+
+
+FIXTURES = [("full-warp", 1, 32, 32, 2., .3), ("partial-tiles", 17, 17, 31, .2, .5),
+            ("occluded", 73, 32, 32, .8, .95), ("empty", 0, 17, 31, .2, .5)]
+
+
+@pytest.mark.parametrize("antialiasing", [False, True])
+@pytest.mark.parametrize("fixture", FIXTURES, ids=[f[0] for f in FIXTURES])
+def test_accumulation_modes_agree_on_reference_fixtures(cuda, fixture, antialiasing):
+    name, n, H, W, scale, opacity = fixture
+    scene = _reference_fixture(name, n, H, W, scale, opacity, antialiasing)
+    torch.manual_seed(7)
+    dpix = (torch.randn(3, H, W) * .01).numpy()
+    dinv = (torch.randn(H, W) * .01).numpy()
+    runs = [_render(scene, cuda, mode, dpix, dinv) for mode in (0, 1, 2)]
+    if name == "full-warp":
+        assert (runs[0][3] > 0).all(), "the full-warp fixture must cover every pixel"
+    base = runs[0]
+    for other in runs[1:]:
+        assert torch.equal(other[1], base[1]) and torch.equal(other[2], base[2])
+        assert torch.equal(other[3], base[3])
+        for g, b in zip(other[4], base[4]):
+            assert torch.isfinite(g).all()
+            torch.testing.assert_close(g, b, rtol=5e-5, atol=2e-6)
+    if n:
+        ref = oracle.raster_backward(scene, dpix, dinv)
+        _close(base[4][3].cpu().numpy(), ref["dmeans"], f"{name}: dL/dmeans3D")
+        _close(base[4][5].cpu().numpy().reshape(n, 48), ref["dsh"], f"{name}: dL/dsh")
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+@pytest.mark.parametrize("step", [1, 100])
+@pytest.mark.parametrize("direct", [False, True])
+def test_consumed_backward_matches_native_plus_fused_adam(cuda, degree, step, direct):
+    """check.py:980-1017: consume path vs native SH grads + torch fused Adam."""
+    import rasterizer
+
+    scene = oracle.raster_scene(64, 40, 56, seed=9 + degree, degree=degree)
+    P, H, W = 64, 40, 56
+    dev = cuda
+    empty = torch.empty(0, device=dev)
+    means = _t(scene["means"], dev)
+    opacity = _t(scene["opacities"], dev).reshape(P, 1)
+    scales, rots = _t(scene["scales"], dev), _t(scene["rotations"], dev)
+    view, proj = _t(scene["view"], dev), _t(scene["proj"], dev)
+    campos, bg = _t(scene["campos"], dev), _t(scene["bg"], dev)
+    coeffs = _t(scene["sh"], dev).reshape(P, 16, 3)
+    num, color, radii, geom, binning, image, inv = rasterizer.rasterize_gaussians(
+        bg, means, empty, opacity, scales, rots, 1.0, empty, view, proj, scene["tanx"],
+        scene["tany"], H, W, coeffs, degree, campos, False, False, False)
+    torch.manual_seed(3)
+    seed = torch.randn(3, H, W, device=dev) * 0.1
+    dseed = torch.zeros(1, H, W, device=dev)
+    common = (bg, means, radii, empty, opacity, scales, rots, 1.0, empty, view, proj,
+              scene["tanx"], scene["tany"], seed, dseed)
+    native = rasterizer.rasterize_gaussians_backward(*common, coeffs, degree, campos, geom,
+                                                     num, binning, image, False, False)
+    dc = coeffs[:, :1].contiguous().clone()
+    rest = coeffs[:, 1:].contiguous().clone()
+    fills = (0.002, 0.01, -0.003, 0.02) if step > 1 else (0.,) * 4
+    moments = [torch.full_like(v, f) for v, f in zip((dc, dc, rest, rest), fills)]
+    b1, b2 = 1 - 0.9 ** step, math.sqrt(1 - 0.999 ** step)
+    if direct:
+        consumed = rasterizer.rasterize_gaussians_backward_consume_direct(
+            *common, empty, degree, campos, geom, num, binning, image, False, False, dc, rest,
+            *moments, b1, b2)
+    else:
+        consumed = rasterizer.rasterize_gaussians_backward_consume(
+            *common, coeffs, degree, campos, geom, num, binning, image, False, False, dc, rest,
+            *moments, b1, b2)
+    params = [torch.nn.Parameter(coeffs[:, :1].contiguous().clone()),
+              torch.nn.Parameter(coeffs[:, 1:].contiguous().clone())]
+    opt = torch.optim.Adam([dict(params=[params[0]], lr=0.0025),
+                            dict(params=[params[1]], lr=0.000125)], eps=1e-15, fused=True,
+                           foreach=False)
+    for p_, g_, m_, v_ in zip(params, (native[5][:, :1], native[5][:, 1:]), fills[::2],
+                              fills[1::2]):
+        opt.state[p_] = dict(step=torch.tensor(float(step - 1), device=dev),
+                             exp_avg=torch.full_like(p_, m_), exp_avg_sq=torch.full_like(p_, v_))
+        p_.grad = g_.contiguous()
+    opt.step()
+    expected = [params[0], params[1], opt.state[params[0]]["exp_avg"],
+                opt.state[params[0]]["exp_avg_sq"], opt.state[params[1]]["exp_avg"],
+                opt.state[params[1]]["exp_avg_sq"]]
+    actual = [dc, rest, moments[0], moments[1], moments[2], moments[3]]
+    torch.cuda.synchronize()
+    for a, e in zip(actual, expected):
+        torch.testing.assert_close(a, e.detach(), rtol=3e-5, atol=2e-7)
+    assert consumed[5].numel() == 0
+    for k in (0, 1, 2, 3, 4, 6, 7):
+        torch.testing.assert_close(consumed[k], native[k], rtol=3e-5, atol=2e-7)
