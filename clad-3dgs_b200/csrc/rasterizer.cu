@@ -9,7 +9,8 @@
 // per-tile ranges -> compositing (one 16x16 CTA per tile, Gaussians staged in
 // shared memory in batches of 256).
 //
-// Pixel backward: the same traversal back to front. Every pixel contributes
+// Pixel backward: the same traversal back to front, starting at the tile's
+// largest last-contributor index rather than the end of its range. Every pixel contributes
 // ten adjoints per Gaussian (RGB, screen mean x/y, conic a/b/c, opacity,
 // inverse depth). Accumulation modes:
 //   0  one atomic per contributing lane and adjoint (the unpatched renderer);
@@ -479,8 +480,8 @@ __global__ void __launch_bounds__(kTilePixels)
   const int lane = threadIdx.x & 31;
   const float fx = (float)px, fy = (float)py;
   const uint2 range = ranges[tile];
-  const int todo = int(range.y - range.x);
   __shared__ uint32_t s_id[kBatch];
+  __shared__ uint32_t s_last_max;
   __shared__ float2 s_xy[kBatch];
   __shared__ float4 s_co[kBatch];
   __shared__ float s_rgb[3 * kBatch];
@@ -488,8 +489,17 @@ __global__ void __launch_bounds__(kTilePixels)
   const int hw = width * height;
   const float T_final = inside ? final_t[pix] : 0.f;
   float T = T_final;
-  uint32_t contributor = todo;
   const uint32_t last = inside ? n_contrib[pix] : 0;
+  // No pixel of the tile has a contributor past the largest last-contributor
+  // index, so the back-to-front walk starts there instead of at the end of the
+  // tile's range (identical results; the skipped Gaussians contribute nothing).
+  if (threadIdx.x == 0) s_last_max = 0;
+  __syncthreads();
+  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, last);
+  if (lane == 0) atomicMax(&s_last_max, warp_max);
+  __syncthreads();
+  const int todo = int(s_last_max);
+  uint32_t contributor = todo;
   float dpix[3] = {0.f, 0.f, 0.f}, dinv = 0.f;
   if (inside) {
     dpix[0] = dpixels[pix];
@@ -505,7 +515,7 @@ __global__ void __launch_bounds__(kTilePixels)
     __syncthreads();
     const int k = base + threadIdx.x;
     if (k < todo) {
-      const uint32_t id = point_list[range.y - k - 1];
+      const uint32_t id = point_list[range.x + todo - k - 1];
       s_id[threadIdx.x] = id;
       s_xy[threadIdx.x] = mean2d[id];
       s_co[threadIdx.x] = conic_opacity[id];

@@ -358,3 +358,39 @@ class GaussianRasterizer(torch.nn.Module):
             empty if colors_precomp is None else colors_precomp, opacities,
             empty if scales is None else scales, empty if rotations is None else rotations,
             empty if cov3D_precomp is None else cov3D_precomp, self.raster_settings)
+
+
+# ----------------------------------------------------------------------------
+# Pixel stage on already projected 2D Gaussians (benchmark and tests).
+
+def forward_2d(mean2d, conic_opacity, rgb, depth, radii, width, height, bg):
+    """Bins, sorts and composites projected Gaussians (mean2d [P,2] px,
+    conic_opacity [P,4], rgb [P,3], depth [P], radii [P] int32). Returns
+    (num_rendered, color [3,H,W], state) with state for render_backward_2d."""
+    device = mean2d.device
+    P = mean2d.shape[0]
+    color = torch.empty((3, height, width), dtype=torch.float32, device=device)
+    invdepth = torch.empty((1, height, width), dtype=torch.float32, device=device)
+    buffers = _Buffers(device)
+    num = ctypes.c_int(0)
+    keep = [t.contiguous() for t in (mean2d, conic_opacity, rgb, depth, radii, bg)]
+    native.check(native.library().clad3dgs_raster_forward_2d(
+        P, *[t.data_ptr() for t in keep[:5]], int(width), int(height), keep[5].data_ptr(),
+        ctypes.cast(buffers.callback, ctypes.c_void_p), None, color.data_ptr(),
+        invdepth.data_ptr(), ctypes.byref(num), native.stream_handle()), "forward_2d")
+    state = dict(P=P, width=int(width), height=int(height), bg=keep[5], geom=buffers.get(0),
+                 binning=buffers.get(2), image=buffers.get(1), num_rendered=num.value)
+    return num.value, color, invdepth, state
+
+
+def render_backward_2d(state, dpixels, grads, mode=None, dinvdepth_pixels=None):
+    """Pixel backward into grads = dict(dmean2d [P,3], dconic [P,4],
+    dopacity [P], dcolor [P,3], dinvdepth [P] or None), accumulated."""
+    mode = pixel_accumulation if mode is None else mode
+    native.check(native.library().clad3dgs_raster_render_backward(
+        state["P"], state["width"], state["height"], state["bg"].data_ptr(),
+        state["geom"].data_ptr(), state["binning"].data_ptr(), state["num_rendered"],
+        state["image"].data_ptr(), dpixels.data_ptr(), native.ptr(dinvdepth_pixels),
+        grads["dmean2d"].data_ptr(), grads["dconic"].data_ptr(), grads["dopacity"].data_ptr(),
+        grads["dcolor"].data_ptr(), native.ptr(grads.get("dinvdepth")), int(mode),
+        native.stream_handle()), "render_backward_2d")
