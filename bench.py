@@ -61,6 +61,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS,
                     help="Gaussians per GPU (smaller cases are for profiling only)")
+    ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
+                    help="pixel-backward: 2D Gaussians (smaller cases are for profiling only)")
+    ap.add_argument("--pixel-modes", default="2,1,0",
+                    help="pixel-backward: accumulation modes to time, first is reported")
     return ap.parse_args()
 
 
@@ -441,7 +445,7 @@ def pixel_backward_arm(args):
     import _native as native
 
     device = torch.device("cuda", 0)
-    W, H, n = 1920, 1080, 3_000_000
+    W, H, n = 1920, 1080, args.pixel_gaussians
     scene = make_2d_scene(n, W, H, device, seed=4)
     bg = torch.zeros(3, device=device)
     num, color, _inv, state = rasterizer.forward_2d(
@@ -459,7 +463,8 @@ def pixel_backward_arm(args):
     algorithmic = H * W * 20 + num * 40 + n * 36 + tiles * 8
     peak, peak_kind = measured_peaks()
     results = {}
-    for mode in (2, 1, 0):
+    modes = [int(m) for m in args.pixel_modes.split(",")]
+    for mode in modes:
         for _ in range(args.warmup):
             rasterizer.render_backward_2d(state, dpix, grads, mode)
         torch.cuda.synchronize()
@@ -471,19 +476,19 @@ def pixel_backward_arm(args):
         torch.cuda.synchronize()
         ms = ev[0].elapsed_time(ev[1]) / args.steps
         results[mode] = ms
-    ms = results[2]
+    ms = results[modes[0]]
+    names = {2: "converged_warp_reduction", 1: "full_warp_only (reference helper)",
+             0: "per_lane_atomics"}
     line = {
-        "metric": "rasterizer pixel backward, tile instances/s (1920x1080, 3M Gaussians)",
+        "metric": "rasterizer pixel backward, tile instances/s (1920x1080)",
         "value": num / (ms / 1e3), "unit": "instances/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "data": "synthetic (seeded 2D Gaussians of the pixel-backward configuration)",
-        "config": {"workload": "pixel backward, 1920x1080, 16x16 tiles, 3,000,000 depth-sorted "
+        "config": {"workload": f"pixel backward, 1920x1080, 16x16 tiles, {n:,} depth-sorted "
                                "2D Gaussians, radii lognormal(1.5, 0.7) px, opacity U(0.05,0.99), "
                                "T stop 1e-4, dL/dpixel N(0,1e-3)",
-                   "tile_instances": num,
-                   "ms_per_mode": {"converged_warp_reduction": results[2],
-                                   "full_warp_only (reference helper)": results[1],
-                                   "per_lane_atomics": results[0]}},
+                   "tile_instances": num, "accumulation_mode": modes[0],
+                   "ms_per_mode": {names[m]: results[m] for m in modes}},
         "roofline": {"bound": "hbm (plus L2 atomics)", "achieved": algorithmic / (ms / 1e3) / 1e9,
                      "peak": peak, "unit": "GB/s",
                      "frac": algorithmic / (ms / 1e3) / 1e9 / peak,
