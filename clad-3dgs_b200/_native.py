@@ -26,6 +26,21 @@ class TorchAdamConfig(ctypes.Structure):
     _fields_ = [("bias1", c_float), ("bias2_sqrt", c_float)]
 
 
+MAX_RANKS, SHARD_GROUPS, IPC_HANDLE_BYTES = 8, 5, 64
+
+
+class ShardUpdateArgs(ctypes.Structure):
+    """clad3dgs_shard_update_args."""
+    _fields_ = [("begin", c_int64), ("end", c_int64), ("grad_origin", c_int64),
+                ("ranks", c_int), ("local", c_int),
+                ("grads", (c_void_p * SHARD_GROUPS) * MAX_RANKS),
+                ("params", (c_void_p * SHARD_GROUPS) * MAX_RANKS),
+                ("first", c_void_p * SHARD_GROUPS), ("second", c_void_p * SHARD_GROUPS),
+                ("saved_scaling", c_void_p), ("saved_opacity", c_void_p),
+                ("saved_norm", c_void_p), ("rates", c_double * (SHARD_GROUPS + 1)),
+                ("bias1", c_float), ("bias2_sqrt", c_float)]
+
+
 _P = c_void_p
 _PP = POINTER(c_void_p)
 # char* (*)(void* ctx, int which, size_t bytes): device buffer for the rasterizer.
@@ -74,6 +89,13 @@ _SIGNATURES = {
                                            + [TorchAdamConfig] + [_PP] * 5
                                            + [POINTER(c_double), POINTER(c_float),
                                               POINTER(c_float), c_int64, _P]),
+    "clad3dgs_activate": (c_int, [c_int64] + [_P] * 7 + [_P]),
+    "clad3dgs_l1_loss": (c_int, [c_int64, _P, _P, _P, _P, _P]),
+    "clad3dgs_shard_update": (c_int, [POINTER(ShardUpdateArgs), _P]),
+    "clad3dgs_ipc_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(ctypes.c_ubyte)]),
+    "clad3dgs_ipc_free": (c_int, [_P]),
+    "clad3dgs_ipc_open": (c_int, [POINTER(ctypes.c_ubyte), POINTER(c_void_p)]),
+    "clad3dgs_ipc_close": (c_int, [_P]),
 }
 
 _lock = threading.Lock()

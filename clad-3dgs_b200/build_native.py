@@ -34,6 +34,7 @@ FLAGS = {
     "gaussian_step.cu": ["-fmad=false"],
     "host_step.cu": [],
     "rasterizer.cu": [],
+    "train_step.cu": ["-fmad=false"],
 }
 
 

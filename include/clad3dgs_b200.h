@@ -295,6 +295,65 @@ int clad3dgs_gaussian_step_host_static(
     const float* bias1, const float* bias2, int64_t chunk_gaussians,
     cudaStream_t stream);
 
+/* ===================== data-parallel training step ===================== */
+/* No counterpart in the reference (its trainer runs on one GPU). These serve
+ * the multi-GPU step: one camera view per GPU, parameters replicated, Adam
+ * moments sharded by Gaussian index. */
+
+#define CLAD3DGS_MAX_RANKS 8
+#define CLAD3DGS_SHARD_GROUPS 5  /* xyz 3, sh 48 ([16][3]), scaling 3, rotation 4, opacity 1 */
+#define CLAD3DGS_IPC_HANDLE_BYTES 64
+
+/* Forward activations of n Gaussians: scaling = exp(scaling_raw), rotation =
+ * rotation_raw / max(|rotation_raw|, 1e-12) with norms = |rotation_raw|,
+ * opacity = sigmoid(opacity_raw) (activation.py:24-37). Quaternion arrays
+ * 16-byte aligned. */
+int clad3dgs_activate(int64_t n, const float* scaling_raw, const float* rotation_raw,
+                      const float* opacity_raw, float* scaling, float* rotation,
+                      float* opacity, float* norms, cudaStream_t stream);
+
+/* Mean absolute error of image and target (n floats): dimage = sign(d) / n,
+ * *loss += sum |d| / n. */
+int clad3dgs_l1_loss(int64_t n, const float* image, const float* target, float* dimage,
+                     float* loss, cudaStream_t stream);
+
+/* Exchange and update of one GPU's share of the Gaussians, [begin, end):
+ * gradient = sum over q < ranks, in rank order, of grads[q][group]; the
+ * scaling, rotation and opacity gradients are taken with respect to the
+ * activated values and go through their activation VJPs (saved values from
+ * clad3dgs_activate); then torch-fused Adam (rates: xyz, f_dc, f_rest,
+ * scaling, rotation, opacity; SH coefficient 0 uses f_dc, 1..15 f_rest) with
+ * the moments first/second [end-begin][k] of this share, reading the current
+ * parameters from params[local] and storing the result into params[q] for every
+ * q < ranks. The pointers may be peer memory (clad3dgs_ipc_open) or local.
+ * grads arrays start at Gaussian grad_origin (0 for full arrays, begin for a
+ * share reduced by a collective); params and saved arrays start at Gaussian 0.
+ * begin, end and grad_origin are multiples of 4; arrays are 16-byte aligned.
+ * The caller orders the call after every source's gradients are complete and
+ * before any replica is read again (a barrier on each side). */
+typedef struct clad3dgs_shard_update_args {
+  int64_t begin, end, grad_origin;
+  int ranks, local;
+  const float* grads[CLAD3DGS_MAX_RANKS][CLAD3DGS_SHARD_GROUPS];
+  float* params[CLAD3DGS_MAX_RANKS][CLAD3DGS_SHARD_GROUPS];
+  float* first[CLAD3DGS_SHARD_GROUPS];
+  float* second[CLAD3DGS_SHARD_GROUPS];
+  const float* saved_scaling;  /* exp(scaling_raw) [N][3] */
+  const float* saved_opacity;  /* sigmoid(opacity_raw) [N] */
+  const float* saved_norm;     /* |rotation_raw| [N] */
+  double rates[CLAD3DGS_SHARD_GROUPS + 1];
+  float bias1, bias2_sqrt;     /* 1 - 0.9^t, sqrt(1 - 0.999^t) */
+} clad3dgs_shard_update_args;
+
+int clad3dgs_shard_update(const clad3dgs_shard_update_args* args, cudaStream_t stream);
+
+/* Device memory shareable with other processes of this node (CUDA IPC):
+ * zero-filled allocation + its 64-byte handle; open / close a peer's handle. */
+int clad3dgs_ipc_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int clad3dgs_ipc_free(void* ptr);
+int clad3dgs_ipc_open(const unsigned char* handle, void** ptr);
+int clad3dgs_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,8 @@
  *   scale/opacity VJP ... controls/ManualActivations.cu:94-100
  *   activation Adam ..... normalization.cu:70-77
  *   reference loss / FD . SHGradientConsumer.cu:404-433, 498-520
+ *   shard update ........ the data-parallel exchange: rank-ordered gradient
+ *                         sum, the activation VJPs and torch fused Adam above
  *
  * Every float/double operation is evaluated on its own, left to right as
  * written (compiled with -ffp-contract=off, no FMA), which is the evaluation
@@ -268,6 +270,54 @@ void oracle_activation_consume(int64_t n, float* const* params,
     const float a = saved[2][i];
     torch_adam(params[2] + i, first[2] + i, second[2] + i,
                (a * (1.f - a)) * seeds[2][i], step[2], bias2[2]);
+  }
+}
+
+/* Data-parallel exchange + update of the Gaussians [begin, end) (no
+ * reference counterpart; it combines the activation VJPs and torch-fused Adam
+ * above with a rank-ordered sum of per-view gradients). Groups g = 0..4 are
+ * xyz [.,3], sh [.,48], scaling [.,3], rotation [.,4], opacity [.,1];
+ * grads[q * 5 + g] start at Gaussian grad_origin, params[g] and the saved
+ * arrays at 0, first/second[g] at begin. rates: xyz, f_dc, f_rest, scaling,
+ * rotation, opacity. */
+void oracle_shard_update(int64_t begin, int64_t end, int64_t grad_origin,
+                         int ranks, const float* const* grads,
+                         float* const* params, float* const* first,
+                         float* const* second, const float* saved_scaling,
+                         const float* saved_opacity, const float* saved_norm,
+                         const double* rates, float bias1, float bias2) {
+  static const int width[5] = {3, 48, 3, 4, 1};
+  float step[6];
+  for (int r = 0; r < 6; ++r) step[r] = (float)(rates[r] / (double)bias1);
+  for (int g = 0; g < 5; ++g) {
+    const int k = width[g];
+    for (int64_t i = begin; i < end; ++i) {
+      float sum[48];
+      for (int c = 0; c < k; ++c) {
+        const int64_t e = (i - grad_origin) * k + c;
+        float s = grads[g][e];
+        for (int q = 1; q < ranks; ++q) s = s + grads[q * 5 + g][e];
+        sum[c] = s;
+      }
+      float grad[48];
+      float* p = params[g] + i * k;
+      for (int c = 0; c < k; ++c) {
+        if (g == 2)
+          grad[c] = saved_scaling[3 * i + c] * sum[c];
+        else if (g == 4)
+          grad[c] = (saved_opacity[i] * (1.f - saved_opacity[i])) * sum[c];
+        else if (g == 3)
+          grad[c] = quaternion_component(p, sum, saved_norm[i], c);
+        else
+          grad[c] = sum[c];
+      }
+      for (int c = 0; c < k; ++c) {
+        const float st = g == 1 ? (c < 3 ? step[1] : step[2])
+                                : step[g == 0 ? 0 : g + 1];
+        const int64_t m = (i - begin) * k + c;
+        torch_adam(p + c, first[g] + m, second[g] + m, grad[c], st, bias2);
+      }
+    }
   }
 }
 

@@ -94,6 +94,21 @@ def activation_consume(params, seeds, saved, first, second, rates, bias1, bias2)
         (ctypes.c_float * 3)(*[float(b) for b in bias2]))
 
 
+SHARD_WIDTHS = (3, 48, 3, 4, 1)  # xyz, sh, scaling, rotation, opacity
+
+
+def shard_update(begin, end, grad_origin, grads, params, first, second, saved_scaling,
+                 saved_opacity, saved_norm, rates, bias1, bias2):
+    """Exchange + update in place: grads[q][g] (rank q, group g), params[g],
+    first/second[g] of the share [begin, end), float32 numpy arrays."""
+    flat = [grads[q][g] for q in range(len(grads)) for g in range(5)]
+    lib().oracle_shard_update(
+        ctypes.c_int64(begin), ctypes.c_int64(end), ctypes.c_int64(grad_origin),
+        ctypes.c_int(len(grads)), _ptrs(flat), _ptrs(params), _ptrs(first), _ptrs(second),
+        _p(saved_scaling), _p(saved_opacity), _p(saved_norm),
+        (ctypes.c_double * 6)(*rates), ctypes.c_float(bias1), ctypes.c_float(bias2))
+
+
 def sh_fd_gradient(degree, means, radii, coeff, weights, camera, h=1e-5):
     """n x 51 central differences of the reference loss (position, 48 coeffs)."""
     n = int(radii.shape[0])

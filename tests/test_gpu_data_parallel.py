@@ -1,0 +1,313 @@
+"""The data-parallel step on the GPU.
+
+* `clad3dgs_shard_update` bit for bit against the oracle, for 1, 2, 3 and 8
+  ranks emulated on one GPU (separate gradient arrays and parameter replicas
+  per rank, every share updated in turn), over consecutive steps, and with a
+  share-sized gradient buffer (the collective path's form);
+* the activation and L1-loss kernels against torch;
+* one trainer step on one GPU against the same step through the autograd
+  rasterizer front end, torch activations and torch fused Adam (the path's
+  tolerances: rtol 3e-5 / atol 2e-7, Adam step-1 sign flips of rounding-level
+  gradients allowed);
+* on two GPUs (skipped with fewer): both exchanges (peer memory and NCCL
+  collectives), each rank's replica and moments bit-identical to the
+  emulation of the same gradients.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+
+from dp_helpers import GROUP_NAMES, RATES, initial_values, oracle_update, saved_from
+
+pytestmark = pytest.mark.gpu
+RATE_TUPLE = tuple(RATES[r] for r in ("xyz", "f_dc", "f_rest", "scaling", "rotation",
+                                      "opacity"))
+WIDTHS = (3, 48, 3, 4, 1)
+
+
+def _bias(t):
+    return 1 - 0.9 ** t, (1 - 0.999 ** t) ** 0.5
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_shard_update_matches_oracle(cuda, world):
+    from data_parallel import ShardStep, native_update, plan
+
+    n = 203
+    padded, share = plan(n, world)
+    values = initial_values(n)
+    dev = lambda a: torch.as_tensor(a).to(cuda).contiguous()
+    # Host copies (oracle) and device copies (kernel) of every replica.
+    host_params = {k: torch.zeros(padded, w) for k, w in zip(GROUP_NAMES, WIDTHS)}
+    for k in GROUP_NAMES:
+        host_params[k][:n] = values[k].reshape(n, -1)
+    replicas = [{k: dev(host_params[k]) for k in GROUP_NAMES} for _ in range(world)]
+    zeros = lambda: {k: torch.zeros(share, w) for k, w in zip(GROUP_NAMES, WIDTHS)}
+    host_m = [zeros() for _ in range(world)]
+    host_v = [zeros() for _ in range(world)]
+    dev_m = [{k: dev(t) for k, t in m.items()} for m in host_m]
+    dev_v = [{k: dev(t) for k, t in v.items()} for v in host_v]
+    for step in range(3):
+        g = torch.Generator().manual_seed(step)
+        grads = [{k: torch.randn(padded, w, generator=g) * 1e-3 for k, w in
+                  zip(GROUP_NAMES, WIDTHS)} for _ in range(world)]
+        saved = saved_from(host_params)
+        saved_t = dict(scaling=torch.from_numpy(saved["scaling"]),
+                       opacity=torch.from_numpy(saved["opacity"]).view(-1, 1),
+                       norm=torch.from_numpy(saved["norm"]))
+        saved_d = {k: dev(v) for k, v in saved_t.items()}
+        dev_grads = [{k: dev(v) for k, v in gr.items()} for gr in grads]
+        b1, b2 = _bias(step + 1)
+        for r in range(world):
+            common = dict(begin=r * share, end=(r + 1) * share, grad_origin=0, local=r,
+                          rates=RATE_TUPLE, bias1=b1, bias2_sqrt=b2)
+            oracle_update(ShardStep(
+                grads=[[grads[q][k] for k in GROUP_NAMES] for q in range(world)],
+                params=[[host_params[k] for k in GROUP_NAMES] for _ in range(world)],
+                first=[host_m[r][k] for k in GROUP_NAMES],
+                second=[host_v[r][k] for k in GROUP_NAMES], saved_scaling=saved_t["scaling"],
+                saved_opacity=saved_t["opacity"], saved_norm=saved_t["norm"], **common))
+            native_update(ShardStep(
+                grads=[[dev_grads[q][k] for k in GROUP_NAMES] for q in range(world)],
+                params=[[replicas[q][k] for k in GROUP_NAMES] for q in range(world)],
+                first=[dev_m[r][k] for k in GROUP_NAMES],
+                second=[dev_v[r][k] for k in GROUP_NAMES], saved_scaling=saved_d["scaling"],
+                saved_opacity=saved_d["opacity"], saved_norm=saved_d["norm"], **common))
+        torch.cuda.synchronize()
+        for q in range(world):
+            for k in GROUP_NAMES:
+                assert torch.equal(replicas[q][k].cpu(), host_params[k]), (step, q, k)
+        for r in range(world):
+            for k in GROUP_NAMES:
+                assert torch.equal(dev_m[r][k].cpu(), host_m[r][k]), (step, r, k)
+                assert torch.equal(dev_v[r][k].cpu(), host_v[r][k]), (step, r, k)
+
+
+def test_shard_update_from_a_reduced_share(cuda):
+    """grad_origin = begin: gradients of the share only (after reduce-scatter)."""
+    from data_parallel import ShardStep, native_update
+
+    n, begin, end = 64, 16, 48
+    values = initial_values(n)
+    host = {k: values[k].reshape(n, -1).clone() for k in GROUP_NAMES}
+    params = {k: v.to(cuda) for k, v in host.items()}
+    g = torch.Generator().manual_seed(9)
+    share = {k: torch.randn(end - begin, w, generator=g) * 1e-3 for k, w in
+             zip(GROUP_NAMES, WIDTHS)}
+    full = {k: torch.zeros(n, w) for k, w in zip(GROUP_NAMES, WIDTHS)}
+    for k in GROUP_NAMES:
+        full[k][begin:end] = share[k]
+    saved = saved_from(host)
+    saved_t = dict(scaling=torch.from_numpy(saved["scaling"]),
+                   opacity=torch.from_numpy(saved["opacity"]).view(-1, 1),
+                   norm=torch.from_numpy(saved["norm"]))
+    m = {k: torch.zeros(end - begin, w) for k, w in zip(GROUP_NAMES, WIDTHS)}
+    v = {k: torch.zeros(end - begin, w) for k, w in zip(GROUP_NAMES, WIDTHS)}
+    md = {k: t.to(cuda) for k, t in m.items()}
+    vd = {k: t.to(cuda) for k, t in v.items()}
+    b1, b2 = _bias(1)
+    oracle_update(ShardStep(begin, end, 0, [[full[k] for k in GROUP_NAMES]],
+                            [[host[k] for k in GROUP_NAMES]], 0, [m[k] for k in GROUP_NAMES],
+                            [v[k] for k in GROUP_NAMES], saved_t["scaling"],
+                            saved_t["opacity"], saved_t["norm"], RATE_TUPLE, b1, b2))
+    native_update(ShardStep(begin, end, begin, [[share[k].to(cuda) for k in GROUP_NAMES]],
+                            [[params[k] for k in GROUP_NAMES]], 0,
+                            [md[k] for k in GROUP_NAMES], [vd[k] for k in GROUP_NAMES],
+                            saved_t["scaling"].to(cuda), saved_t["opacity"].to(cuda),
+                            saved_t["norm"].to(cuda), RATE_TUPLE, b1, b2))
+    torch.cuda.synchronize()
+    for k in GROUP_NAMES:
+        assert torch.equal(params[k].cpu(), host[k]), k
+        assert torch.equal(md[k].cpu(), m[k]) and torch.equal(vd[k].cpu(), v[k]), k
+    assert torch.equal(params["xyz"][:begin].cpu(), values["xyz"][:begin])
+
+
+def test_shard_update_rejects_bad_ranges(cuda):
+    from data_parallel import ShardStep, native_update
+
+    t = torch.zeros(64, 48, device=cuda)
+    row = [t] * 5
+    bad = ShardStep(2, 34, 0, [row], [row], 0, row, row, t, t, t, RATE_TUPLE, 0.1, 0.03)
+    with pytest.raises(ValueError, match="multiples of 4"):
+        native_update(bad)
+    with pytest.raises(ValueError, match="local replica"):
+        native_update(bad._replace(begin=0, end=32, local=1))
+
+
+def test_activate_and_l1_loss_kernels(cuda):
+    import _native as native
+
+    n = 1001
+    v = initial_values(n, device=cuda)
+    out = dict(scaling=torch.empty(n, 3, device=cuda), rotation=torch.empty(n, 4, device=cuda),
+               opacity=torch.empty(n, 1, device=cuda), norm=torch.empty(n, device=cuda))
+    v["rotation"][5] = 0.0  # clamp branch
+    native.check(native.library().clad3dgs_activate(
+        n, v["scaling"].data_ptr(), v["rotation"].data_ptr(), v["opacity"].data_ptr(),
+        out["scaling"].data_ptr(), out["rotation"].data_ptr(), out["opacity"].data_ptr(),
+        out["norm"].data_ptr(), native.stream_handle()), "activate")
+    torch.testing.assert_close(out["scaling"], torch.exp(v["scaling"]), rtol=2e-7, atol=0)
+    torch.testing.assert_close(out["opacity"], torch.sigmoid(v["opacity"]), rtol=4e-7, atol=0)
+    torch.testing.assert_close(out["rotation"], torch.nn.functional.normalize(v["rotation"]),
+                               rtol=4e-7, atol=1e-30)
+    torch.testing.assert_close(out["norm"], v["rotation"].norm(dim=1), rtol=4e-7, atol=0)
+    img = torch.rand(3, 37, 53, device=cuda)
+    tgt = torch.rand(3, 37, 53, device=cuda)
+    tgt[0, 0, 0] = img[0, 0, 0]
+    x = img.clone().requires_grad_()
+    ref = (x - tgt).abs().mean()
+    ref.backward()
+    dimg = torch.empty_like(img)
+    loss = torch.zeros(1, device=cuda)
+    native.check(native.library().clad3dgs_l1_loss(img.numel(), img.data_ptr(), tgt.data_ptr(),
+                                                   dimg.data_ptr(), loss.data_ptr(),
+                                                   native.stream_handle()), "l1")
+    assert torch.equal(dimg, x.grad)
+    torch.testing.assert_close(loss[0], ref.detach(), rtol=1e-5, atol=0)
+
+
+def _small_scene(n, cuda):
+    v = initial_values(n, seed=5)
+    v["xyz"] = v["xyz"] * 0.6
+    v["scaling"] = torch.rand(n, 3, generator=torch.Generator().manual_seed(6)) * 2 - 5
+    return {k: t.to(cuda) for k, t in v.items()}
+
+
+def test_trainer_step_on_one_gpu_matches_autograd_path(cuda):
+    import rasterizer
+    from data_parallel import DataParallelTrainer, orbit_camera
+
+    n, W, H = 3000, 96, 64
+    values = _small_scene(n, cuda)
+    cam = orbit_camera(1, 8, width=W, height=H, device=cuda)
+    torch.manual_seed(1)
+    target = torch.rand(3, H, W, device=cuda)
+    trainer = DataParallelTrainer(values, RATES, device=cuda)
+    loss, rendered = trainer.step(cam, target)
+    assert rendered > 0
+    # The same step through the autograd front end and torch fused Adam.
+    P = {k: torch.nn.Parameter(values[k].clone()) for k in ("xyz", "scaling", "rotation",
+                                                             "opacity")}
+    dc = torch.nn.Parameter(values["sh"].view(n, 16, 3)[:, :1].clone())
+    rest = torch.nn.Parameter(values["sh"].view(n, 16, 3)[:, 1:].clone())
+    opt = torch.optim.Adam([dict(params=[P["xyz"]], lr=RATES["xyz"]),
+                            dict(params=[dc], lr=RATES["f_dc"]),
+                            dict(params=[rest], lr=RATES["f_rest"]),
+                            dict(params=[P["scaling"]], lr=RATES["scaling"]),
+                            dict(params=[P["rotation"]], lr=RATES["rotation"]),
+                            dict(params=[P["opacity"]], lr=RATES["opacity"])],
+                           eps=1e-15, fused=True)
+    settings = rasterizer.GaussianRasterizationSettings(
+        image_height=H, image_width=W, tanfovx=cam.tan_x, tanfovy=cam.tan_y,
+        bg=torch.zeros(3, device=cuda), scale_modifier=1.0, viewmatrix=cam.view,
+        projmatrix=cam.proj, sh_degree=3, campos=cam.campos, prefiltered=False, debug=False)
+    image, _radii, _depth = rasterizer.GaussianRasterizer(settings)(
+        means3D=P["xyz"], means2D=torch.zeros_like(P["xyz"], requires_grad=True),
+        opacities=torch.sigmoid(P["opacity"]), shs=torch.cat((dc, rest), 1),
+        scales=torch.exp(P["scaling"]), rotations=torch.nn.functional.normalize(P["rotation"]))
+    ref_loss = (image - target).abs().mean()
+    ref_loss.backward()
+    grads = {"xyz": P["xyz"].grad, "sh": torch.cat((dc.grad, rest.grad), 1).reshape(n, 48),
+             "scaling": P["scaling"].grad, "rotation": P["rotation"].grad,
+             "opacity": P["opacity"].grad}
+    opt.step()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(loss[0], ref_loss.detach(), rtol=1e-5, atol=0)
+    got = trainer.adam.params
+    expect = {"xyz": P["xyz"], "sh": torch.cat((dc, rest), 1).reshape(n, 48),
+              "scaling": P["scaling"], "rotation": P["rotation"], "opacity": P["opacity"]}
+    lr = {"xyz": RATES["xyz"], "sh": RATES["f_dc"], "scaling": RATES["scaling"],
+          "rotation": RATES["rotation"], "opacity": RATES["opacity"]}
+    for k in GROUP_NAMES:
+        a, b = got[k][:n], expect[k].detach()
+        close = (a - b).abs() <= 2e-7 + 3e-5 * b.abs()
+        g = grads[k]
+        tiny = g.abs() <= 1e-4 * g.abs().max()
+        close |= tiny & ((a - b).abs() <= 2.0001 * lr[k])
+        assert close.all(), (k, int((~close).sum()))
+    moved = (got["xyz"][:n] != values["xyz"]).any(dim=1)
+    assert moved.sum() > n // 4
+    trainer.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _dp_worker(rank, world, port, exchange, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from data_parallel import DataParallelTrainer, ShardStep, carve, native_update, orbit_camera
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=device)
+    trainer = None
+    try:
+        n, W, H = 2003, 96, 64
+        values = _small_scene(n, device)
+        trainer = DataParallelTrainer(values, RATES, exchange=exchange, device=device)
+        a = trainer.adam
+        assert a.world == world and a.exchange == exchange
+        cam = orbit_camera(rank, 8, width=W, height=H, device=device)
+        target = torch.rand(3, H, W, device=device,
+                            generator=torch.Generator(device=device).manual_seed(rank))
+        for step in range(3):
+            trainer.backward(cam, target)
+            # Every rank's gradients, the replica and this share's moments before the exchange.
+            mine = a.grad_slab.clone()
+            every = torch.empty(world * mine.numel(), device=device)
+            dist.all_gather_into_tensor(every, mine)
+            every = every.view(world, -1)
+            params = a.param_slab.clone()
+            first = {k: v.clone() for k, v in a.first.items()}
+            second = {k: v.clone() for k, v in a.second.items()}
+            a.step()
+            torch.cuda.synchronize()
+            # Emulation: the same kernel over local copies of all ranks' data.
+
+            grads = [carve(every[q], a.padded) for q in range(world)]
+            replica = carve(params, a.padded)
+            names = GROUP_NAMES
+            b1, b2 = _bias(step + 1)
+            native_update(ShardStep(a.begin, a.end, 0,
+                                    [[grads[q][k] for k in names] for q in range(world)],
+                                    [[replica[k] for k in names]] * world, 0,
+                                    [first[k] for k in names],
+                                    [second[k] for k in names], a.saved["scaling"],
+                                    a.saved["opacity"], a.saved["norm"], RATE_TUPLE, b1, b2))
+            lo, hi = a.begin, a.end
+            torch.cuda.synchronize()
+            for k in names:
+                assert torch.equal(a.params[k][lo:hi], replica[k][lo:hi]), (rank, step, k)
+                assert torch.equal(a.first[k], first[k]), (rank, step, k)
+                assert torch.equal(a.second[k], second[k]), (rank, step, k)
+            # Replicas agree across ranks.
+            ref = a.param_slab.clone()
+            dist.broadcast(ref, 0)
+            assert torch.equal(ref, a.param_slab), (rank, step)
+        with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
+            f.write("ok")
+    finally:
+        torch.cuda.synchronize()
+        if trainer is not None:
+            trainer.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("exchange", ["peer", "collective"])
+def test_two_gpu_exchange_matches_emulation(cuda, exchange, tmp_path):
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_dp_worker, args=(2, _free_port(), exchange, str(tmp_path)), nprocs=2)
+    assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
