@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--workload", choices=["fused-step", "pixel-backward"],
+    ap.add_argument("--workload", choices=["fused-step", "pixel-backward", "train-step"],
                     default="fused-step",
                     help="pixel-backward: the 1920x1080, 3M-Gaussian rasterizer pixel "
                          "backward configuration (timed for all accumulation modes)")
@@ -61,6 +61,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS,
                     help="Gaussians per GPU (smaller cases are for profiling only)")
+    ap.add_argument("--train-gaussians", type=int, default=6_000_000,
+                    help="train-step: replicated Gaussians (smaller cases are for profiling)")
+    ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
+                    help="train-step: gradient exchange (default: peer memory on >1 GPU)")
     ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
                     help="pixel-backward: 2D Gaussians (smaller cases are for profiling only)")
     ap.add_argument("--pixel-modes", default="2,1,0",
@@ -498,12 +502,193 @@ def pixel_backward_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def train_values(n, device, seed=3):
+    """Gaussians of the 8-view data-parallel configuration: means U[-1,1]^3,
+    f_dc N(0.5, 0.1), f_rest N(0, 0.05), log-scales U(-6, -2), quaternions
+    N(0, 1), opacity logits N(-2, 1)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    sh = torch.randn(n, 16, 3, generator=g, device=device) * 0.05
+    sh[:, 0] = 0.5 + 0.1 * torch.randn(n, 3, generator=g, device=device)
+    return dict(xyz=torch.rand(n, 3, generator=g, device=device) * 2 - 1,
+                sh=sh.reshape(n, 48),
+                scaling=torch.rand(n, 3, generator=g, device=device) * 4 - 6,
+                rotation=torch.randn(n, 4, generator=g, device=device),
+                opacity=torch.randn(n, 1, generator=g, device=device) - 2)
+
+
+TRAIN_GAUSSIANS, TRAIN_W, TRAIN_H = 6_000_000, 1920, 1080
+# Kernels of ours per training step: activate, preprocess, duplicate, ranges,
+# render forward, L1 loss, render backward, preprocess backward, shard update
+# (CUB's scan and sort and NCCL's barriers are library launches).
+TRAIN_LAUNCHES_PER_STEP = 9
+
+
+def train_step_arm(args):
+    """Full data-parallel training step: one 1920x1080 view per GPU of 6M
+    replicated Gaussians (SH degree 3), L1 loss, rasterizer backward, exchange +
+    sharded Adam. Value: views trained per second over all GPUs."""
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    import _native as native
+    from data_parallel import DataParallelTrainer, ShardedAdam, orbit_camera
+
+    n = args.train_gaussians
+    values = train_values(n, device)
+    trainer = DataParallelTrainer(values, exchange=args.exchange, device=device)
+    del values
+    cam = orbit_camera(rank % 8, 8, width=TRAIN_W, height=TRAIN_H, device=device)
+    gen = torch.Generator(device=device).manual_seed(100 + rank)
+    target = torch.rand(3, TRAIN_H, TRAIN_W, generator=gen, device=device)
+    stream = torch.cuda.current_stream()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def bracket():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    first_loss = None
+    instances = 0
+    with ClockSampler(local) as clocks:
+        for k in range(args.warmup):
+            loss, instances = trainer.step(cam, target)
+            if k == 0:
+                first_loss = float(loss.item())
+        bracket()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            loss, instances = trainer.step(cam, target)
+        ev[1].record(stream)
+        bracket()
+    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / args.steps)
+    last_loss = float(loss.item())
+    # The exchange + update alone (gradients of a real backward in place).
+    exchange_steps = max(3, min(args.steps, 20))
+    total = 0.0
+    for _ in range(exchange_steps):
+        trainer.backward(cam, target)
+        bracket()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        trainer.adam.step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    exchange_ms = max_over_ranks(total / exchange_steps)
+    adam = trainer.adam
+    baseline_ms = None
+    if world > 1 and adam.exchange == "peer":
+        # NCCL baseline of the same exchange: reduce-scatter, update, all-gather.
+        other = ShardedAdam(n, exchange="collective", device=device)
+        other.activate()
+        bracket()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(2):
+            other.step()
+        bracket()
+        e0.record(stream)
+        for _ in range(exchange_steps):
+            other.step()
+        e1.record(stream)
+        bracket()
+        baseline_ms = max_over_ranks(e0.elapsed_time(e1) / exchange_steps)
+        other.close()
+        del other
+    # End to end: each step's target comes from pinned host memory and the
+    # loss goes back to the host.
+    e2e = None
+    if not args.no_e2e:
+        host_target = target.cpu().pin_memory()
+        dev_target = torch.empty_like(target)
+        loss_host = torch.empty(1, pin_memory=True)
+        e2e_steps = max(3, min(args.steps, 20))
+        bracket()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            dev_target.copy_(host_target, non_blocking=True)
+            loss, _ = trainer.step(cam, dev_target)
+            loss_host.copy_(loss, non_blocking=True)
+        e1.record(stream)
+        bracket()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+        e2e = {"value": world / (e2e_ms / 1e3), "unit": "views/s",
+               "h2d_bytes_per_step": host_target.numel() * 4, "d2h_bytes_per_step": 4,
+               "ms_per_step": e2e_ms}
+    fault = native.fault_status()
+    padded, share = adam.padded, adam.share
+    trainer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    # Exchange roofline: bytes that must cross NVLink per GPU and direction
+    # (the other ranks' gradients of this share in, this share's parameters out
+    # to the other ranks), against the measured 770 GB/s peer copy; with one GPU
+    # the update is HBM-bound (grads, params, moments read; params, moments written).
+    floats = 59
+    if world > 1:
+        link = (world - 1) * share * floats * 4
+        exchange_roof = {"bound": "nvlink", "achieved": link / (exchange_ms / 1e3) / 1e9,
+                         "peak": 770.0, "unit": "GB/s",
+                         "frac": link / (exchange_ms / 1e3) / 1e9 / 770.0,
+                         "bytes_per_direction": link,
+                         "peak_kind": "measured peer copy per direction"}
+    else:
+        hbm = share * floats * 4 * 7  # grads, params, 2 moments read; params, 2 moments written
+        peak, peak_kind = measured_peaks()
+        exchange_roof = {"bound": "hbm", "achieved": hbm / (exchange_ms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": hbm / (exchange_ms / 1e3) / 1e9 / peak,
+                         "algorithmic_bytes": hbm, "peak_kind": peak_kind}
+    line = {
+        "metric": "data-parallel training step, views/s (one 1920x1080 view per GPU)",
+        "value": world / (step_ms / 1e3), "unit": "views/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "iters_per_s": 1e3 / step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32+f64",
+        "data": "synthetic (seeded; 6M Gaussians of the 8-view configuration, random targets)",
+        "config": {"workload": f"{n:,} Gaussians SH degree 3 replicated, one {TRAIN_W}x{TRAIN_H} "
+                               "view per GPU on a radius-4 orbit (fov 60), L1 loss, rasterizer "
+                               "backward, exchange + sharded torch-fused Adam",
+                   "exchange": adam.exchange, "padded_gaussians": padded,
+                   "share_per_gpu": share, "tile_instances_rank0": instances,
+                   "l2": "parameters 1.4 GB per replica exceed the 126 MB L2"},
+        "loss": {"first": first_loss, "last": last_loss},
+        "exchange": {"ms": exchange_ms, "nccl_baseline_ms": baseline_ms,
+                     "roofline": exchange_roof},
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+        "gpu_launches": TRAIN_LAUNCHES_PER_STEP * args.steps,
+        "device_fault_word": fault,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
     elif args.workload == "pixel-backward":
         pixel_backward_arm(args)
+    elif args.workload == "train-step":
+        train_step_arm(args)
     else:
         native_arm(args)
 
