@@ -31,6 +31,8 @@
 // fused SH + Adam kernel instead (see gaussian_step.cu).
 #include <cub/cub.cuh>
 
+#include <algorithm>
+#include <climits>
 #include <cstdint>
 #include <string>
 
@@ -64,14 +66,27 @@ struct GeomState {
   float4* conic_opacity; // conic (a, b, c), opacity x antialias factor
   float* rgb;            // [P][3]
   uint32_t* tiles;       // tiles touched
-  uint32_t* offsets;     // inclusive scan of tiles
+  uint32_t* offsets;     // inclusive scan of tiles touched, in depth order
+  uint32_t* depth_keys;  // depth bits (then tiles touched in depth order)
+  uint32_t* ids;         // 0..P-1
+  uint32_t* depth_sorted;
+  uint32_t* order;       // Gaussian ids by increasing depth
   void* scan_tmp;
   size_t scan_bytes;
+  void* order_tmp;
+  size_t order_bytes;
 };
 
 size_t scan_temp_bytes(int P) {
   size_t bytes = 0;
   cub::DeviceScan::InclusiveSum(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr, P);
+  return bytes;
+}
+
+size_t order_temp_bytes(int P) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (uint32_t*)nullptr, (uint32_t*)nullptr, P, 0, 32);
   return bytes;
 }
 
@@ -84,9 +99,9 @@ size_t geom_bytes(int P) {
   s += aligned<float>(sizeof(float) * 6 * P);
   s += aligned<float4>(sizeof(float4) * P);
   s += aligned<float>(sizeof(float) * 3 * P);
-  s += aligned<uint32_t>(sizeof(uint32_t) * P);
-  s += aligned<uint32_t>(sizeof(uint32_t) * P);
+  s += 6 * aligned<uint32_t>(sizeof(uint32_t) * P);
   s += aligned<char>(scan_temp_bytes(P));
+  s += aligned<char>(order_temp_bytes(P));
   return s + 128;
 }
 
@@ -107,8 +122,14 @@ GeomState geom_from(char* base, int P) {
   g.rgb = reinterpret_cast<float*>(take(sizeof(float) * 3 * P));
   g.tiles = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
   g.offsets = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.depth_keys = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.ids = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.depth_sorted = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.order = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
   g.scan_bytes = scan_temp_bytes(P);
   g.scan_tmp = take(g.scan_bytes);
+  g.order_bytes = order_temp_bytes(P);
+  g.order_tmp = take(g.order_bytes);
   return g;
 }
 
@@ -134,40 +155,38 @@ ImageState image_from(char* base, int pixels, int tiles) {
   return s;
 }
 
+// Tile instances: tile id keys and Gaussian id values, before and after the
+// stable sort by tile.
 struct BinningState {
-  uint64_t* keys_unsorted;
+  uint32_t* keys_unsorted;
   uint32_t* values_unsorted;
-  uint64_t* keys;
+  uint32_t* keys;
   uint32_t* values;
   void* sort_tmp;
   size_t sort_bytes;
 };
 
-size_t sort_temp_bytes(int n, int end_bit) {
+size_t sort_temp_bytes(int n) {
   size_t bytes = 0;
-  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint64_t*)nullptr, (uint64_t*)nullptr,
-                                  (uint32_t*)nullptr, (uint32_t*)nullptr, n, 0, end_bit);
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (uint32_t*)nullptr, (uint32_t*)nullptr, n, 0, 32);
   return bytes;
 }
 
 size_t binning_bytes(int n) {
-  return 2 * aligned<uint64_t>(8 * size_t(n)) + 2 * aligned<uint32_t>(4 * size_t(n)) +
-         aligned<char>(sort_temp_bytes(n, 64)) + 128;
+  return 4 * aligned<uint32_t>(4 * size_t(n)) + aligned<char>(sort_temp_bytes(n)) + 128;
 }
 
 BinningState binning_from(char* base, int n) {
   BinningState b;
   char* c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 127) & ~uintptr_t(127));
-  b.keys_unsorted = reinterpret_cast<uint64_t*>(c);
-  c += aligned<uint64_t>(8 * size_t(n));
-  b.keys = reinterpret_cast<uint64_t*>(c);
-  c += aligned<uint64_t>(8 * size_t(n));
-  b.values_unsorted = reinterpret_cast<uint32_t*>(c);
-  c += aligned<uint32_t>(4 * size_t(n));
-  b.values = reinterpret_cast<uint32_t*>(c);
-  c += aligned<uint32_t>(4 * size_t(n));
+  uint32_t** arrays[4] = {&b.keys_unsorted, &b.keys, &b.values_unsorted, &b.values};
+  for (uint32_t** a : arrays) {
+    *a = reinterpret_cast<uint32_t*>(c);
+    c += aligned<uint32_t>(4 * size_t(n));
+  }
   b.sort_tmp = c;
-  b.sort_bytes = sort_temp_bytes(n, 64);
+  b.sort_bytes = sort_temp_bytes(n);
   return b;
 }
 
@@ -313,30 +332,56 @@ __global__ void preprocess_kernel(int P, int degree, const float* __restrict__ m
   g.tiles[i] = touched;
 }
 
-__global__ void duplicate_kernel(int P, GeomState g, Camera cam, uint64_t* keys,
-                                 uint32_t* values) {
+// Binning. The Gaussians are first ordered by depth (a stable sort of P
+// depth keys), each Gaussian then writes its tile instances in that order, and
+// the instances are stable-sorted by tile id alone: within a tile they come out
+// by depth, ties by Gaussian index, the order a stable sort of
+// (tile << 32 | depth) keys gives, for a fraction of the sort traffic.
+__global__ void depth_key_kernel(int P, GeomState g) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= P || g.radii[i] <= 0) return;
-  uint32_t out = i == 0 ? 0 : g.offsets[i - 1];
-  int x0, y0, x1, y1;
-  const float2 m = g.mean2d[i];
-  tile_rect(m.x, m.y, g.radii[i], cam.grid_x, cam.grid_y, x0, y0, x1, y1);
-  const uint32_t depth_bits = __float_as_uint(g.depth[i]);
-  for (int y = y0; y < y1; ++y)
-    for (int x = x0; x < x1; ++x) {
-      keys[out] = (uint64_t(uint32_t(y * cam.grid_x + x)) << 32) | depth_bits;
-      values[out] = i;
-      ++out;
-    }
+  if (i >= P) return;
+  // Depths of drawn Gaussians are positive, so their bits order like floats;
+  // Gaussians without tiles go last.
+  g.depth_keys[i] = g.tiles[i] > 0 ? __float_as_uint(g.depth[i]) : 0xffffffffu;
+  g.ids[i] = uint32_t(i);
 }
 
-__global__ void ranges_kernel(int n, const uint64_t* keys, uint2* ranges) {
+__global__ void gather_counts_kernel(int P, GeomState g) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  g.depth_keys[i] = g.tiles[g.order[i]];
+}
+
+// One warp per Gaussian (in depth order): the lanes write consecutive
+// instances, so the stores coalesce.
+__global__ void duplicate_kernel(int P, GeomState g, int grid_x, int grid_y, uint32_t* keys,
+                                 uint32_t* values) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < P; i += warps) {
+    const uint32_t id = g.order[i];
+    const uint32_t count = g.tiles[id];
+    if (count == 0) continue;
+    const uint32_t start = i == 0 ? 0u : g.offsets[i - 1];
+    int x0, y0, x1, y1;
+    const float2 m = g.mean2d[id];
+    tile_rect(m.x, m.y, g.radii[id], grid_x, grid_y, x0, y0, x1, y1);
+    const uint32_t w = uint32_t(x1 - x0);
+    for (uint32_t j = lane; j < count; j += 32) {
+      const uint32_t y = uint32_t(y0) + j / w, x = uint32_t(x0) + j % w;
+      keys[start + j] = y * uint32_t(grid_x) + x;
+      values[start + j] = id;
+    }
+  }
+}
+
+__global__ void ranges_kernel(int n, const uint32_t* keys, uint2* ranges) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const uint32_t tile = uint32_t(keys[i] >> 32);
+  const uint32_t tile = keys[i];
   if (i == 0) ranges[tile].x = 0;
   else {
-    const uint32_t prev = uint32_t(keys[i - 1] >> 32);
+    const uint32_t prev = keys[i - 1];
     if (tile != prev) {
       ranges[prev].y = i;
       ranges[tile].x = i;
@@ -822,6 +867,45 @@ int bits_for(uint32_t v) {
   return b;
 }
 
+// Depth order, instance counts and their scan (see duplicate_kernel); reads
+// the instance total back to the host. Needs g.depth, g.tiles, g.mean2d, g.radii.
+int order_and_count(int P, GeomState& g, uint32_t& total, cudaStream_t stream) {
+  const int blocks = (P + 255) / 256;
+  depth_key_kernel<<<blocks, 256, 0, stream>>>(P, g);
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(g.order_tmp, g.order_bytes, g.depth_keys,
+                                                  g.depth_sorted, g.ids, g.order, P, 0, 32,
+                                                  stream);
+  if (e != cudaSuccess) return status_of(e, "depth order");
+  gather_counts_kernel<<<blocks, 256, 0, stream>>>(P, g);
+  e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.depth_keys, g.offsets, P,
+                                    stream);
+  if (e != cudaSuccess) return status_of(e, "tile scan");
+  total = 0;
+  e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                      stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return status_of(e, "reading the instance count");
+  return CLAD3DGS_OK;
+}
+
+// Instances in depth order, stable-sorted by tile, and the per-tile ranges.
+int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t total,
+                  const BinningState& b, const ImageState& img, cudaStream_t stream) {
+  const int warps_per_block = 8;
+  const int blocks = int(std::min<long long>((P + warps_per_block - 1) / warps_per_block,
+                                             148LL * 64));
+  duplicate_kernel<<<blocks, 32 * warps_per_block, 0, stream>>>(P, g, grid_x, grid_y,
+                                                               b.keys_unsorted,
+                                                               b.values_unsorted);
+  size_t sort_bytes = b.sort_bytes;
+  const cudaError_t e = cub::DeviceRadixSort::SortPairs(
+      b.sort_tmp, sort_bytes, b.keys_unsorted, b.keys, b.values_unsorted, b.values,
+      int(total), 0, bits_for(uint32_t(grid_x * grid_y)), stream);
+  if (e != cudaSuccess) return status_of(e, "tile sort");
+  ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+  return CLAD3DGS_OK;
+}
+
 Camera make_camera(const float* view, const float* proj, const float* campos, int width,
                    int height, float tan_x, float tan_y) {
   Camera c;
@@ -882,26 +966,18 @@ extern "C" int clad3dgs_raster_forward(
     preprocess_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
         P, degree, means, scales, scale_modifier, rotations, opacities, colors_precomp,
         cov3d_precomp, sh, cam, antialiasing != 0, g, radii);
-    e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.tiles, g.offsets, P, stream);
-    if (e != cudaSuccess) return status_of(e, "tile scan");
     uint32_t total = 0;
-    e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                        stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return status_of(e, "reading the instance count");
+    int status = order_and_count(P, g, total, stream);
+    if (status != CLAD3DGS_OK) return status;
+    if (total > uint32_t(INT32_MAX))
+      return fail(CLAD3DGS_INVALID_ARGUMENT, "more than 2^31 - 1 tile instances");
     *num_rendered = int(total);
     if (total > 0) {
       char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
       if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
       BinningState b = binning_from(bin_base, int(total));
-      duplicate_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, cam, b.keys_unsorted,
-                                                           b.values_unsorted);
-      const int end_bit = 32 + bits_for(uint32_t(tiles));
-      e = cub::DeviceRadixSort::SortPairs(b.sort_tmp, b.sort_bytes, b.keys_unsorted, b.keys,
-                                          b.values_unsorted, b.values, int(total), 0,
-                                          end_bit, stream);
-      if (e != cudaSuccess) return status_of(e, "tile sort");
-      ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+      status = bin_instances(P, g, cam.grid_x, cam.grid_y, total, b, img, stream);
+      if (status != CLAD3DGS_OK) return status;
       render_forward_kernel<<<dim3(cam.grid_x, cam.grid_y), kTilePixels, 0, stream>>>(
           img.ranges, b.values, width, height, cam.grid_x, g.mean2d, g.rgb,
           g.conic_opacity, g.depth, bg, img.final_t, img.n_contrib, out_color, out_invdepth);
@@ -1046,28 +1122,18 @@ extern "C" int clad3dgs_raster_forward_2d(int P, const float* mean2d,
   if (e != cudaSuccess) return status_of(e, "clearing tile ranges");
   fill_2d_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, mean2d, conic_opacity, rgb, depth,
                                                       radii, gx, gy, g);
-  e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.tiles, g.offsets, P, stream);
-  if (e != cudaSuccess) return status_of(e, "tile scan");
   uint32_t total = 0;
-  e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                      stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-  if (e != cudaSuccess) return status_of(e, "reading the instance count");
+  int status = order_and_count(P, g, total, stream);
+  if (status != CLAD3DGS_OK) return status;
+  if (total > uint32_t(INT32_MAX))
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "more than 2^31 - 1 tile instances");
   *num_rendered = int(total);
   if (total == 0) return CLAD3DGS_OK;
   char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
   if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
   BinningState b = binning_from(bin_base, int(total));
-  Camera cam{};
-  cam.grid_x = gx;
-  cam.grid_y = gy;
-  duplicate_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, cam, b.keys_unsorted,
-                                                       b.values_unsorted);
-  e = cub::DeviceRadixSort::SortPairs(b.sort_tmp, b.sort_bytes, b.keys_unsorted, b.keys,
-                                      b.values_unsorted, b.values, int(total), 0,
-                                      32 + bits_for(uint32_t(gx * gy)), stream);
-  if (e != cudaSuccess) return status_of(e, "tile sort");
-  ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+  status = bin_instances(P, g, gx, gy, total, b, img, stream);
+  if (status != CLAD3DGS_OK) return status;
   render_forward_kernel<<<dim3(gx, gy), kTilePixels, 0, stream>>>(
       img.ranges, b.values, width, height, gx, g.mean2d, g.rgb, g.conic_opacity, g.depth, bg,
       img.final_t, img.n_contrib, out_color, out_invdepth);
