@@ -138,5 +138,85 @@ __device__ __forceinline__ void tile_rect(float px, float py, int radius, int gr
   y1 = min(grid_y, max(0, (int)((py + radius + kTileY - 1) / kTileY)));
 }
 
+// Exact tile footprint. The renderer skips a (pixel, Gaussian) pair when
+// alpha = opacity * exp(-q/2) < 1/255, q = A dx^2 + 2B dx dy + C dy^2 with the
+// conic (A, B, C) and d = pixel centre - mean. So a tile whose pixel centres all
+// have q > tau = 2 ln(255 opacity) receives nothing from the Gaussian and can be
+// left out of its instance list without changing any output. Per tile row, the
+// pixel-centre band [16 ty, 16 ty + 15] meets the ellipse q <= tau in one x
+// interval (the ellipse is convex); its ends come from the ellipse's extreme
+// points clamped into the band. tau and the interval carry a margin far above
+// float rounding, and the result never leaves the 3-sigma tile rectangle the
+// renderer uses, so the kept set always contains every contributing tile.
+struct Footprint {
+  float mx, my;     // mean, pixels
+  float A, B, C;    // conic
+  float tau;        // culling level (with margin); < 0: no pixel can contribute
+  bool ellipse;     // false: conic not positive definite, keep whole rows
+  int x0, y0, x1, y1;  // tile rectangle of the 3-sigma radius
+};
+
+__device__ __forceinline__ Footprint make_footprint(float px, float py, float4 co, int radius,
+                                                    int grid_x, int grid_y) {
+  Footprint f;
+  f.mx = px;
+  f.my = py;
+  f.A = co.x;
+  f.B = co.y;
+  f.C = co.z;
+  const float o255 = __fmul_rn(255.f, co.w);
+  f.tau = o255 > 0.f ? __fmul_rn(2.f, logf(o255)) : -1.f;
+  if (f.tau >= 0.f) f.tau = __fadd_rn(__fmul_rn(f.tau, 1.001f), 0.01f);
+  const float detc = __fsub_rn(__fmul_rn(f.A, f.C), __fmul_rn(f.B, f.B));
+  f.ellipse = f.A > 0.f && f.C > 0.f && detc > 0.f;
+  tile_rect(px, py, radius, grid_x, grid_y, f.x0, f.y0, f.x1, f.y1);
+  return f;
+}
+
+// Tiles [lo, hi) of tile row ty that the footprint reaches (lo >= hi: none).
+// Every operation is an explicitly rounded intrinsic, so the count taken in
+// one kernel and the instances written in another agree bit for bit.
+__device__ __forceinline__ void row_span(const Footprint& f, int ty, int& lo, int& hi) {
+  lo = f.x0;
+  hi = f.x1;
+  if (!f.ellipse) return;
+  if (f.tau < 0.f) {
+    hi = lo;
+    return;
+  }
+  constexpr float kPad = 0.05f;  // pixels
+  const float detc = __fsub_rn(__fmul_rn(f.A, f.C), __fmul_rn(f.B, f.B));
+  const float ymax = __fsqrt_rn(__fdiv_rn(__fmul_rn(f.tau, f.A), detc));
+  const float a = fmaxf(__fsub_rn(float(ty * kTileY) - kPad, f.my), -ymax);
+  const float b = fminf(__fsub_rn(float(ty * kTileY + kTileY - 1) + kPad, f.my), ymax);
+  if (a > b) {
+    hi = lo;
+    return;
+  }
+  // Extreme points of the ellipse in x sit at dy = -/+ B sqrt(tau / (C detc)).
+  const float dyr = __fmul_rn(-f.B, __fsqrt_rn(__fdiv_rn(f.tau, __fmul_rn(f.C, detc))));
+  const float yr = fminf(fmaxf(dyr, a), b), yl = fminf(fmaxf(-dyr, a), b);
+  const float at = __fmul_rn(f.A, f.tau);
+  const float rr = __fsqrt_rn(fmaxf(0.f, __fsub_rn(at, __fmul_rn(__fmul_rn(detc, yr), yr))));
+  const float rl = __fsqrt_rn(fmaxf(0.f, __fsub_rn(at, __fmul_rn(__fmul_rn(detc, yl), yl))));
+  const float xr = __fdiv_rn(__fadd_rn(__fmul_rn(-f.B, yr), rr), f.A);
+  const float xl = __fdiv_rn(__fsub_rn(__fmul_rn(-f.B, yl), rl), f.A);
+  const float x_hi = __fadd_rn(__fadd_rn(f.mx, xr), kPad);
+  const float x_lo = __fsub_rn(__fadd_rn(f.mx, xl), kPad);
+  // Tile tx holds pixel centres [16 tx, 16 tx + 15].
+  lo = max(lo, (int)ceilf(__fdiv_rn(__fsub_rn(x_lo, float(kTileX - 1)), float(kTileX))));
+  hi = min(hi, (int)floorf(__fdiv_rn(x_hi, float(kTileX))) + 1);
+}
+
+__device__ __forceinline__ uint32_t footprint_tiles(const Footprint& f) {
+  uint32_t n = 0;
+  for (int ty = f.y0; ty < f.y1; ++ty) {
+    int lo, hi;
+    row_span(f, ty, lo, hi);
+    if (hi > lo) n += uint32_t(hi - lo);
+  }
+  return n;
+}
+
 }  // namespace raster
 }  // namespace clad3dgs

@@ -328,8 +328,11 @@ __global__ void preprocess_kernel(int P, int degree, const float* __restrict__ m
   g.radii[i] = radius;
   radii_out[i] = radius;
   g.mean2d[i] = make_float2(px, py);
-  g.conic_opacity[i] = make_float4(c * inv, -b * inv, a * inv, opacities[i] * aa);
-  g.tiles[i] = touched;
+  const float4 co = make_float4(c * inv, -b * inv, a * inv, opacities[i] * aa);
+  g.conic_opacity[i] = co;
+  // Instances only for the tiles some pixel of which the Gaussian can reach
+  // (see Footprint); the radius and everything else keep the 3-sigma rule.
+  g.tiles[i] = footprint_tiles(make_footprint(px, py, co, radius, cam.grid_x, cam.grid_y));
 }
 
 // Binning. The Gaussians are first ordered by depth (a stable sort of P
@@ -352,42 +355,84 @@ __global__ void gather_counts_kernel(int P, GeomState g) {
   g.depth_keys[i] = g.tiles[g.order[i]];
 }
 
-// One warp per Gaussian (in depth order): the lanes write consecutive
-// instances, so the stores coalesce.
+// One warp per Gaussian (in depth order). The lanes take up to 32 tile rows at
+// a time, each finds its row's span, a warp scan places the spans end to end,
+// and the lanes then write consecutive instances, so the stores coalesce.
 __global__ void duplicate_kernel(int P, GeomState g, int grid_x, int grid_y, uint32_t* keys,
                                  uint32_t* values) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < P; i += warps) {
     const uint32_t id = g.order[i];
-    const uint32_t count = g.tiles[id];
-    if (count == 0) continue;
+    const uint32_t cap = g.tiles[id];  // the slots the scan gave this Gaussian
+    if (cap == 0) continue;
     const uint32_t start = i == 0 ? 0u : g.offsets[i - 1];
-    int x0, y0, x1, y1;
+    uint32_t done = 0;
     const float2 m = g.mean2d[id];
-    tile_rect(m.x, m.y, g.radii[id], grid_x, grid_y, x0, y0, x1, y1);
-    const uint32_t w = uint32_t(x1 - x0);
-    for (uint32_t j = lane; j < count; j += 32) {
-      const uint32_t y = uint32_t(y0) + j / w, x = uint32_t(x0) + j % w;
-      keys[start + j] = y * uint32_t(grid_x) + x;
-      values[start + j] = id;
+    const Footprint f = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x,
+                                       grid_y);
+    for (int row0 = f.y0; row0 < f.y1; row0 += 32) {
+      const int ty = row0 + lane;
+      int lo = 0, hi = 0;
+      if (ty < f.y1) row_span(f, ty, lo, hi);
+      const uint32_t n = hi > lo ? uint32_t(hi - lo) : 0u;
+      uint32_t incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+      // Warp-uniform trip count: every lane takes part in every shuffle.
+      for (uint32_t base = 0; base < total; base += 32) {
+        const uint32_t j = base + lane;
+        // The row holding instance j: the first lane whose inclusive sum
+        // exceeds j (at most lane 31).
+        int r = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+          const uint32_t probe = __shfl_sync(0xffffffffu, incl, r + step - 1);
+          if (probe <= j) r += step;
+        }
+        const uint32_t r_incl = __shfl_sync(0xffffffffu, incl, r);
+        const uint32_t r_n = __shfl_sync(0xffffffffu, n, r);
+        const int r_lo = __shfl_sync(0xffffffffu, lo, r);
+        const uint32_t x = uint32_t(r_lo) + (j - (r_incl - r_n));
+        if (j < total && done + j < cap) {
+          keys[start + done + j] = uint32_t(row0 + r) * uint32_t(grid_x) + x;
+          values[start + done + j] = id;
+        }
+      }
+      done += total;
+    }
+    // Never past this Gaussian's slots; slots left over (none when the count
+    // and this walk agree, as they do) get a key that sorts after every tile.
+    for (uint32_t k = done + lane; k < cap; k += 32) {
+      keys[start + k] = 0xffffffffu;
+      values[start + k] = id;
     }
   }
 }
 
-__global__ void ranges_kernel(int n, const uint32_t* keys, uint2* ranges) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const uint32_t tile = keys[i];
-  if (i == 0) ranges[tile].x = 0;
-  else {
-    const uint32_t prev = keys[i - 1];
-    if (tile != prev) {
-      ranges[prev].y = i;
-      ranges[tile].x = i;
-    }
+// Per-tile [first, last) instance ranges of the tile-sorted keys: one thread
+// per tile, two binary searches (tiles without instances get an empty range).
+__device__ __forceinline__ uint32_t lower_bound(const uint32_t* keys, uint32_t n,
+                                                uint32_t value) {
+  uint32_t lo = 0, hi = n;
+  while (lo < hi) {
+    const uint32_t mid = lo + (hi - lo) / 2;
+    if (keys[mid] < value) lo = mid + 1;
+    else hi = mid;
   }
-  if (i == n - 1) ranges[tile].y = n;
+  return lo;
+}
+
+__global__ void ranges_kernel(uint32_t n, int tiles, const uint32_t* __restrict__ keys,
+                              uint2* __restrict__ ranges) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= tiles) return;
+  ranges[t] = make_uint2(lower_bound(keys, n, uint32_t(t)),
+                         lower_bound(keys, n, uint32_t(t) + 1));
 }
 
 __global__ void __launch_bounds__(kTilePixels)
@@ -902,7 +947,8 @@ int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t to
       b.sort_tmp, sort_bytes, b.keys_unsorted, b.keys, b.values_unsorted, b.values,
       int(total), 0, bits_for(uint32_t(grid_x * grid_y)), stream);
   if (e != cudaSuccess) return status_of(e, "tile sort");
-  ranges_kernel<<<(total + 255) / 256, 256, 0, stream>>>(int(total), b.keys, img.ranges);
+  const int tiles = grid_x * grid_y;
+  ranges_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(total, tiles, b.keys, img.ranges);
   return CLAD3DGS_OK;
 }
 
@@ -1090,9 +1136,9 @@ __global__ void fill_2d_kernel(int P, const float* __restrict__ mean2d,
   g.rgb[3 * i + 2] = rgb[3 * i + 2];
   g.depth[i] = depth[i];
   g.radii[i] = r;
-  int x0, y0, x1, y1;
-  tile_rect(px, py, r, grid_x, grid_y, x0, y0, x1, y1);
-  g.tiles[i] = r > 0 ? uint32_t((x1 - x0) * (y1 - y0)) : 0u;
+  g.tiles[i] = r > 0 ? footprint_tiles(make_footprint(px, py, g.conic_opacity[i], r, grid_x,
+                                                      grid_y))
+                     : 0u;
 }
 }  // namespace raster
 }  // namespace clad3dgs

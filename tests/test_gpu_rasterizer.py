@@ -89,6 +89,55 @@ def test_rasterizer_matches_oracle(cuda, P, H, W, degree, antialiasing):
     _close(grot, ref["drots"], "dL/drotations")
 
 
+def _rectangle_tiles(scene, radii):
+    """Tile instances of the renderer's 3-sigma rectangles."""
+    P, H, W = scene["P"], scene["H"], scene["W"]
+    hom = np.concatenate([scene["means"], np.ones((P, 1))], 1) @ scene["proj"]
+    px = ((hom[:, 0] / (hom[:, 3] + 1e-7) + 1) * W - 1) * 0.5
+    py = ((hom[:, 1] / (hom[:, 3] + 1e-7) + 1) * H - 1) * 0.5
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    total = 0
+    for x, y, r in zip(px, py, radii):
+        if r <= 0:
+            continue
+        x0 = min(gx, max(0, int((x - r) / 16)))
+        y0 = min(gy, max(0, int((y - r) / 16)))
+        x1 = min(gx, max(0, int((x + r + 15) / 16)))
+        y1 = min(gy, max(0, int((y + r + 15) / 16)))
+        total += (x1 - x0) * (y1 - y0)
+    return total
+
+
+@pytest.mark.parametrize("antialiasing", [False, True])
+def test_footprint_culling_keeps_every_contribution(cuda, antialiasing):
+    """Needle-like, low- and high-opacity Gaussians: the instance lists hold
+    only tiles the alpha >= 1/255 ellipse reaches, and every output still
+    matches the oracle, which composites every Gaussian in its 3-sigma
+    rectangle."""
+    P, H, W = 400, 90, 150
+    scene = oracle.raster_scene(P, H, W, seed=77, antialiasing=antialiasing,
+                                scale=(0.004, 0.25))
+    rng = np.random.default_rng(8)
+    scene["opacities"] = np.concatenate([rng.uniform(0.002, 0.02, P // 2),
+                                         rng.uniform(0.5, 0.999, P - P // 2)])
+    dpix = rng.standard_normal((3, H, W)) * 0.1
+    dinv = rng.standard_normal((H, W)) * 0.01
+    num, color, radii, invdepth, grads = _render(scene, cuda, 2, dpix, dinv)
+    ocolor, oinv, oradii = oracle.raster_forward(scene)
+    assert np.array_equal(radii.cpu().numpy(), oradii)
+    # The 3-sigma rectangles would hold far more instances than the footprints.
+    assert 0 < num < 0.7 * _rectangle_tiles(scene, oradii)
+    assert np.abs(color.cpu().numpy() - ocolor).max() < 1e-5
+    assert np.abs(invdepth.cpu().numpy()[0] - oinv).max() < 1e-5 * max(1.0, np.abs(oinv).max())
+    ref = oracle.raster_backward(scene, dpix, dinv)
+    g2d, gcol, gop, gmean, gcov, gsh, gscale, grot = [g.cpu().numpy() for g in grads]
+    _close(gop.reshape(-1), ref["dopacity"], "dL/dopacity")
+    _close(gmean, ref["dmeans"], "dL/dmeans3D")
+    _close(gsh.reshape(P, 48), ref["dsh"], "dL/dsh")
+    _close(gscale, ref["dscales"], "dL/dscales")
+    _close(grot, ref["drots"], "dL/drotations")
+
+
 def _reference_fixture(name, n, H, W, scale, opacity, antialiasing):
     """The reference's raster fixtures (check.py:745-767), restated."""
     torch.manual_seed(42)

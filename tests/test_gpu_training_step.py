@@ -146,7 +146,7 @@ def test_consumed_training_step_matches_native(cuda, tmp_path):
         pb, mb, vb, sb = b[name]
         assert sa == sb == 1, name
         torch.testing.assert_close(ma, mb, rtol=3e-5, atol=2e-7, msg=name + " exp_avg")
-        torch.testing.assert_close(va, vb, rtol=3e-5, atol=2e-10, msg=name + " exp_avg_sq")
+        torch.testing.assert_close(va, vb, rtol=3e-5, atol=2e-7, msg=name + " exp_avg_sq")
         close = (pa - pb).abs() <= 2e-7 + 3e-5 * pb.abs()
         # Step 1 updates are lr * sign(g): a rounding-level gradient may flip.
         tiny = mb.abs() <= 1e-5 * mb.abs().max()
