@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS,
                     help="Gaussians per GPU (smaller cases are for profiling only)")
+    ap.add_argument("--no-train-step", action="store_true",
+                    help="fused-step line without the attached training-step measurement")
     ap.add_argument("--train-gaussians", type=int, default=6_000_000,
                     help="train-step: replicated Gaussians (smaller cases are for profiling)")
     ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
@@ -88,7 +90,8 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"clocks_{os.getpid()}.csv"
+        self.path = (Path(os.environ.get("TMPDIR", "/tmp"))
+                     / f"clocks_{os.getpid()}_{id(self):x}.csv")
 
     def __enter__(self):
         try:
@@ -296,6 +299,7 @@ def native_arm(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+    clock_summary = clocks.summary()
     per_step = [events[k].elapsed_time(events[k + 1]) for k in range(args.steps)]
     elapsed_ms = events[0].elapsed_time(events[-1])
     fault = native.fault_status()
@@ -305,6 +309,11 @@ def native_arm(args):
     elapsed_ms = float(local_ms.item())
 
     e2e = e2e_measurement(args, device, consume) if rank == 0 and not args.no_e2e else None
+    del state
+    train = None
+    if not args.no_train_step:
+        torch.cuda.empty_cache()
+        train = measure_train_step(args, steps=20, warmup=3, with_e2e=False)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -332,11 +341,16 @@ def native_arm(args):
                      "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
                      "algorithmic_bytes_per_gaussian": BYTES_PER_GAUSSIAN,
                      "kernel_time_ms": mean_step_s * 1e3},
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
         "device_fault_word": fault,
     }
+    if train is not None:
+        line["train_step"] = {k: train[k] for k in ("metric", "value", "unit", "ms_per_step",
+                                                    "iters_per_s", "steps", "warmup",
+                                                    "exchange", "loss", "gpu_launches")}
+        line["train_step"]["config"] = train["config"]
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
@@ -484,8 +498,9 @@ def pixel_backward_arm(args):
     names = {2: "converged_warp_reduction", 1: "full_warp_only (reference helper)",
              0: "per_lane_atomics"}
     line = {
-        "metric": "rasterizer pixel backward, tile instances/s (1920x1080)",
-        "value": num / (ms / 1e3), "unit": "instances/s", "n_gpus": 1, "steps": args.steps,
+        "metric": "rasterizer pixel backward, Gaussians/s (1920x1080, one pass over every "
+                  "2D Gaussian)",
+        "value": n / (ms / 1e3), "unit": "Gaussians/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "data": "synthetic (seeded 2D Gaussians of the pixel-backward configuration)",
         "config": {"workload": f"pixel backward, 1920x1080, 16x16 tiles, {n:,} depth-sorted "
@@ -493,7 +508,9 @@ def pixel_backward_arm(args):
                                "T stop 1e-4, dL/dpixel N(0,1e-3)",
                    "tile_instances": num, "accumulation_mode": modes[0],
                    "ms_per_mode": {names[m]: results[m] for m in modes}},
-        "roofline": {"bound": "hbm (plus L2 atomics)", "achieved": algorithmic / (ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "limiter": "instruction issue (the ncu summary of this "
+                                                "kernel: issue-active ~85%, DRAM <1%)",
+                     "achieved": algorithmic / (ms / 1e3) / 1e9,
                      "peak": peak, "unit": "GB/s",
                      "frac": algorithmic / (ms / 1e3) / 1e9 / peak,
                      "algorithmic_bytes": algorithmic, "peak_kind": peak_kind},
@@ -538,6 +555,22 @@ def train_step_arm(args):
     device = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    line = measure_train_step(args, args.steps, args.warmup, not args.no_e2e)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_train_step(args, steps, warmup, with_e2e):
+    """Times the data-parallel training step on every rank (process group, if
+    any, already up); returns the JSON line on rank 0, None elsewhere."""
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
     import _native as native
     from data_parallel import DataParallelTrainer, ShardedAdam, orbit_camera
 
@@ -565,21 +598,21 @@ def train_step_arm(args):
     first_loss = None
     instances = 0
     with ClockSampler(local) as clocks:
-        for k in range(args.warmup):
+        for k in range(warmup):
             loss, instances = trainer.step(cam, target)
             if k == 0:
                 first_loss = float(loss.item())
         bracket()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         ev[0].record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             loss, instances = trainer.step(cam, target)
         ev[1].record(stream)
         bracket()
-    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / args.steps)
+    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps)
     last_loss = float(loss.item())
     # The exchange + update alone (gradients of a real backward in place).
-    exchange_steps = max(3, min(args.steps, 20))
+    exchange_steps = max(3, min(steps, 20))
     total = 0.0
     for _ in range(exchange_steps):
         trainer.backward(cam, target)
@@ -613,11 +646,11 @@ def train_step_arm(args):
     # End to end: each step's target comes from pinned host memory and the
     # loss goes back to the host.
     e2e = None
-    if not args.no_e2e:
+    if with_e2e:
         host_target = target.cpu().pin_memory()
         dev_target = torch.empty_like(target)
         loss_host = torch.empty(1, pin_memory=True)
-        e2e_steps = max(3, min(args.steps, 20))
+        e2e_steps = max(3, min(steps, 20))
         bracket()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -634,11 +667,8 @@ def train_step_arm(args):
     fault = native.fault_status()
     padded, share = adam.padded, adam.share
     trainer.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     if rank != 0:
-        return
+        return None
     # Exchange roofline: bytes that must cross NVLink per GPU and direction
     # (the other ranks' gradients of this share in, this share's parameters out
     # to the other ranks), against the measured 770 GB/s peer copy; with one GPU
@@ -661,7 +691,7 @@ def train_step_arm(args):
     line = {
         "metric": "data-parallel training step, views/s (one 1920x1080 view per GPU)",
         "value": world / (step_ms / 1e3), "unit": "views/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "steps": steps, "warmup": warmup, "ms_per_step": step_ms,
         "iters_per_s": 1e3 / step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32+f64",
         "data": "synthetic (seeded; 6M Gaussians of the 8-view configuration, random targets)",
@@ -676,10 +706,10 @@ def train_step_arm(args):
                      "roofline": exchange_roof},
         "clocks": clocks.summary(),
         "e2e": e2e,
-        "gpu_launches": TRAIN_LAUNCHES_PER_STEP * args.steps,
+        "gpu_launches": TRAIN_LAUNCHES_PER_STEP * steps,
         "device_fault_word": fault,
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def main():
