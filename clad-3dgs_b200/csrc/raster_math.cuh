@@ -150,62 +150,67 @@ __device__ __forceinline__ void tile_rect(float px, float py, int radius, int gr
 // renderer uses, so the kept set always contains every contributing tile.
 struct Footprint {
   float mx, my;     // mean, pixels
-  float A, B, C;    // conic
-  float tau;        // culling level (with margin); < 0: no pixel can contribute
+  float B, invA;    // conic off-diagonal, 1 / A
+  float at, detc;   // A tau, A C - B^2
+  float ymax, dyr;  // ellipse half-height; dy of its rightmost point
+  bool any;         // false: no pixel can contribute
   bool ellipse;     // false: conic not positive definite, keep whole rows
   int x0, y0, x1, y1;  // tile rectangle of the 3-sigma radius
 };
 
+// Row-independent terms, once per Gaussian. Every operation is an explicitly
+// rounded intrinsic, so the count taken in one kernel and the instances written
+// in another agree bit for bit.
 __device__ __forceinline__ Footprint make_footprint(float px, float py, float4 co, int radius,
                                                     int grid_x, int grid_y) {
   Footprint f;
   f.mx = px;
   f.my = py;
-  f.A = co.x;
+  const float A = co.x, C = co.z;
   f.B = co.y;
-  f.C = co.z;
   const float o255 = __fmul_rn(255.f, co.w);
-  f.tau = o255 > 0.f ? __fmul_rn(2.f, logf(o255)) : -1.f;
-  if (f.tau >= 0.f) f.tau = __fadd_rn(__fmul_rn(f.tau, 1.001f), 0.01f);
-  const float detc = __fsub_rn(__fmul_rn(f.A, f.C), __fmul_rn(f.B, f.B));
-  f.ellipse = f.A > 0.f && f.C > 0.f && detc > 0.f;
+  float tau = o255 > 0.f ? __fmul_rn(2.f, logf(o255)) : -1.f;
+  f.any = tau >= 0.f;
+  if (f.any) tau = __fadd_rn(__fmul_rn(tau, 1.001f), 0.01f);
+  f.detc = __fsub_rn(__fmul_rn(A, C), __fmul_rn(f.B, f.B));
+  f.ellipse = A > 0.f && C > 0.f && f.detc > 0.f;
+  f.invA = f.ellipse ? __frcp_rn(A) : 0.f;
+  f.at = __fmul_rn(A, tau);
+  f.ymax = f.ellipse && f.any ? __fsqrt_rn(__fdiv_rn(f.at, f.detc)) : 0.f;
+  // Extreme points of the ellipse in x sit at dy = -/+ B sqrt(tau / (C detc)).
+  f.dyr = f.ellipse && f.any
+              ? __fmul_rn(-f.B, __fsqrt_rn(__fdiv_rn(tau, __fmul_rn(C, f.detc))))
+              : 0.f;
   tile_rect(px, py, radius, grid_x, grid_y, f.x0, f.y0, f.x1, f.y1);
   return f;
 }
 
 // Tiles [lo, hi) of tile row ty that the footprint reaches (lo >= hi: none).
-// Every operation is an explicitly rounded intrinsic, so the count taken in
-// one kernel and the instances written in another agree bit for bit.
 __device__ __forceinline__ void row_span(const Footprint& f, int ty, int& lo, int& hi) {
   lo = f.x0;
   hi = f.x1;
   if (!f.ellipse) return;
-  if (f.tau < 0.f) {
+  if (!f.any) {
     hi = lo;
     return;
   }
   constexpr float kPad = 0.05f;  // pixels
-  const float detc = __fsub_rn(__fmul_rn(f.A, f.C), __fmul_rn(f.B, f.B));
-  const float ymax = __fsqrt_rn(__fdiv_rn(__fmul_rn(f.tau, f.A), detc));
-  const float a = fmaxf(__fsub_rn(float(ty * kTileY) - kPad, f.my), -ymax);
-  const float b = fminf(__fsub_rn(float(ty * kTileY + kTileY - 1) + kPad, f.my), ymax);
+  const float a = fmaxf(__fsub_rn(float(ty * kTileY) - kPad, f.my), -f.ymax);
+  const float b = fminf(__fsub_rn(float(ty * kTileY + kTileY - 1) + kPad, f.my), f.ymax);
   if (a > b) {
     hi = lo;
     return;
   }
-  // Extreme points of the ellipse in x sit at dy = -/+ B sqrt(tau / (C detc)).
-  const float dyr = __fmul_rn(-f.B, __fsqrt_rn(__fdiv_rn(f.tau, __fmul_rn(f.C, detc))));
-  const float yr = fminf(fmaxf(dyr, a), b), yl = fminf(fmaxf(-dyr, a), b);
-  const float at = __fmul_rn(f.A, f.tau);
-  const float rr = __fsqrt_rn(fmaxf(0.f, __fsub_rn(at, __fmul_rn(__fmul_rn(detc, yr), yr))));
-  const float rl = __fsqrt_rn(fmaxf(0.f, __fsub_rn(at, __fmul_rn(__fmul_rn(detc, yl), yl))));
-  const float xr = __fdiv_rn(__fadd_rn(__fmul_rn(-f.B, yr), rr), f.A);
-  const float xl = __fdiv_rn(__fsub_rn(__fmul_rn(-f.B, yl), rl), f.A);
+  const float yr = fminf(fmaxf(f.dyr, a), b), yl = fminf(fmaxf(-f.dyr, a), b);
+  const float rr = __fsqrt_rn(fmaxf(0.f, __fsub_rn(f.at, __fmul_rn(__fmul_rn(f.detc, yr), yr))));
+  const float rl = __fsqrt_rn(fmaxf(0.f, __fsub_rn(f.at, __fmul_rn(__fmul_rn(f.detc, yl), yl))));
+  const float xr = __fmul_rn(__fadd_rn(__fmul_rn(-f.B, yr), rr), f.invA);
+  const float xl = __fmul_rn(__fsub_rn(__fmul_rn(-f.B, yl), rl), f.invA);
   const float x_hi = __fadd_rn(__fadd_rn(f.mx, xr), kPad);
   const float x_lo = __fsub_rn(__fadd_rn(f.mx, xl), kPad);
-  // Tile tx holds pixel centres [16 tx, 16 tx + 15].
-  lo = max(lo, (int)ceilf(__fdiv_rn(__fsub_rn(x_lo, float(kTileX - 1)), float(kTileX))));
-  hi = min(hi, (int)floorf(__fdiv_rn(x_hi, float(kTileX))) + 1);
+  // Tile tx holds pixel centres [16 tx, 16 tx + 15]; x / 16 is exact as x * 0.0625.
+  lo = max(lo, (int)ceilf(__fmul_rn(__fsub_rn(x_lo, float(kTileX - 1)), 0.0625f)));
+  hi = min(hi, (int)floorf(__fmul_rn(x_hi, 0.0625f)) + 1);
 }
 
 __device__ __forceinline__ uint32_t footprint_tiles(const Footprint& f) {

@@ -203,6 +203,12 @@ struct ShSource {
   }
 };
 
+// Coefficients of one Gaussian staged in a shared-memory row ([16][3]).
+struct RowSource {
+  float* row;
+  __device__ __forceinline__ const float* term(int, int j) const { return row + 3 * j; }
+};
+
 template <int J>
 __device__ __forceinline__ void colour_terms(const Direction& d, const ShSource& sh, int i,
                                              int nterms, float rgb[3]) {
@@ -221,8 +227,8 @@ __device__ __forceinline__ void colour_terms(const Direction& d, const ShSource&
 
 // SH backward for one Gaussian: d colour / d coefficients (optional) and the
 // adjoint of the view direction.
-template <int J>
-__device__ __forceinline__ void colour_adjoint_terms(const Direction& d, const ShSource& sh,
+template <int J, class Source>
+__device__ __forceinline__ void colour_adjoint_terms(const Direction& d, const Source& sh,
                                                      int i, int nterms, const float g[3],
                                                      float* dsh, float dd[3]) {
   if constexpr (J < 16) {
@@ -355,61 +361,99 @@ __global__ void gather_counts_kernel(int P, GeomState g) {
   g.depth_keys[i] = g.tiles[g.order[i]];
 }
 
-// One warp per Gaussian (in depth order). The lanes take up to 32 tile rows at
-// a time, each finds its row's span, a warp scan places the spans end to end,
-// and the lanes then write consecutive instances, so the stores coalesce.
+// Tile instances of one Gaussian (footprint f, slots [start, start + cap)),
+// written by the whole warp: the lanes take up to 32 tile rows at a time, each
+// finds its row's span, a warp scan places the spans end to end, and the lanes
+// then write consecutive instances, so the stores coalesce. Warp-uniform
+// control flow throughout (every lane takes part in every shuffle).
+__device__ __forceinline__ void emit_instances(const Footprint& f, uint32_t id, uint32_t cap,
+                                               uint32_t start, int grid_x, int lane,
+                                               uint32_t* keys, uint32_t* values) {
+  uint32_t done = 0;
+  for (int row0 = f.y0; row0 < f.y1; row0 += 32) {
+    const int ty = row0 + lane;
+    int lo = 0, hi = 0;
+    if (ty < f.y1) row_span(f, ty, lo, hi);
+    const uint32_t n = hi > lo ? uint32_t(hi - lo) : 0u;
+    uint32_t incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    for (uint32_t base = 0; base < total; base += 32) {
+      const uint32_t j = base + lane;
+      // The row holding instance j: the first lane whose inclusive sum exceeds
+      // j (at most lane 31).
+      int r = 0;
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1) {
+        const uint32_t probe = __shfl_sync(0xffffffffu, incl, r + step - 1);
+        if (probe <= j) r += step;
+      }
+      const uint32_t r_incl = __shfl_sync(0xffffffffu, incl, r);
+      const uint32_t r_n = __shfl_sync(0xffffffffu, n, r);
+      const int r_lo = __shfl_sync(0xffffffffu, lo, r);
+      const uint32_t x = uint32_t(r_lo) + (j - (r_incl - r_n));
+      if (j < total && done + j < cap) {
+        keys[start + done + j] = uint32_t(row0 + r) * uint32_t(grid_x) + x;
+        values[start + done + j] = id;
+      }
+    }
+    done += total;
+  }
+  // Never past this Gaussian's slots; slots left over (none when the count
+  // and this walk agree, as they do) get a key that sorts after every tile.
+  for (uint32_t k = done + lane; k < cap; k += 32) {
+    keys[start + k] = 0xffffffffu;
+    values[start + k] = id;
+  }
+}
+
+// One warp per 32 consecutive Gaussians of the depth order. Each lane gathers
+// one Gaussian's header (id, slot count, first slot, footprint), so the
+// dependent loads of 32 Gaussians overlap; the warp then emits them one at a
+// time from registers.
 __global__ void duplicate_kernel(int P, GeomState g, int grid_x, int grid_y, uint32_t* keys,
                                  uint32_t* values) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < P; i += warps) {
-    const uint32_t id = g.order[i];
-    const uint32_t cap = g.tiles[id];  // the slots the scan gave this Gaussian
-    if (cap == 0) continue;
-    const uint32_t start = i == 0 ? 0u : g.offsets[i - 1];
-    uint32_t done = 0;
-    const float2 m = g.mean2d[id];
-    const Footprint f = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x,
-                                       grid_y);
-    for (int row0 = f.y0; row0 < f.y1; row0 += 32) {
-      const int ty = row0 + lane;
-      int lo = 0, hi = 0;
-      if (ty < f.y1) row_span(f, ty, lo, hi);
-      const uint32_t n = hi > lo ? uint32_t(hi - lo) : 0u;
-      uint32_t incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
+  for (int base = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; base < P;
+       base += warps * 32) {
+    const int i = base + lane;
+    uint32_t id = 0, cap = 0, start = 0;
+    Footprint mine{};
+    if (i < P) {
+      id = g.order[i];
+      cap = g.tiles[id];
+      if (cap) {
+        start = i == 0 ? 0u : g.offsets[i - 1];
+        const float2 m = g.mean2d[id];
+        mine = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x, grid_y);
       }
-      const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-      // Warp-uniform trip count: every lane takes part in every shuffle.
-      for (uint32_t base = 0; base < total; base += 32) {
-        const uint32_t j = base + lane;
-        // The row holding instance j: the first lane whose inclusive sum
-        // exceeds j (at most lane 31).
-        int r = 0;
-#pragma unroll
-        for (int step = 16; step > 0; step >>= 1) {
-          const uint32_t probe = __shfl_sync(0xffffffffu, incl, r + step - 1);
-          if (probe <= j) r += step;
-        }
-        const uint32_t r_incl = __shfl_sync(0xffffffffu, incl, r);
-        const uint32_t r_n = __shfl_sync(0xffffffffu, n, r);
-        const int r_lo = __shfl_sync(0xffffffffu, lo, r);
-        const uint32_t x = uint32_t(r_lo) + (j - (r_incl - r_n));
-        if (j < total && done + j < cap) {
-          keys[start + done + j] = uint32_t(row0 + r) * uint32_t(grid_x) + x;
-          values[start + done + j] = id;
-        }
-      }
-      done += total;
     }
-    // Never past this Gaussian's slots; slots left over (none when the count
-    // and this walk agree, as they do) get a key that sorts after every tile.
-    for (uint32_t k = done + lane; k < cap; k += 32) {
-      keys[start + k] = 0xffffffffu;
-      values[start + k] = id;
+    uint32_t pending = __ballot_sync(0xffffffffu, cap != 0);
+    while (pending) {
+      const int src = __ffs(pending) - 1;
+      pending &= pending - 1;
+      Footprint f;
+      f.mx = __shfl_sync(0xffffffffu, mine.mx, src);
+      f.my = __shfl_sync(0xffffffffu, mine.my, src);
+      f.B = __shfl_sync(0xffffffffu, mine.B, src);
+      f.invA = __shfl_sync(0xffffffffu, mine.invA, src);
+      f.at = __shfl_sync(0xffffffffu, mine.at, src);
+      f.detc = __shfl_sync(0xffffffffu, mine.detc, src);
+      f.ymax = __shfl_sync(0xffffffffu, mine.ymax, src);
+      f.dyr = __shfl_sync(0xffffffffu, mine.dyr, src);
+      f.any = __shfl_sync(0xffffffffu, int(mine.any), src) != 0;
+      f.ellipse = __shfl_sync(0xffffffffu, int(mine.ellipse), src) != 0;
+      f.x0 = __shfl_sync(0xffffffffu, mine.x0, src);
+      f.y0 = __shfl_sync(0xffffffffu, mine.y0, src);
+      f.x1 = __shfl_sync(0xffffffffu, mine.x1, src);
+      f.y1 = __shfl_sync(0xffffffffu, mine.y1, src);
+      emit_instances(f, __shfl_sync(0xffffffffu, id, src), __shfl_sync(0xffffffffu, cap, src),
+                     __shfl_sync(0xffffffffu, start, src), grid_x, lane, keys, values);
     }
   }
 }
@@ -889,6 +933,62 @@ __global__ void preprocess_backward_kernel(
   }
 }
 
+// SH colour -> coefficients and view direction, 32 Gaussians per warp: the
+// warp stages its block of coefficients in shared memory with coalesced loads,
+// each lane works in its own row (reading coefficient j before overwriting it
+// with dL/dsh_j), and the warp stores the dL/dsh block coalesced. The direction
+// adjoint is added into dmeans after the geometry backward's share (dmeans is
+// zeroed by the caller, so the sum rounds as the single sum would).
+constexpr int kShRow = 49;  // 48 floats + 1: rows start in distinct banks
+constexpr int kShWarps = 4;
+
+__global__ void __launch_bounds__(32 * kShWarps)
+    sh_backward_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
+                       const float* __restrict__ campos, GeomState g,
+                       const int* __restrict__ radii, const float* __restrict__ dcolor,
+                       float* __restrict__ dsh, float* __restrict__ dmeans) {
+  __shared__ float rows[kShWarps][32 * kShRow];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* blk = rows[warp];
+  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
+  if (i0 >= P) return;  // whole warp
+  const int n = min(32, P - i0);
+  if (sh.packed) {
+    const float* src = sh.packed + 48 * size_t(i0);
+    for (int e = lane; e < n * 48; e += 32) blk[(e / 48) * kShRow + e % 48] = src[e];
+  } else {
+    const float* dc = sh.dc + 3 * size_t(i0);
+    const float* rest = sh.rest + 45 * size_t(i0);
+    for (int e = lane; e < n * 3; e += 32) blk[(e / 3) * kShRow + e % 3] = dc[e];
+    for (int e = lane; e < n * 45; e += 32) blk[(e / 45) * kShRow + 3 + e % 45] = rest[e];
+  }
+  __syncwarp();
+  float* row = blk + lane * kShRow;
+  const int i = i0 + lane;
+  if (lane < n) {
+    if (radii[i] > 0) {
+      const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
+                                         campos[0], campos[1], campos[2]);
+      float gcol[3];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) gcol[k] = g.clamped[3 * i + k] ? 0.f : dcolor[3 * i + k];
+      float dd[3] = {0.f, 0.f, 0.f};
+      colour_adjoint_terms<0>(d, RowSource{row}, i, (degree + 1) * (degree + 1), gcol, row, dd);
+      float om[3];
+      direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dmeans[3 * i + k] += om[k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 48; ++k) row[k] = 0.f;
+    }
+  }
+  __syncwarp();
+  if (!dsh) return;  // direction adjoint only
+  float* dst = dsh + 48 * size_t(i0);
+  for (int e = lane; e < n * 48; e += 32) dst[e] = blk[(e / 48) * kShRow + e % 48];
+}
+
 }  // namespace raster
 }  // namespace clad3dgs
 
@@ -937,8 +1037,9 @@ int order_and_count(int P, GeomState& g, uint32_t& total, cudaStream_t stream) {
 int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t total,
                   const BinningState& b, const ImageState& img, cudaStream_t stream) {
   const int warps_per_block = 8;
-  const int blocks = int(std::min<long long>((P + warps_per_block - 1) / warps_per_block,
-                                             148LL * 64));
+  const long long warps_needed = (P + 31) / 32;  // one warp per 32 Gaussians
+  const int blocks = int(std::min<long long>(
+      (warps_needed + warps_per_block - 1) / warps_per_block, 148LL * 64));
   duplicate_kernel<<<blocks, 32 * warps_per_block, 0, stream>>>(P, g, grid_x, grid_y,
                                                                b.keys_unsorted,
                                                                b.values_unsorted);
@@ -1107,7 +1208,12 @@ extern "C" int clad3dgs_raster_backward(
   const bool from_sh = colors_precomp == nullptr && !consume_sh;
   preprocess_backward_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
       P, degree, means, scales, scale_modifier, rotations, opacities, cov3d_precomp, sh, cam,
-      antialiasing != 0, radii, g, from_sh, o);
+      antialiasing != 0, radii, g, false, o);
+  if (from_sh) {
+    const int warps = (P + 31) / 32;
+    sh_backward_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
+        P, degree, means, sh, campos, g, radii, dcolor, dsh, dmeans);
+  }
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) return status_of(e, "geometry backward");
   if (consume_sh && colors_precomp == nullptr)

@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+int blocks_for(int64_t work);
+
 struct ShardParams {
   int64_t begin, end, grad_origin;
   int ranks, local;
@@ -106,7 +108,8 @@ struct ShardParams {
   double inv_bias2;
 };
 
-__global__ void __launch_bounds__(kThreads)
+template <int R>
+__global__ void __launch_bounds__(kThreads, R <= 2 ? 4 : 3)
     shard_update_kernel(const __grid_constant__ ShardParams a) {
   const int64_t n = a.end - a.begin;  // a multiple of 4
   // Chunk boundaries of the five groups (float4 chunks of the owned spans).
@@ -133,14 +136,13 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t melem = 4 * local;                    // index into moments
     // All sources first (independent loads, many in flight over NVLink), then
     // the sum in rank order.
-    float4 t[kMaxRanks];
+    float4 t[R];
 #pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q)
-      if (q < a.ranks) t[q] = __ldcs(reinterpret_cast<const float4*>(a.grads[q][g] + gelem));
+    for (int q = 0; q < R; ++q)
+      t[q] = __ldcs(reinterpret_cast<const float4*>(a.grads[q][g] + gelem));
     float4 grad = t[0];
 #pragma unroll
-    for (int q = 1; q < kMaxRanks; ++q)
-      if (q < a.ranks) grad = add4(grad, t[q]);
+    for (int q = 1; q < R; ++q) grad = add4(grad, t[q]);
     float4 p = *reinterpret_cast<const float4*>(a.params[a.local][g] + elem);
     float4 m = *reinterpret_cast<const float4*>(a.first[g] + melem);
     float4 v = *reinterpret_cast<const float4*>(a.second[g] + melem);
@@ -176,11 +178,16 @@ __global__ void __launch_bounds__(kThreads)
     *reinterpret_cast<float4*>(a.second[g] + melem) = make_float4(vv[0], vv[1], vv[2], vv[3]);
     const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
 #pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q)
-      if (q < a.ranks) __stcs(reinterpret_cast<float4*>(a.params[q][g] + elem), out);
+    for (int q = 0; q < R; ++q) __stcs(reinterpret_cast<float4*>(a.params[q][g] + elem), out);
   }
   // Make the peer stores visible system-wide before the kernel retires.
-  if (a.ranks > 1) __threadfence_system();
+  if (R > 1) __threadfence_system();
+}
+
+template <int R>
+cudaError_t launch_shard_update(const ShardParams& p, int64_t chunks, cudaStream_t stream) {
+  shard_update_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 int blocks_for(int64_t work) {
@@ -280,8 +287,17 @@ extern "C" int clad3dgs_shard_update(const clad3dgs_shard_update_args* args,
   for (int r = 0; r < kGroups + 1; ++r) p.step[r] = float(x.rates[r] / double(x.bias1));
   p.inv_bias2 = 1.0 / double(x.bias2_sqrt);
   const int64_t chunks = (x.end - x.begin) * 59 / 4;
-  shard_update_kernel<<<blocks_for(chunks), kThreads, 0, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  switch (x.ranks) {
+    case 1: e = launch_shard_update<1>(p, chunks, stream); break;
+    case 2: e = launch_shard_update<2>(p, chunks, stream); break;
+    case 3: e = launch_shard_update<3>(p, chunks, stream); break;
+    case 4: e = launch_shard_update<4>(p, chunks, stream); break;
+    case 5: e = launch_shard_update<5>(p, chunks, stream); break;
+    case 6: e = launch_shard_update<6>(p, chunks, stream); break;
+    case 7: e = launch_shard_update<7>(p, chunks, stream); break;
+    default: e = launch_shard_update<8>(p, chunks, stream); break;
+  }
   return e == cudaSuccess ? CLAD3DGS_OK
                           : fail(CLAD3DGS_CUDA_ERROR, std::string("shard update: ") +
                                                           cudaGetErrorString(e));
