@@ -349,7 +349,8 @@ def native_arm(args):
     if train is not None:
         line["train_step"] = {k: train[k] for k in ("metric", "value", "unit", "ms_per_step",
                                                     "iters_per_s", "steps", "warmup",
-                                                    "exchange", "loss", "gpu_launches")}
+                                                    "exchange", "loss", "per_rank",
+                                                    "gpu_launches")}
         line["train_step"]["config"] = train["config"]
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
@@ -583,11 +584,19 @@ def measure_train_step(args, steps, warmup, with_e2e):
     target = torch.rand(3, TRAIN_H, TRAIN_W, generator=gen, device=device)
     stream = torch.cuda.current_stream()
 
-    def max_over_ranks(x):
+    per_rank = {}
+
+    def max_over_ranks(x, name=None):
         t = torch.tensor([x], device=device, dtype=torch.float64)
         if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+            every = torch.empty(world, device=device, dtype=torch.float64)
+            dist.all_gather_into_tensor(every, t)
+            values = every.tolist()
+        else:
+            values = [x]
+        if name:
+            per_rank[name] = [round(v, 4) for v in values]
+        return max(values)
 
     def bracket():
         torch.cuda.synchronize()
@@ -609,7 +618,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
             loss, instances = trainer.step(cam, target)
         ev[1].record(stream)
         bracket()
-    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps)
+    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps, "step_ms")
     last_loss = float(loss.item())
     # The exchange + update alone (gradients of a real backward in place).
     exchange_steps = max(3, min(steps, 20))
@@ -623,7 +632,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
         e1.record(stream)
         torch.cuda.synchronize()
         total += e0.elapsed_time(e1)
-    exchange_ms = max_over_ranks(total / exchange_steps)
+    exchange_ms = max_over_ranks(total / exchange_steps, "exchange_ms")
     adam = trainer.adam
     baseline_ms = None
     if world > 1 and adam.exchange == "peer":
@@ -664,6 +673,13 @@ def measure_train_step(args, steps, warmup, with_e2e):
         e2e = {"value": world / (e2e_ms / 1e3), "unit": "views/s",
                "h2d_bytes_per_step": host_target.numel() * 4, "d2h_bytes_per_step": 4,
                "ms_per_step": e2e_ms}
+    inst = torch.tensor([float(instances)], device=device, dtype=torch.float64)
+    if world > 1:
+        every = torch.empty(world, device=device, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, inst)
+        instances_all = [int(v) for v in every.tolist()]
+    else:
+        instances_all = [int(instances)]
     fault = native.fault_status()
     padded, share = adam.padded, adam.share
     trainer.close()
@@ -702,6 +718,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
                    "share_per_gpu": share, "tile_instances_rank0": instances,
                    "l2": "parameters 1.4 GB per replica exceed the 126 MB L2"},
         "loss": {"first": first_loss, "last": last_loss},
+        "per_rank": dict(per_rank, tile_instances=instances_all),
         "exchange": {"ms": exchange_ms, "nccl_baseline_ms": baseline_ms,
                      "roofline": exchange_roof},
         "clocks": clocks.summary(),
