@@ -83,6 +83,7 @@ constexpr int kMaxCtasPerSm = CLAD3DGS_CTAS_PER_SM;  // cap on persistent CTAs p
 constexpr int kConsumers = 512;                  // 16 warps: one per SH term
 constexpr int kPersistThreads = kConsumers + 32;  // + 1 producer warp
 constexpr int kMaxStages = 8;
+constexpr int kUpdateFirst = 64;  // first consumer thread of phase B
 static_assert(kTile == 32, "one lane per Gaussian of a tile");
 // Dynamic shared memory for the stages of one CTA when `ctas` CTAs share an
 // SM's 226 KB: less each CTA's static scratch and a reserve.
@@ -454,9 +455,9 @@ __device__ __forceinline__ void update_group(const StepParams& p,
   }
 }
 
-// Each consumer updates four consecutive elements with 128-bit shared-memory
-// accesses; every group's region is a multiple of four elements long, so the
-// four share one group (one step size).
+// Each consumer of warps 2-15 updates four consecutive elements with 128-bit
+// shared-memory accesses; every group's region is a multiple of four elements
+// long, so the four share one group (one step size).
 template <class C>
 __device__ __forceinline__ void phase_update(const StepParams& p,
                                              const Stage<C>& st,
@@ -470,7 +471,11 @@ __device__ __forceinline__ void phase_update(const StepParams& p,
   float4* M = kMoments ? reinterpret_cast<float4*>(st.template f<R::kFirstArr>()) : nullptr;
   float4* V = kMoments ? reinterpret_cast<float4*>(st.template f<R::kSecondArr>()) : nullptr;
   const float4* G = reinterpret_cast<const float4*>(sc.grad);
-  for (int q = ct; q < R::kTotal / 4; q += kConsumers) {
+  // Warps 2-15 (448 threads: one float4 each for a full 56-parameter tile);
+  // warp 0 is busy with the position adjoint meanwhile, and the tile's closing
+  // barrier waits for the slowest warp.
+  if (ct < kUpdateFirst) return;
+  for (int q = ct - kUpdateFirst; q < R::kTotal / 4; q += kConsumers - kUpdateFirst) {
     const int e = 4 * q;
     float4 pv = P[q], gv = G[q];
     float4 mv = make_float4(0.f, 0.f, 0.f, 0.f), vv = mv;
