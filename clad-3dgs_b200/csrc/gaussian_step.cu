@@ -89,7 +89,7 @@ static_assert(kTile == 32, "one lane per Gaussian of a tile");
 // SM's 226 KB: less each CTA's static scratch and a reserve.
 constexpr uint32_t stage_budget(int ctas) {
   return (226u * 1024u) / ctas -
-         (16u * kTile * 3u + 56u * kTile + 16u * kTile) * 4u - 1536u;
+         (16u * kTile * 3u + 48u * kTile + 2u * 14u * kTile) * 4u - 1536u;
 }
 constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
@@ -202,14 +202,15 @@ struct Stage {
 // (dc, rest, rotation, scaling, opacity share one index with the moments and
 // the gradient tile) with one compact Adam update per element.
 
-// Per-CTA scratch shared by the consumers (one copy, reused every tile).
+// Per-CTA scratch shared by the consumers. The per-Gaussian view data has two
+// copies: warp 1 fills the next tile's while the current tile is updated.
 struct __align__(16) Scratch {
   float partial[16][kTile][3];  // direction adjoint of every term
-  __align__(16) float grad[kTile * 56];  // gradients, laid out like the parameters
-  float dir[10][kTile];         // view direction of every Gaussian (x, y, z,
+  __align__(16) float grad[kTile * 48];  // SH gradients, laid out like the parameters
+  float dir[2][10][kTile];      // view direction of every Gaussian (x, y, z,
                                 // r, xx, yy, zz, xy, yz, xz), one row per field
-  float seed[kTile][3];         // clamped-masked colour seed
-  int visible[kTile];
+  float seed[2][kTile][3];      // clamped-masked colour seed
+  int visible[2][kTile];
   int abort;                    // set by a consumer whose wait timed out
 };
 
@@ -256,19 +257,20 @@ __device__ __forceinline__ const float* term_coefficients(const Stage<C>& st,
   }
 }
 
-__device__ __forceinline__ void store_direction(Scratch& sc, int gl,
+__device__ __forceinline__ void store_direction(Scratch& sc, int buf, int gl,
                                                 const Direction& d) {
   const float f[10] = {d.x, d.y, d.z, d.r, d.xx, d.yy, d.zz, d.xy, d.yz, d.xz};
 #pragma unroll
-  for (int k = 0; k < 10; ++k) sc.dir[k][gl] = f[k];
+  for (int k = 0; k < 10; ++k) sc.dir[buf][k][gl] = f[k];
 }
 
-__device__ __forceinline__ Direction load_direction(const Scratch& sc, int gl) {
+__device__ __forceinline__ Direction load_direction(const Scratch& sc, int buf, int gl) {
+  const auto& r = sc.dir[buf];
   Direction d;
-  d.x = sc.dir[0][gl]; d.y = sc.dir[1][gl]; d.z = sc.dir[2][gl];
-  d.r = sc.dir[3][gl]; d.xx = sc.dir[4][gl]; d.yy = sc.dir[5][gl];
-  d.zz = sc.dir[6][gl]; d.xy = sc.dir[7][gl]; d.yz = sc.dir[8][gl];
-  d.xz = sc.dir[9][gl];
+  d.x = r[0][gl]; d.y = r[1][gl]; d.z = r[2][gl];
+  d.r = r[3][gl]; d.xx = r[4][gl]; d.yy = r[5][gl];
+  d.zz = r[6][gl]; d.xy = r[7][gl]; d.yz = r[8][gl];
+  d.xz = r[9][gl];
   return d;
 }
 
@@ -276,12 +278,12 @@ __device__ __forceinline__ Direction load_direction(const Scratch& sc, int gl) {
 // Gaussian or above the degree) get a zero gradient, which still advances Adam.
 template <class C, int J>
 __device__ __forceinline__ void term_gradient(const Stage<C>& st, Scratch& sc,
-                                              int gl, int nterms) {
+                                              int buf, int gl, int nterms) {
   float* g = sc.grad + grad_offset<C, J>(gl);
   float* t = sc.partial[J][gl];
-  if (sc.visible[gl] && J < nterms) {
-    const Direction d = load_direction(sc, gl);
-    const float* s = sc.seed[gl];
+  if (sc.visible[buf][gl] && J < nterms) {
+    const Direction d = load_direction(sc, buf, gl);
+    const float* s = sc.seed[buf][gl];
     float b, gx, gy, gz;
     sh_basis<J>(d, b, gx, gy, gz);
     const float* c = term_coefficients<C, J>(st, gl);
@@ -298,81 +300,83 @@ __device__ __forceinline__ void term_gradient(const Stage<C>& st, Scratch& sc,
   }
 }
 
-// Phase A0. Returns nothing; `ready` is false for a consumer whose stage wait
-// timed out (it then only joins the barriers).
+// View data of a tile (one warp, lane = Gaussian): visibility, direction and
+// clamp-masked colour seed into copy `buf` of the scratch.
 template <class C>
-__device__ __forceinline__ void phase_directions(const Stage<C>& st, Scratch& sc,
-                                                 int cnt, int ct,
-                                                 const float cam[3]) {
-  using R = Region<C>;
-  const int cw = ct >> 5, gl = ct & 31;
-  if (gl >= cnt) return;
+__device__ __forceinline__ void phase_directions(const Stage<C>& st, Scratch& sc, int cnt,
+                                                 int gl, const float cam[3], int buf) {
   if constexpr (C::kSh != SH_NONE) {
-    if (cw == 0) {
-      const bool visible = st.template i<RADII>()[gl] > 0;
-      sc.visible[gl] = visible;
-      if (visible) {
-        const float* m = st.template f<MEANS>() + 3 * gl;
-        store_direction(sc, gl, make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]));
-        const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
-        const float* sd = st.template f<SEED>() + 3 * gl;
+    if (gl >= cnt) return;
+    const bool visible = st.template i<RADII>()[gl] > 0;
+    sc.visible[buf][gl] = visible;
+    if (visible) {
+      const float* m = st.template f<MEANS>() + 3 * gl;
+      store_direction(sc, buf, gl, make_direction(m[0], m[1], m[2], cam[0], cam[1], cam[2]));
+      const unsigned char* cl = st.template b<CLAMPED>() + 3 * gl;
+      const float* sd = st.template f<SEED>() + 3 * gl;
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) sc.seed[gl][ch] = cl[ch] ? 0.f : sd[ch];
-      }
+      for (int ch = 0; ch < 3; ++ch) sc.seed[buf][gl][ch] = cl[ch] ? 0.f : sd[ch];
     }
   }
-  if constexpr (C::kAct) {
-    if (cw == 1) {
-      const float* q = st.template f<ROT>() + 4 * gl;
-      const float* sq = st.template f<SEED_ROT>() + 4 * gl;
-      float qr[4], sr[4], out[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        qr[k] = q[k];
-        sr[k] = sq[k];
-      }
-      quaternion_vjp(qr, sr, st.template f<SAVED_NORM>()[gl], out);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) sc.grad[R::kRot + 4 * gl + k] = out[k];
-    } else if (cw == 2) {
-      const float* ss = st.template f<SEED_SCL>() + 3 * gl;
-      const float* se = st.template f<SAVED_SCL>() + 3 * gl;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) sc.grad[R::kScl + 3 * gl + k] = se[k] * ss[k];
-    } else if (cw == 3) {
-      const float a = st.template f<SAVED_OPA>()[gl];
-      sc.grad[R::kOpa + gl] = (a * (1.f - a)) * st.template f<SEED_OPA>()[gl];
-    }
+}
+
+// Activation VJPs for the float4 group at element e of the activation regions
+// (controls/ManualActivations.cu:20-36, 94-100), computed in phase B: a rotation
+// group is one Gaussian's quaternion (pv holds its values before the update);
+// scaling and opacity groups are elementwise.
+template <class C>
+__device__ __forceinline__ float4 activation_gradient(const Stage<C>& st, int e,
+                                                      const float4& pv) {
+  using R = Region<C>;
+  if (e < R::kScl) {
+    const int gl = (e - R::kRot) >> 2;
+    const float4 sq = *reinterpret_cast<const float4*>(st.template f<SEED_ROT>() + 4 * gl);
+    const float qr[4] = {pv.x, pv.y, pv.z, pv.w};
+    const float sr[4] = {sq.x, sq.y, sq.z, sq.w};
+    float out[4];
+    quaternion_vjp(qr, sr, st.template f<SAVED_NORM>()[gl], out);
+    return make_float4(out[0], out[1], out[2], out[3]);
   }
+  if (e < R::kOpa) {
+    const int k = e - R::kScl;
+    const float4 ss = *reinterpret_cast<const float4*>(st.template f<SEED_SCL>() + k);
+    const float4 se = *reinterpret_cast<const float4*>(st.template f<SAVED_SCL>() + k);
+    return make_float4(se.x * ss.x, se.y * ss.y, se.z * ss.z, se.w * ss.w);
+  }
+  const int k = e - R::kOpa;
+  const float4 a = *reinterpret_cast<const float4*>(st.template f<SAVED_OPA>() + k);
+  const float4 so = *reinterpret_cast<const float4*>(st.template f<SEED_OPA>() + k);
+  return make_float4((a.x * (1.f - a.x)) * so.x, (a.y * (1.f - a.y)) * so.y,
+                     (a.z * (1.f - a.z)) * so.z, (a.w * (1.f - a.w)) * so.w);
 }
 
 // Phase A1.
 template <class C>
 __device__ __forceinline__ void phase_terms(const StepParams& p,
                                             const Stage<C>& st, Scratch& sc,
-                                            int cnt, int ct) {
+                                            int cnt, int ct, int buf) {
   if constexpr (C::kSh != SH_NONE) {
     const int term = ct >> 5, gl = ct & 31;  // term is warp-uniform
     if (gl >= cnt) return;
-    if (C::kSh == SH_SGD && !sc.visible[gl]) return;  // SGD skips invisible
+    if (C::kSh == SH_SGD && !sc.visible[buf][gl]) return;  // SGD skips invisible
     const int nterms = (p.degree + 1) * (p.degree + 1);
     switch (term) {
-      case 0: term_gradient<C, 0>(st, sc, gl, nterms); break;
-      case 1: term_gradient<C, 1>(st, sc, gl, nterms); break;
-      case 2: term_gradient<C, 2>(st, sc, gl, nterms); break;
-      case 3: term_gradient<C, 3>(st, sc, gl, nterms); break;
-      case 4: term_gradient<C, 4>(st, sc, gl, nterms); break;
-      case 5: term_gradient<C, 5>(st, sc, gl, nterms); break;
-      case 6: term_gradient<C, 6>(st, sc, gl, nterms); break;
-      case 7: term_gradient<C, 7>(st, sc, gl, nterms); break;
-      case 8: term_gradient<C, 8>(st, sc, gl, nterms); break;
-      case 9: term_gradient<C, 9>(st, sc, gl, nterms); break;
-      case 10: term_gradient<C, 10>(st, sc, gl, nterms); break;
-      case 11: term_gradient<C, 11>(st, sc, gl, nterms); break;
-      case 12: term_gradient<C, 12>(st, sc, gl, nterms); break;
-      case 13: term_gradient<C, 13>(st, sc, gl, nterms); break;
-      case 14: term_gradient<C, 14>(st, sc, gl, nterms); break;
-      default: term_gradient<C, 15>(st, sc, gl, nterms); break;
+      case 0: term_gradient<C, 0>(st, sc, buf, gl, nterms); break;
+      case 1: term_gradient<C, 1>(st, sc, buf, gl, nterms); break;
+      case 2: term_gradient<C, 2>(st, sc, buf, gl, nterms); break;
+      case 3: term_gradient<C, 3>(st, sc, buf, gl, nterms); break;
+      case 4: term_gradient<C, 4>(st, sc, buf, gl, nterms); break;
+      case 5: term_gradient<C, 5>(st, sc, buf, gl, nterms); break;
+      case 6: term_gradient<C, 6>(st, sc, buf, gl, nterms); break;
+      case 7: term_gradient<C, 7>(st, sc, buf, gl, nterms); break;
+      case 8: term_gradient<C, 8>(st, sc, buf, gl, nterms); break;
+      case 9: term_gradient<C, 9>(st, sc, buf, gl, nterms); break;
+      case 10: term_gradient<C, 10>(st, sc, buf, gl, nterms); break;
+      case 11: term_gradient<C, 11>(st, sc, buf, gl, nterms); break;
+      case 12: term_gradient<C, 12>(st, sc, buf, gl, nterms); break;
+      case 13: term_gradient<C, 13>(st, sc, buf, gl, nterms); break;
+      case 14: term_gradient<C, 14>(st, sc, buf, gl, nterms); break;
+      default: term_gradient<C, 15>(st, sc, buf, gl, nterms); break;
     }
   }
 }
@@ -380,10 +384,10 @@ __device__ __forceinline__ void phase_terms(const StepParams& p,
 // Position adjoint (warp 0, lane = Gaussian), after phase A1.
 template <class C>
 __device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
-                                                int cnt, int ct) {
+                                                int cnt, int ct, int buf) {
   if constexpr (C::kSh != SH_NONE) {
     const int gl = ct & 31;
-    if ((ct >> 5) != 0 || gl >= cnt || !sc.visible[gl]) return;
+    if ((ct >> 5) != 0 || gl >= cnt || !sc.visible[buf][gl]) return;
     float dd[3];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
@@ -395,7 +399,7 @@ __device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
       dd[k] = (v[0] + v[2]) + (v[1] + v[3]);
     }
     float o[3];
-    direction_vjp(load_direction(sc, gl), dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+    direction_vjp(load_direction(sc, buf, gl), dd[0], dd[1], dd[2], o[0], o[1], o[2]);
     float* dm = st.template f<DM>() + 3 * gl;
 #pragma unroll
     for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
@@ -477,7 +481,14 @@ __device__ __forceinline__ void phase_update(const StepParams& p,
   if (ct < kUpdateFirst) return;
   for (int q = ct - kUpdateFirst; q < R::kTotal / 4; q += kConsumers - kUpdateFirst) {
     const int e = 4 * q;
-    float4 pv = P[q], gv = G[q];
+    const float4 pv0 = P[q];
+    float4 pv = pv0, gv;
+    if constexpr (C::kAct) {
+      if (C::kSh == SH_NONE || e >= R::kRot) gv = activation_gradient<C>(st, e, pv0);
+      else gv = G[q];
+    } else {
+      gv = G[q];
+    }
     float4 mv = make_float4(0.f, 0.f, 0.f, 0.f), vv = mv;
     if constexpr (kMoments) {
       mv = M[q];
@@ -492,22 +503,18 @@ __device__ __forceinline__ void phase_update(const StepParams& p,
   }
 }
 
-// Phases A0, A1 and B with barriers between them; returns false (on every
-// consumer) if some consumer's stage wait timed out.
+// One whole tile (the one-tile kernel): warp 1 prepares the view data, then
+// phase A, then the position adjoint (warp 0) and phase B (warps 2-15).
 template <class C>
-__device__ __forceinline__ bool process_tile(const StepParams& p,
-                                             const Stage<C>& st, Scratch& sc,
-                                             int cnt, int ct,
-                                             const float cam[3], bool ready) {
-  if (!ready) sc.abort = 1;
-  else phase_directions<C>(st, sc, cnt, ct, cam);
+__device__ __forceinline__ void process_tile(const StepParams& p, const Stage<C>& st,
+                                             Scratch& sc, int cnt, int ct,
+                                             const float cam[3]) {
+  if ((ct >> 5) == 1) phase_directions<C>(st, sc, cnt, ct & 31, cam, 0);
   named_barrier(1, kConsumers);
-  if (sc.abort) return false;
-  phase_terms<C>(p, st, sc, cnt, ct);
-  if constexpr (C::kSh != SH_NONE) named_barrier(1, kConsumers);
-  finish_position<C>(st, sc, cnt, ct);
+  phase_terms<C>(p, st, sc, cnt, ct, 0);
+  named_barrier(1, kConsumers);
+  finish_position<C>(st, sc, cnt, ct, 0);
   phase_update<C>(p, st, sc, ct);
-  return true;
 }
 
 template <class C>
@@ -605,19 +612,43 @@ __global__ void __launch_bounds__(kPersistThreads, C::ctas)
     if (store_present && store_written)
       out_base = static_cast<char*>(const_cast<void*>(p.ptr[ct]));
   }
+  // Warp 1 waits for each stage and fills that tile's view data one tile ahead
+  // (the first before the loop, the next during phase B); the barrier that
+  // follows its wait orders every other consumer after its acquire, so only
+  // warp 1 waits on the full barriers.
+  const int cw = ct >> 5;
+  if (cw == 1 && first < p.tile_end) {
+    if (!mbar_wait_bounded(&full_bar[0], 0)) {
+      atomicOr(&g_fault_word, kFaultConsumerWait);
+      scratch.abort = 1;
+    } else {
+      phase_directions<C>(Stage<C>{smem}, scratch, kTile, ct & 31, cam, 0);
+    }
+  }
+  named_barrier(1, kConsumers);
   int k = 0;
   for (long long t = first; t < p.tile_end; t += stride, ++k) {
-    const int s = k % S;
-    // Warps 0-3 read the stage in phase A0 and wait for it; the others first
-    // touch it after the barrier that follows A0, which orders them after the
-    // waiters' acquire.
-    bool ready = true;
-    if (ct < 128) {
-      ready = mbar_wait_bounded(&full_bar[s], (k / S) & 1);
-      if (!ready) atomicOr(&g_fault_word, kFaultConsumerWait);
-    }
+    if (scratch.abort) break;
+    const int s = k % S, buf = k & 1;
     Stage<C> st{smem + size_t(s) * C::stage_bytes};
-    if (!process_tile<C>(p, st, scratch, kTile, ct, cam, ready)) break;
+    phase_terms<C>(p, st, scratch, kTile, ct, buf);
+    named_barrier(1, kConsumers);
+    if (cw == 0) {
+      finish_position<C>(st, scratch, kTile, ct, buf);
+    } else if (cw == 1) {
+      if (t + stride < p.tile_end) {
+        const int k1 = k + 1, s1 = k1 % S;
+        if (!mbar_wait_bounded(&full_bar[s1], (k1 / S) & 1)) {
+          atomicOr(&g_fault_word, kFaultConsumerWait);
+          scratch.abort = 1;
+        } else {
+          phase_directions<C>(Stage<C>{smem + size_t(s1) * C::stage_bytes}, scratch, kTile,
+                              ct & 31, cam, k1 & 1);
+        }
+      }
+    } else {
+      phase_update<C>(p, st, scratch, ct);
+    }
     fence_async_shared();
     named_barrier(1, kConsumers);
     if (ct < 32) {
@@ -670,7 +701,7 @@ __global__ void __launch_bounds__(kConsumers)
   float cam[3];
   load_camera<C>(p, cam);
   __syncthreads();
-  process_tile<C>(p, st, scratch, cnt, threadIdx.x, cam, true);
+  process_tile<C>(p, st, scratch, cnt, threadIdx.x, cam);
   __syncthreads();
   for_each_arr([&](auto a_) {
     constexpr int a = decltype(a_)::value;
