@@ -82,13 +82,20 @@ _SIGNATURES = {
     "clad3dgs_raster_backward": (c_int, [c_int, c_int] + [_P] * 6 + [c_float] + [_P] * 4
                                  + [c_float, c_float, c_int, c_int] + [_P] * 7 + [c_int]
                                  + [_P] * 2 + [c_int] + [_P] * 10 + [c_int, c_int]
-                                 + [_P] * 6 + [TorchAdamConfig, _P]),
+                                 + [_P] * 6 + [TorchAdamConfig, _P, _P, c_double,
+                                               TorchAdamConfig, _P]),
     "clad3dgs_raster_forward_2d": (c_int, [c_int] + [_P] * 5 + [c_int, c_int, _P, _P, _P,
                                                                _P, _P, POINTER(c_int), _P]),
     "clad3dgs_gaussian_step_host_static": (c_int, [c_int64, c_int] + [_P] * 12
                                            + [TorchAdamConfig] + [_PP] * 5
                                            + [POINTER(c_double), POINTER(c_float),
                                               POINTER(c_float), c_int64, _P]),
+    "clad3dgs_sh_consume_xyz": (c_int, [c_int64, c_int] + [_P] * 13 + [TorchAdamConfig]
+                                + [_P, _P, c_double, TorchAdamConfig, _P]),
+    "clad3dgs_gaussian_step_xyz": (c_int, [c_int64, c_int] + [_P] * 13 + [TorchAdamConfig]
+                                   + [_PP] * 5 + [POINTER(c_double), POINTER(c_float),
+                                                  POINTER(c_float)]
+                                   + [_P, _P, c_double, TorchAdamConfig, _P]),
     "clad3dgs_activate": (c_int, [c_int64] + [_P] * 7 + [_P]),
     "clad3dgs_l1_loss": (c_int, [c_int64, _P, _P, _P, _P, _P]),
     "clad3dgs_shard_update": (c_int, [POINTER(ShardUpdateArgs), _P]),

@@ -16,6 +16,14 @@ ownership between forward and backward raises before a write.
 
 The cached state is nothing: every step binds the optimizer's current
 objects, so checkpoint restore, densification and pruning need no hook.
+
+`consume_position=True` (not in the reference, whose trainer leaves xyz to
+torch's Adam) also binds the optimizer's "xyz" group: once the direction
+adjoint is added dL/dmeans is the positions' complete gradient, so the same
+kernel runs their Adam, the backward returns no position gradient, and the
+frame advances the xyz counter with the SH ones. Only valid when the means feed
+nothing but this renderer; an ineligible xyz group leaves the positions to the
+optimizer (`position_reason` says why) and the SH groups are still consumed.
 """
 
 from __future__ import annotations
@@ -83,12 +91,21 @@ class ConsumerRender(torch.autograd.Function):
         m_dc, v_dc = owner.moments["dc"]
         m_rest, v_rest = owner.moments["rest"]
         step = owner.iteration
+        bias1, bias2 = 1 - 0.9 ** step, math.sqrt(1 - 0.999 ** step)
         consume = (owner.extension.rasterize_gaussians_backward_consume_direct
                    if getattr(owner, "direct_inputs", False)
                    else owner.extension.rasterize_gaussians_backward_consume)
+        extra = {}
+        position = "xyz" in owner.params
+        if position:
+            m_xyz, v_xyz = owner.moments["xyz"]
+            extra["xyz"] = dict(first=m_xyz, second=v_xyz, rate=owner.position_rate,
+                                bias1=bias1, bias2_sqrt=bias2)
         grads = consume(*args, owner.params["dc"], owner.params["rest"], m_dc, v_dc,
-                        m_rest, v_rest, 1 - 0.9 ** step, math.sqrt(1 - 0.999 ** step))
+                        m_rest, v_rest, bias1, bias2, **extra)
         g_screen, _, g_opacity, g_means, _, _, g_scale, g_rot = grads
+        if position:
+            g_means = None  # applied by the kernel
         return g_means, g_screen, None, None, g_opacity, g_scale, g_rot, None, None
 
 
@@ -136,9 +153,10 @@ class BoundStep:
         self.groups = groups
         self.states = states
         self.extension = extension
-        self.params = {k: g["params"][0] for k, g in zip(("dc", "rest"), groups)}
-        self.moments = {k: (st["exp_avg"], st["exp_avg_sq"])
-                        for k, st in zip(("dc", "rest"), states)}
+        keys = ("dc", "rest", "xyz")[:len(groups)]
+        self.params = {k: g["params"][0] for k, g in zip(keys, groups)}
+        self.moments = {k: (st["exp_avg"], st["exp_avg_sq"]) for k, st in zip(keys, states)}
+        self.position_rate = float(groups[2]["lr"]) if len(groups) > 2 else None
         self.iteration = iteration
         self.consumed = False
         self.versions = [p._version for p in self.params.values()]
@@ -182,7 +200,8 @@ class LifecycleRender(ConsumerRender):
 
 
 class DenseSHConsumer:
-    def __init__(self, optimizer, *, native, extension, direct_inputs=False):
+    def __init__(self, optimizer, *, native, extension, direct_inputs=False,
+                 consume_position=False):
         if direct_inputs and not all(
                 hasattr(extension, name) for name in
                 ("rasterize_gaussians_direct", "rasterize_gaussians_backward_consume_direct")):
@@ -191,14 +210,79 @@ class DenseSHConsumer:
         self.extension = extension
         self.direct_inputs = direct_inputs
         self.optimizer = optimizer
+        self.consume_position = consume_position
         self.active = None
         self.last_reason = None
+        self.position_reason = None
 
     def _fallback(self, reason):
         self.last_reason = reason
         return None
 
-    def bind(self, dc, rest, policy):
+    @staticmethod
+    def _group_reason(group, param, shape, what):
+        """Why `group` cannot be consumed (None if it can); the rate is checked
+        by the caller."""
+        if len(group["params"]) != 1 or group["params"][0] is not param:
+            return f"{what} parameter ownership mismatch"
+        if (tuple(param.shape) != shape or not param.is_contiguous()
+                or param.dtype != torch.float32 or not param.is_cuda):
+            return f"unsupported {what} tensor layout"
+        if not param.requires_grad or param.grad is not None:
+            return f"frozen or accumulated {what} gradients"
+        if group["betas"] != (0.9, 0.999) or group["eps"] != 1e-15:
+            return f"unsupported {what} Adam hyperparameters"
+        if group.get("fused") is not True or group.get("foreach"):
+            return f"{what} consumption requires fused Adam without foreach"
+        if (any(group.get(k, False) for k in
+                ("amsgrad", "maximize", "differentiable", "capturable"))
+                or group.get("weight_decay", 0) != 0):
+            return "unsupported Adam option"
+        return None
+
+    @staticmethod
+    def _state_for(optimizer, group):
+        param = group["params"][0]
+        state = optimizer.state.get(param)
+        if not state:
+            state = {"step": torch.tensor(0.0, device=param.device if group.get("fused")
+                                          else "cpu"),
+                     "exp_avg": torch.zeros_like(param),
+                     "exp_avg_sq": torch.zeros_like(param)}
+        for key in ("exp_avg", "exp_avg_sq"):
+            value = state.get(key)
+            if (not torch.is_tensor(value) or value.shape != param.shape
+                    or value.dtype != param.dtype or value.device != param.device
+                    or not value.is_contiguous()):
+                return None, "moment layout"
+        step = state.get("step")
+        if (not torch.is_tensor(step) or step.device != param.device
+                or step.dtype != torch.float32 or step.numel() != 1):
+            return None, "step counter"
+        return state, None
+
+    def _position_group(self, means, count, device):
+        """The xyz group and its state, or (None, reason)."""
+        if means is None:
+            return None, None, "positions not given"
+        matches = [g for g in self.optimizer.param_groups if g.get("name") == "xyz"]
+        if len(matches) != 1:
+            return None, None, "missing or duplicate xyz optimizer group"
+        group = matches[0]
+        reason = self._group_reason(group, means, (count, 3), "position")
+        rate = group.get("lr")
+        if reason is None and (not isinstance(rate, (float, int)) or not math.isfinite(rate)):
+            reason = "unsupported position learning rate"
+        if reason is None and means.device != device:
+            reason = "position device mismatch"
+        if reason is not None:
+            return None, None, reason
+        state, bad = self._state_for(self.optimizer, group)
+        if state is None:
+            return None, None, f"unsupported position {bad}"
+        return group, state, None
+
+    def bind(self, dc, rest, policy, means=None):
         if self.active is not None:
             raise RuntimeError("finish the previous optimizer step first")
         reason = policy.reason()
@@ -271,6 +355,21 @@ class DenseSHConsumer:
             return self._fallback("invalid SH step counter")
         if counters[0] != counters[1]:
             return self._fallback("different SH Adam step counters")
+        self.position_reason = None
+        if self.consume_position:
+            group, state, why = self._position_group(means, dc.shape[0], dc.device)
+            if why is None and state["step"].item() != counters[0]:
+                why = "position and SH Adam step counters differ"
+            if why is None:
+                extra = [means] + [state[k] for k in STATE_KEYS]
+                spans = sorted((v.data_ptr(), v.data_ptr() + v.numel() * v.element_size())
+                               for v in writable + extra if v.numel())
+                if any(a[1] > b[0] for a, b in zip(spans, spans[1:])):
+                    why = "positions overlap the SH parameters or moments"
+            if why is None:
+                groups.append(group)
+                states.append(state)
+            self.position_reason = why
         for group, state in zip(groups, states):
             self.optimizer.state[group["params"][0]] = state
         self.active = BoundStep(self.optimizer, groups, states, self.extension,
@@ -280,7 +379,7 @@ class DenseSHConsumer:
         return self.active
 
     def render(self, means, screen, dc, rest, opacity, scale, rotation, settings, policy):
-        owner = self.bind(dc, rest, policy)
+        owner = self.bind(dc, rest, policy, means)
         if owner is not None:
             return LifecycleRender.apply(means, screen, dc, rest, opacity, scale, rotation,
                                          settings, owner)

@@ -43,14 +43,29 @@ def _cuda_f32(t, device, name, contiguous=True):
         _require(t.is_contiguous(), f"{name} must be contiguous")
 
 
+def _position_state(xyz, means, n, device):
+    """Checks the optional position Adam state {first, second, rate, bias1,
+    bias2_sqrt}; means is then updated in place and must be the parameter."""
+    if xyz is None:
+        return None
+    _cuda_f32(means, device, "means")
+    for key in ("first", "second"):
+        _cuda_f32(xyz[key], device, "xyz " + key)
+        _require(xyz[key].numel() == 3 * n, f"bad xyz {key} shape")
+    return xyz
+
+
 def sh_consume_split_torch_adam(means, radii, clamped, camera, seed, dm, dc, rest,
                                 dc_first, dc_second, rest_first, rest_second, *,
                                 bias1: float, bias2_sqrt: float, degree: int,
-                                coefficient=None, stream=None):
+                                coefficient=None, xyz=None, stream=None):
     """Fused SH VJP + torch-fused Adam on split dc/rest (in place), dm += the
-    position adjoint. Same contract as sh_consumer_split_torch_adam."""
+    position adjoint. Same contract as sh_consumer_split_torch_adam. With `xyz`
+    ({first, second, rate, bias1, bias2_sqrt}) the same pass also runs
+    torch-fused Adam on means in place, dm being their complete gradient."""
     n = means.shape[0]
     device = means.device
+    xyz = _position_state(xyz, means, n, device)
     _require(0 <= degree <= 3, "SH degree must be between zero and three")
     _require(means.dim() == 2 and means.shape[1] == 3, "means must be [N, 3]")
     for name, t, numel in (("dc", dc, 3 * n), ("rest", rest, 45 * n),
@@ -74,10 +89,24 @@ def sh_consume_split_torch_adam(means, radii, clamped, camera, seed, dm, dc, res
         coefficient = coefficient.contiguous()
         _require(coefficient.numel() == 48 * n and coefficient.dtype == torch.float32,
                  "coefficient snapshot must be float32 [N, 16, 3]")
-    check_disjoint([dc, rest, dc_first, dc_second, rest_first, rest_second, dm],
-                   [means, clamped, seed, camera, coefficient],
+    writable = [dc, rest, dc_first, dc_second, rest_first, rest_second, dm]
+    if xyz is not None:
+        writable += [means, xyz["first"], xyz["second"]]
+    check_disjoint(writable, [clamped, seed, camera, coefficient] +
+                   ([] if xyz is not None else [means]),
                    "direct SH coefficient and moment buffers must be disjoint")
     if n == 0:
+        return
+    if xyz is not None:
+        native.check(native.library().clad3dgs_sh_consume_xyz(
+            n, degree, native.ptr(means), native.ptr(radii), native.ptr(coefficient),
+            native.ptr(clamped), native.ptr(camera), native.ptr(seed), native.ptr(dm),
+            native.ptr(dc), native.ptr(rest), native.ptr(dc_first), native.ptr(dc_second),
+            native.ptr(rest_first), native.ptr(rest_second),
+            native.TorchAdamConfig(bias1, bias2_sqrt), native.ptr(xyz["first"]),
+            native.ptr(xyz["second"]), float(xyz["rate"]),
+            native.TorchAdamConfig(xyz["bias1"], xyz["bias2_sqrt"]),
+            native.stream_handle(stream)), "SH + position consume")
         return
     native.check(native.library().clad3dgs_sh_consume_split_torch_adam(
         n, degree, native.ptr(means), native.ptr(radii), native.ptr(coefficient),
@@ -138,8 +167,10 @@ def quaternion_backward_raw(q, seed, norms, out, stream=None):
 def gaussian_step(means, radii, clamped, camera, seed, dm, dc, rest, dc_first,
                   dc_second, rest_first, rest_second, *, bias1, bias2_sqrt, degree,
                   act_parameters, act_seeds, act_saved, act_first, act_second,
-                  act_rates, act_bias1, act_bias2, coefficient=None, stream=None):
-    """SH consume and activation consume fused into one pass per Gaussian.
+                  act_rates, act_bias1, act_bias2, coefficient=None, xyz=None,
+                  stream=None):
+    """SH consume and activation consume fused into one pass per Gaussian (with
+    `xyz`, the positions' Adam too: all 59 parameters of a Gaussian in one pass).
     Inputs are trusted to be contiguous, disjoint CUDA float32 buffers in the
     reference layouts (validate with the separate entry points' rules)."""
     n = means.shape[0]
@@ -147,6 +178,18 @@ def gaussian_step(means, radii, clamped, camera, seed, dm, dc, rest, dc_first,
         return
     arrays = _activation_arrays(act_parameters, act_seeds, act_saved, act_first,
                                 act_second)
+    if xyz is not None:
+        native.check(native.library().clad3dgs_gaussian_step_xyz(
+            n, degree, native.ptr(means), native.ptr(radii), native.ptr(coefficient),
+            native.ptr(clamped), native.ptr(camera), native.ptr(seed), native.ptr(dm),
+            native.ptr(dc), native.ptr(rest), native.ptr(dc_first), native.ptr(dc_second),
+            native.ptr(rest_first), native.ptr(rest_second),
+            native.TorchAdamConfig(bias1, bias2_sqrt), *arrays,
+            native.doubles(act_rates), native.floats(act_bias1), native.floats(act_bias2),
+            native.ptr(xyz["first"]), native.ptr(xyz["second"]), float(xyz["rate"]),
+            native.TorchAdamConfig(xyz["bias1"], xyz["bias2_sqrt"]),
+            native.stream_handle(stream)), "fused Gaussian step with positions")
+        return
     native.check(native.library().clad3dgs_gaussian_step(
         n, degree, native.ptr(means), native.ptr(radii), native.ptr(coefficient),
         native.ptr(clamped), native.ptr(camera), native.ptr(seed), native.ptr(dm),

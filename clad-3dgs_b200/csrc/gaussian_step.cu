@@ -53,6 +53,8 @@ enum Arr : int {
   DC_M, REST_M, COEF_M, ROT_M, SCL_M, OPA_M,
   DC_V, REST_V, COEF_V, ROT_V, SCL_V, OPA_V,
   SNAP, SEED_ROT, SEED_SCL, SEED_OPA, SAVED_NORM, SAVED_SCL, SAVED_OPA,
+  // Adam moments of the positions (means are then updated and written back).
+  XYZ_M, XYZ_V,
   NUM_ARR
 };
 
@@ -60,12 +62,14 @@ constexpr int kWidth[NUM_ARR] = {3, 1, 3, 3, 3,
                                  3, 45, 48, 4, 3, 1,
                                  3, 45, 48, 4, 3, 1,
                                  3, 45, 48, 4, 3, 1,
-                                 48, 4, 3, 1, 1, 3, 1};
+                                 48, 4, 3, 1, 1, 3, 1,
+                                 3, 3};
 constexpr bool kWritten[NUM_ARR] = {0, 0, 0, 0, 1,
                                     1, 1, 1, 1, 1, 1,
                                     1, 1, 1, 1, 1, 1,
                                     1, 1, 1, 1, 1, 1,
-                                    0, 0, 0, 0, 0, 0, 0};
+                                    0, 0, 0, 0, 0, 0, 0,
+                                    1, 1};
 constexpr int elem_bytes(int a) { return a == CLAMPED ? 1 : 4; }
 
 enum ShMode : int { SH_NONE, SH_SGD, SH_ADAM, SH_SPLIT_ADAM, SH_SPLIT_TORCH };
@@ -93,12 +97,16 @@ constexpr uint32_t stage_budget(int ctas) {
 }
 constexpr uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-template <int Sh, bool Act, bool Snap>
+template <int Sh, bool Act, bool Snap, bool Xyz = false>
 struct Cfg {
   static constexpr int kSh = Sh;
   static constexpr bool kAct = Act;
   static constexpr bool kSnap = Snap;
+  // Torch-fused Adam on the positions too (dm is their complete gradient).
+  static constexpr bool kXyz = Xyz && Sh == SH_SPLIT_TORCH;
+  static constexpr bool written(int a) { return kWritten[a] || (kXyz && a == MEANS); }
   static constexpr bool has(int a) {
+    if (a == XYZ_M || a == XYZ_V) return kXyz;
     if (a == MEANS || a == RADII || a == CLAMPED || a == SEED || a == DM)
       return Sh != SH_NONE;
     if (a == COEF) return Sh == SH_SGD || Sh == SH_ADAM;
@@ -155,6 +163,8 @@ struct StepParams {
   float inv_bias1, inv_bias2;                // float Adam (AdamConfig)
   float act_step[3];                         // rotation, scaling, opacity
   double act_inv_bias2[3];
+  float xyz_step;                            // torch Adam on the positions
+  double xyz_inv_bias2;
 };
 
 template <class F, int... Is>
@@ -381,28 +391,41 @@ __device__ __forceinline__ void phase_terms(const StepParams& p,
   }
 }
 
-// Position adjoint (warp 0, lane = Gaussian), after phase A1.
+// Position adjoint (warp 0, lane = Gaussian), after phase A: the direction
+// adjoints of the 16 terms in the reference's tree order, into dm; then, in the
+// configurations that own the positions, torch-fused Adam on them with dm as
+// the gradient (every Gaussian, as the optimizer would).
 template <class C>
-__device__ __forceinline__ void finish_position(const Stage<C>& st, Scratch& sc,
-                                                int cnt, int ct, int buf) {
+__device__ __forceinline__ void finish_position(const StepParams& p, const Stage<C>& st,
+                                                Scratch& sc, int cnt, int ct, int buf) {
   if constexpr (C::kSh != SH_NONE) {
     const int gl = ct & 31;
-    if ((ct >> 5) != 0 || gl >= cnt || !sc.visible[buf][gl]) return;
-    float dd[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      float v[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-        v[r] = (sc.partial[r][gl][k] + sc.partial[r + 8][gl][k]) +
-               (sc.partial[r + 4][gl][k] + sc.partial[r + 12][gl][k]);
-      dd[k] = (v[0] + v[2]) + (v[1] + v[3]);
-    }
-    float o[3];
-    direction_vjp(load_direction(sc, buf, gl), dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+    if ((ct >> 5) != 0 || gl >= cnt) return;
     float* dm = st.template f<DM>() + 3 * gl;
+    if (sc.visible[buf][gl]) {
+      float dd[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
+      for (int k = 0; k < 3; ++k) {
+        float v[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          v[r] = (sc.partial[r][gl][k] + sc.partial[r + 8][gl][k]) +
+                 (sc.partial[r + 4][gl][k] + sc.partial[r + 12][gl][k]);
+        dd[k] = (v[0] + v[2]) + (v[1] + v[3]);
+      }
+      float o[3];
+      direction_vjp(load_direction(sc, buf, gl), dd[0], dd[1], dd[2], o[0], o[1], o[2]);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dm[k] = dm[k] + o[k];
+    }
+    if constexpr (C::kXyz) {
+      float* m = st.template f<MEANS>() + 3 * gl;
+      float* first = st.template f<XYZ_M>() + 3 * gl;
+      float* second = st.template f<XYZ_V>() + 3 * gl;
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+        torch_adam(m[k], first[k], second[k], dm[k], p.xyz_step, p.xyz_inv_bias2);
+    }
   }
 }
 
@@ -513,7 +536,7 @@ __device__ __forceinline__ void process_tile(const StepParams& p, const Stage<C>
   named_barrier(1, kConsumers);
   phase_terms<C>(p, st, sc, cnt, ct, 0);
   named_barrier(1, kConsumers);
-  finish_position<C>(st, sc, cnt, ct, 0);
+  finish_position<C>(p, st, sc, cnt, ct, 0);
   phase_update<C>(p, st, sc, ct);
 }
 
@@ -537,7 +560,7 @@ __device__ __forceinline__ void lane_array(int lane, bool& present, bool& writte
   for_each_arr([&](auto a_) {
     constexpr int a = decltype(a_)::value;
     if constexpr (C::has(a)) {
-      constexpr bool kWrites = kWritten[a];
+      constexpr bool kWrites = C::written(a);
       constexpr uint32_t kOffset = C::offset(a), kBytes = C::tile_bytes(a);
       if (lane == a) {
         present = true;
@@ -634,7 +657,7 @@ __global__ void __launch_bounds__(kPersistThreads, C::ctas)
     phase_terms<C>(p, st, scratch, kTile, ct, buf);
     named_barrier(1, kConsumers);
     if (cw == 0) {
-      finish_position<C>(st, scratch, kTile, ct, buf);
+      finish_position<C>(p, st, scratch, kTile, ct, buf);
     } else if (cw == 1) {
       if (t + stride < p.tile_end) {
         const int k1 = k + 1, s1 = k1 % S;
@@ -705,7 +728,7 @@ __global__ void __launch_bounds__(kConsumers)
   __syncthreads();
   for_each_arr([&](auto a_) {
     constexpr int a = decltype(a_)::value;
-    if constexpr (C::has(a) && kWritten[a]) {
+    if constexpr (C::has(a) && C::written(a)) {
       const int count = cnt * kWidth[a];
       const long long base = g0 * kWidth[a];
       float* dst = static_cast<float*>(const_cast<void*>(p.ptr[a]));
@@ -887,6 +910,13 @@ void set_activations(StepParams& p, float* const* parameters,
   }
 }
 
+void set_xyz(StepParams& p, float* first, float* second, double rate, TorchAdamConfig c) {
+  p.ptr[XYZ_M] = first;
+  p.ptr[XYZ_V] = second;
+  p.xyz_step = float(rate / double(c.bias1));
+  p.xyz_inv_bias2 = 1.0 / double(c.bias2_sqrt);
+}
+
 bool degree_ok(int degree) { return degree >= 0 && degree <= 3; }
 
 int status_of(cudaError_t e, const char* what) {
@@ -904,6 +934,10 @@ using PackedSgd = Cfg<SH_SGD, false, false>;
 using ActOnly = Cfg<SH_NONE, true, false>;
 using Fused = Cfg<SH_SPLIT_TORCH, true, false>;
 using FusedSnap = Cfg<SH_SPLIT_TORCH, true, true>;
+using SplitTorchXyz = Cfg<SH_SPLIT_TORCH, false, false, true>;
+using SplitTorchXyzSnap = Cfg<SH_SPLIT_TORCH, false, true, true>;
+using FusedXyz = Cfg<SH_SPLIT_TORCH, true, false, true>;
+using FusedXyzSnap = Cfg<SH_SPLIT_TORCH, true, true, true>;
 
 cudaError_t run_split_torch(StepParams& p, cudaStream_t stream) {
   return p.ptr[SNAP] ? run<SplitTorchSnap>(p, stream) : run<SplitTorch>(p, stream);
@@ -1150,5 +1184,50 @@ extern "C" int clad3dgs_gaussian_step(
   set_activations(p, parameters, seeds, saved, first, second, rates, bias1,
                   bias2);
   cudaError_t e = coefficient ? run<FusedSnap>(p, stream) : run<Fused>(p, stream);
+  return status_of(e, "fused Gaussian step launch");
+}
+
+extern "C" int clad3dgs_sh_consume_xyz(
+    int64_t n, int degree, float* means, const int* radii, const float* coefficient,
+    const bool* clamped, const float* camera, const float* seed, float* dm, float* dc,
+    float* rest, float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* xyz_first, float* xyz_second, double xyz_rate,
+    TorchAdamConfig xyz_config, cudaStream_t stream) {
+  if (n <= 0) return CLAD3DGS_OK;
+  if (!degree_ok(degree))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  set_torch_config(p, sh_config);
+  set_xyz(p, xyz_first, xyz_second, xyz_rate, xyz_config);
+  cudaError_t e = coefficient ? run<SplitTorchXyzSnap>(p, stream)
+                              : run<SplitTorchXyz>(p, stream);
+  return status_of(e, "SH + position consume launch");
+}
+
+extern "C" int clad3dgs_gaussian_step_xyz(
+    int64_t n, int degree, float* means, const int* radii, const float* coefficient,
+    const bool* clamped, const float* camera, const float* seed, float* dm, float* dc,
+    float* rest, float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* const* parameters, const float* const* seeds,
+    const float* const* saved, float* const* first, float* const* second,
+    const double* rates, const float* bias1, const float* bias2, float* xyz_first,
+    float* xyz_second, double xyz_rate, TorchAdamConfig xyz_config, cudaStream_t stream) {
+  if (n <= 0) return CLAD3DGS_OK;
+  if (!degree_ok(degree))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "SH degree must be between zero and three");
+  StepParams p = base_params(n);
+  set_sh_inputs(p, degree, means, radii, clamped, camera, seed, dm);
+  set_split(p, coefficient, dc, rest, dc_first, dc_second, rest_first,
+            rest_second);
+  set_torch_config(p, sh_config);
+  set_activations(p, parameters, seeds, saved, first, second, rates, bias1,
+                  bias2);
+  set_xyz(p, xyz_first, xyz_second, xyz_rate, xyz_config);
+  cudaError_t e = coefficient ? run<FusedXyzSnap>(p, stream) : run<FusedXyz>(p, stream);
   return status_of(e, "fused Gaussian step launch");
 }

@@ -1190,7 +1190,8 @@ extern "C" int clad3dgs_raster_backward(
     float* dcov3d, float* dsh, float* dscales, float* drotations, float* dconic_scratch,
     float* dinvdepth_scratch, int mode, int consume_sh, float* dc, float* rest,
     float* dc_first, float* dc_second, float* rest_first, float* rest_second,
-    TorchAdamConfig config, cudaStream_t stream) {
+    TorchAdamConfig config, float* xyz_first, float* xyz_second, double xyz_rate,
+    TorchAdamConfig xyz_config, cudaStream_t stream) {
   if (degree < 0 || degree > 3)
     return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
   if (P <= 0) return CLAD3DGS_OK;
@@ -1216,10 +1217,16 @@ extern "C" int clad3dgs_raster_backward(
   }
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) return status_of(e, "geometry backward");
-  if (consume_sh && colors_precomp == nullptr)
+  if (consume_sh && colors_precomp == nullptr) {
+    if (xyz_first)  // the positions' Adam too; means are updated after every read of them
+      return clad3dgs_sh_consume_xyz(P, degree, const_cast<float*>(means), radii, sh_packed,
+                                     g.clamped, campos, dcolor, dmeans, dc, rest, dc_first,
+                                     dc_second, rest_first, rest_second, config, xyz_first,
+                                     xyz_second, xyz_rate, xyz_config, stream);
     return clad3dgs_sh_consume_split_torch_adam(
         P, degree, means, radii, sh_packed, g.clamped, campos, dcolor, dmeans, dc, rest,
         dc_first, dc_second, rest_first, rest_second, config, stream);
+  }
   return CLAD3DGS_OK;
 }
 

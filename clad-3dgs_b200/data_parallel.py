@@ -442,5 +442,6 @@ class DataParallelTrainer:
             g["xyz"].data_ptr(), s["cov"].data_ptr(), g["sh"].data_ptr(),
             g["scaling"].data_ptr(), g["rotation"].data_ptr(), s["conic"].data_ptr(),
             s["invdepth"].data_ptr(), self.mode, 0, None, None, None, None, None, None,
-            native.TorchAdamConfig(1.0, 1.0), stream), "rasterize (backward)")
+            native.TorchAdamConfig(1.0, 1.0), None, None, 0.0, native.TorchAdamConfig(1.0, 1.0),
+            stream), "rasterize (backward)")
         return self.loss, rendered.value

@@ -15,7 +15,8 @@ Module globals, set by the launcher: SUMMARY (a routing.RoutingSummary),
 TRACE (a JSON path; trace mode synchronises and snapshots parameters, for
 small functional fixtures only), DIRECT_INPUTS (render from dc/rest directly),
 ACTIVATION_EXTENSION (the clad_quaternion surface, or None to disable
-activation consumption).
+activation consumption), POSITION (also consume the xyz group; not in the
+reference).
 """
 
 from __future__ import annotations
@@ -35,6 +36,7 @@ SUMMARY = None
 TRACE = None
 DIRECT_INPUTS = False
 ACTIVATION_EXTENSION = None
+POSITION = False  # also consume the xyz group (see adapter.DenseSHConsumer)
 
 
 def counters(model, parameters=None):
@@ -90,9 +92,10 @@ def render_consumer(model, means, screen, opacity, scale, rotation, settings, po
     if SUMMARY is not None and hasattr(model, "_clad_routing"):
         model._clad_routing["sh_called"] = True
     consumer = getattr(model, "_clad_consumer", None)
-    if consumer is None or consumer.optimizer is not model.optimizer:
+    if (consumer is None or consumer.optimizer is not model.optimizer
+            or consumer.consume_position != POSITION):
         consumer = DenseSHConsumer(model.optimizer, native=native, extension=extension,
-                                   direct_inputs=DIRECT_INPUTS)
+                                   direct_inputs=DIRECT_INPUTS, consume_position=POSITION)
         model._clad_consumer = consumer
     return consumer.render(means, screen, model._features_dc, model._features_rest, opacity,
                            scale, rotation, settings, policy)

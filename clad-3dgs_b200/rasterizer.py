@@ -16,9 +16,11 @@ results, backed by libclad3dgs_b200.so:
   binningBuffer, imageBuffer, antialiasing, debug) -> (dL_dmeans2D, dL_dcolors,
   dL_dopacity, dL_dmeans3D, dL_dcov3D, dL_dsh, dL_dscales, dL_drotations)`
 * `rasterize_gaussians_backward_consume(<the 24 above>, dc, rest, dc_first,
-  dc_second, rest_first, rest_second, bias1, bias2_sqrt)`: the SH adjoint goes
-  to the fused SH + Adam kernel (dc/rest and moments updated in place) and the
-  returned dL_dsh is empty (prepare_native.py:32-93).
+  dc_second, rest_first, rest_second, bias1, bias2_sqrt, *, xyz=None)`: the SH
+  adjoint goes to the fused SH + Adam kernel (dc/rest and moments updated in
+  place) and the returned dL_dsh is empty (prepare_native.py:32-93). With
+  `xyz={first, second, rate, bias1, bias2_sqrt}` the same kernel also runs the
+  positions' Adam (means3D updated in place; an addition of this package).
 * `*_direct` variants take (dc, rest) in place of the packed `sh`
   (direct_inputs.py:80-220).
 * `mark_visible(means3D, viewmatrix, projmatrix)`.
@@ -171,6 +173,7 @@ def _backward(bg, means3D, radii, colors, opacities, scales, rotations, scale_mo
                 g["scales"], g["rotations"])
     c = consume or {}
     b1, b2 = (consume["bias1"], consume["bias2_sqrt"]) if consume else (1.0, 1.0)
+    xyz = c.get("xyz") or {}
     dpix = dL_dout_color.contiguous()
     dinv = _contig(dL_dout_invdepth)
     keep = dict(bg=bg.contiguous(), means=means3D.contiguous(), radii=radii.contiguous(),
@@ -192,7 +195,10 @@ def _backward(bg, means3D, radii, colors, opacities, scales, rotations, scale_mo
         int(consume is not None), native.ptr(c.get("dc")), native.ptr(c.get("rest")),
         native.ptr(c.get("dc_first")), native.ptr(c.get("dc_second")),
         native.ptr(c.get("rest_first")), native.ptr(c.get("rest_second")),
-        native.TorchAdamConfig(b1, b2), native.stream_handle())
+        native.TorchAdamConfig(b1, b2), native.ptr(xyz.get("first")),
+        native.ptr(xyz.get("second")), float(xyz.get("rate", 0.0)),
+        native.TorchAdamConfig(xyz.get("bias1", 1.0), xyz.get("bias2_sqrt", 1.0)),
+        native.stream_handle())
     native.check(status, "rasterize_gaussians_backward")
     return (g["mean2d"], g["colors"], g["opacity"], g["means"], g["cov"], g["sh"],
             g["scales"], g["rotations"])
@@ -223,7 +229,7 @@ def rasterize_gaussians_backward_direct(bg, means3D, radii, colors, opacities, s
 
 
 def _consume_state(means3D, degree, dc, rest, dc_first, dc_second, rest_first, rest_second,
-                   bias1, bias2_sqrt):
+                   bias1, bias2_sqrt, xyz=None):
     # prepare_native.py:52-67: default stream, split shapes and layouts.
     _check(torch.cuda.current_stream().cuda_stream == 0,
            "SH consumption requires the default CUDA stream")
@@ -237,9 +243,22 @@ def _consume_state(means3D, degree, dc, rest, dc_first, dc_second, rest_first, r
     _check(dc.numel() == 3 * P and dc_first.numel() == 3 * P and dc_second.numel() == 3 * P
            and rest.numel() == 45 * P and rest_first.numel() == 45 * P
            and rest_second.numel() == 45 * P, "bad split coefficient or optimizer-state shape")
-    return dict(dc=dc, rest=rest, dc_first=dc_first, dc_second=dc_second,
-                rest_first=rest_first, rest_second=rest_second, bias1=float(bias1),
-                bias2_sqrt=float(bias2_sqrt))
+    state = dict(dc=dc, rest=rest, dc_first=dc_first, dc_second=dc_second,
+                 rest_first=rest_first, rest_second=rest_second, bias1=float(bias1),
+                 bias2_sqrt=float(bias2_sqrt))
+    if xyz is not None:
+        # The positions' Adam in the same kernel: means3D is updated in place.
+        for t in (means3D, xyz["first"], xyz["second"]):
+            _check(t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+                   and t.device == means3D.device and t.numel() == 3 * P,
+                   "positions and their moments must be contiguous CUDA float32 [P, 3]")
+        _check_disjoint([means3D, xyz["first"], xyz["second"], dc, rest, dc_first,
+                         dc_second, rest_first, rest_second],
+                        "positions, their moments and the SH buffers must be disjoint")
+        state["xyz"] = dict(first=xyz["first"], second=xyz["second"],
+                            rate=float(xyz["rate"]), bias1=float(xyz["bias1"]),
+                            bias2_sqrt=float(xyz["bias2_sqrt"]))
+    return state
 
 
 def rasterize_gaussians_backward_consume(bg, means3D, radii, colors, opacities, scales,
@@ -248,10 +267,10 @@ def rasterize_gaussians_backward_consume(bg, means3D, radii, colors, opacities, 
                                          dL_dout_invdepth, sh, degree, campos, geomBuffer, R,
                                          binningBuffer, imageBuffer, antialiasing, debug, dc,
                                          rest, dc_first, dc_second, rest_first, rest_second,
-                                         bias1, bias2_sqrt):
+                                         bias1, bias2_sqrt, *, xyz=None):
     _check(sh.dim() == 3 and sh.shape[1] == MAX_SH_COEFFS, "unsupported SH layout")
     consume = _consume_state(means3D, degree, dc, rest, dc_first, dc_second, rest_first,
-                             rest_second, bias1, bias2_sqrt)
+                             rest_second, bias1, bias2_sqrt, xyz)
     return _backward(bg, means3D, radii, colors, opacities, scales, rotations, scale_modifier,
                      cov3D_precomp, viewmatrix, projmatrix, tanfovx, tanfovy, dL_dout_color,
                      dL_dout_invdepth, sh.contiguous(), None, None, degree, campos, geomBuffer,
@@ -265,13 +284,13 @@ def rasterize_gaussians_backward_consume_direct(bg, means3D, radii, colors, opac
                                                 campos, geomBuffer, R, binningBuffer,
                                                 imageBuffer, antialiasing, debug, dc, rest,
                                                 dc_first, dc_second, rest_first, rest_second,
-                                                bias1, bias2_sqrt):
+                                                bias1, bias2_sqrt, *, xyz=None):
     _check_direct(means3D, dc, rest, degree)
     _check(sh.numel() == 0, "direct input path needs no coefficient snapshot")
     _check_disjoint([dc, rest, dc_first, dc_second, rest_first, rest_second],
                     "direct SH coefficient and moment buffers must be disjoint")
     consume = _consume_state(means3D, degree, dc, rest, dc_first, dc_second, rest_first,
-                             rest_second, bias1, bias2_sqrt)
+                             rest_second, bias1, bias2_sqrt, xyz)
     return _backward(bg, means3D, radii, colors, opacities, scales, rotations, scale_modifier,
                      cov3D_precomp, viewmatrix, projmatrix, tanfovx, tanfovy, dL_dout_color,
                      dL_dout_invdepth, None, dc, rest, degree, campos, geomBuffer, R,

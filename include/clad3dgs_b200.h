@@ -194,6 +194,31 @@ int clad3dgs_gaussian_step_host(
     const float* bias1, const float* bias2, void* workspace_dev,
     size_t workspace_bytes, int64_t chunk_gaussians, cudaStream_t stream);
 
+/* Positions owned by the same pass. No counterpart in the reference, whose
+ * trainer leaves the xyz group to torch's Adam (optimizer_setup.py:5-24): once
+ * the direction adjoint is added, dm is the complete position gradient, so the
+ * kernel also runs torch-fused Adam on means [N][3] in place with the moments
+ * xyz_first / xyz_second, the group's rate xyz_rate (double, the position
+ * schedule's value for this step) and its bias corrections xyz_config, for
+ * every Gaussian. dm is still written. Otherwise as
+ * clad3dgs_sh_consume_split_torch_adam / clad3dgs_gaussian_step; means is read
+ * and written, so it must not alias any other array. */
+int clad3dgs_sh_consume_xyz(
+    int64_t n, int degree, float* means, const int* radii, const float* coefficient,
+    const bool* clamped, const float* camera, const float* seed, float* dm, float* dc,
+    float* rest, float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* xyz_first, float* xyz_second, double xyz_rate,
+    TorchAdamConfig xyz_config, cudaStream_t stream);
+
+int clad3dgs_gaussian_step_xyz(
+    int64_t n, int degree, float* means, const int* radii, const float* coefficient,
+    const bool* clamped, const float* camera, const float* seed, float* dm, float* dc,
+    float* rest, float* dc_first, float* dc_second, float* rest_first, float* rest_second,
+    TorchAdamConfig sh_config, float* const* parameters, const float* const* seeds,
+    const float* const* saved, float* const* first, float* const* second,
+    const double* rates, const float* bias1, const float* bias2, float* xyz_first,
+    float* xyz_second, double xyz_rate, TorchAdamConfig xyz_config, cudaStream_t stream);
+
 /* ============================ rasterizer ============================ */
 
 /* Caller-provided buffer allocation: returns device memory of `bytes` for
@@ -236,6 +261,9 @@ int clad3dgs_raster_render_backward(
  * or, with consume_sh, the consumed variant (prepare_native.py:32-93,
  * direct_inputs.py:151-171): the SH adjoint is applied by the fused SH + Adam
  * kernel to dc/rest and both moments in place instead of being written to dsh.
+ * With consume_sh and xyz_first non-null the same kernel also runs the
+ * positions' Adam (clad3dgs_sh_consume_xyz): means are updated in place after
+ * the geometry backward has read them; xyz_* are ignored otherwise.
  * Outputs are accumulated into zeroed tensors; dconic_scratch [P][4] and
  * dinvdepth_scratch [P] are zeroed scratch. */
 int clad3dgs_raster_backward(
@@ -250,7 +278,8 @@ int clad3dgs_raster_backward(
     float* dcov3d, float* dsh, float* dscales, float* drotations, float* dconic_scratch,
     float* dinvdepth_scratch, int mode, int consume_sh, float* dc, float* rest,
     float* dc_first, float* dc_second, float* rest_first, float* rest_second,
-    TorchAdamConfig config, cudaStream_t stream);
+    TorchAdamConfig config, float* xyz_first, float* xyz_second, double xyz_rate,
+    TorchAdamConfig xyz_config, cudaStream_t stream);
 
 /* Binning + compositing of already projected 2D Gaussians (mean2d [P][2] px,
  * conic_opacity [P][4], rgb [P][3], depth [P], radii [P]); fills the buffers

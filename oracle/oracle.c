@@ -21,6 +21,7 @@
  *   scale/opacity VJP ... controls/ManualActivations.cu:94-100
  *   activation Adam ..... normalization.cu:70-77
  *   reference loss / FD . SHGradientConsumer.cu:404-433, 498-520
+ *   position Adam ....... torch fused Adam on xyz with dm as gradient
  *   shard update ........ the data-parallel exchange: rank-ordered gradient
  *                         sum, the activation VJPs and torch fused Adam above
  *
@@ -271,6 +272,15 @@ void oracle_activation_consume(int64_t n, float* const* params,
     torch_adam(params[2] + i, first[2] + i, second[2] + i,
                (a * (1.f - a)) * seeds[2][i], step[2], bias2[2]);
   }
+}
+
+/* Torch-fused Adam on positions [n][3] with dm as the gradient (no reference
+ * counterpart; the same update as torch_adam above, every element). */
+void oracle_xyz_adam(int64_t n, float* means, const float* dm, float* first,
+                     float* second, double rate, float bias1, float bias2) {
+  const float step = (float)(rate / (double)bias1);
+  for (int64_t e = 0; e < 3 * n; ++e)
+    torch_adam(means + e, first + e, second + e, dm[e], step, bias2);
 }
 
 /* Data-parallel exchange + update of the Gaussians [begin, end) (no

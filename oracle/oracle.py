@@ -94,6 +94,13 @@ def activation_consume(params, seeds, saved, first, second, rates, bias1, bias2)
         (ctypes.c_float * 3)(*[float(b) for b in bias2]))
 
 
+def xyz_adam(means, dm, first, second, rate, bias1, bias2):
+    """Torch-fused Adam on positions in place (float32 numpy arrays)."""
+    lib().oracle_xyz_adam(ctypes.c_int64(means.shape[0]), _p(means), _p(dm), _p(first),
+                          _p(second), ctypes.c_double(rate), ctypes.c_float(bias1),
+                          ctypes.c_float(bias2))
+
+
 SHARD_WIDTHS = (3, 48, 3, 4, 1)  # xyz, sh, scaling, rotation, opacity
 
 

@@ -105,7 +105,9 @@ def _state(model):
     return out
 
 
-def test_consumed_training_step_matches_native(cuda, tmp_path):
+@pytest.mark.parametrize("position", [False, True])
+def test_consumed_training_step_matches_native(cuda, tmp_path, position):
+    """With `position` the xyz group is consumed too (integration.POSITION)."""
     import clad_quaternion
     import integration
     import rasterizer
@@ -124,6 +126,7 @@ def test_consumed_training_step_matches_native(cuda, tmp_path):
     consumed, native = make_model(scene, cuda), make_model(scene, cuda)
     integration.ACTIVATION_EXTENSION = clad_quaternion
     integration.TRACE = str(tmp_path / "trace.json")
+    integration.POSITION = position
     try:
         with RoutingSummary(tmp_path / "routing.json", dict(test=True)) as summary:
             integration.SUMMARY = summary
@@ -131,10 +134,16 @@ def test_consumed_training_step_matches_native(cuda, tmp_path):
         integration.SUMMARY = None
         integration.TRACE = None
         train_step(native, settings, target, 7, enabled=False)
+        consumer = consumed._clad_consumer
+        assert consumer.position_reason is None or not position, consumer.position_reason
     finally:
         integration.SUMMARY = integration.TRACE = None
         integration.ACTIVATION_EXTENSION = None
+        integration.POSITION = False
     torch.cuda.synchronize()
+    if position:
+        # The kernel updated xyz, so the optimizer never saw a position gradient.
+        assert consumed._xyz.grad is None
     routing = json.loads((tmp_path / "routing.json").read_text())
     assert routing["status"] == "completed"
     assert routing["sh"]["consumed_steps"] == 1 and routing["activations"]["consumed_steps"] == 1
