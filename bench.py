@@ -57,6 +57,8 @@ def parse():
                     help="pixel-backward: the 1920x1080, 3M-Gaussian rasterizer pixel "
                          "backward configuration (timed for all accumulation modes)")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-chunk", type=int, default=131072,
+                    help="Gaussians per host-buffer chunk (a multiple of 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS,
@@ -368,7 +370,7 @@ def e2e_measurement(args, device, consume):
     act = {k: ([x.cpu().pin_memory() for x in v] if k != "rates" else v)
            for k, v in s["act"].items()}
     del s
-    chunk = 65536
+    chunk = args.e2e_chunk
     ws = torch.empty(consume.host_step_workspace(chunk), dtype=torch.uint8, device=device)
 
     def one(t):
@@ -396,8 +398,8 @@ def e2e_measurement(args, device, consume):
             "h2d_bytes_per_step": H2D_BYTES_PER_GAUSSIAN * N_GAUSSIANS + 12,
             "d2h_bytes_per_step": D2H_BYTES_PER_GAUSSIAN * N_GAUSSIANS,
             "steps": steps, "ms_per_step": ms / steps,
-            "path": "clad3dgs_gaussian_step_host (C ABI), pinned host buffers, 64K-Gaussian "
-                    "chunks on 3 streams"}
+            "path": f"clad3dgs_gaussian_step_host (C ABI), pinned host buffers, {chunk:,}-"
+                    "Gaussian chunks on 3 streams"}
 
 
 def reference_arm(args):
