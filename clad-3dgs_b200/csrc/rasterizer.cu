@@ -773,6 +773,16 @@ __global__ void preprocess_backward_kernel(
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
   if (radii[i] <= 0) {
+    // Outputs this kernel writes outright are zero for invisible Gaussians
+    // (dmeans, accumulated with +=, and dopacity are left to the caller).
+#pragma unroll
+    for (int k = 0; k < 6; ++k) o.dcov3d[6 * i + k] = 0.f;
+    if (!cov3d_precomp) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) o.dscales[3 * i + k] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o.drotations[4 * i + k] = 0.f;
+    }
     return;
   }
   const Vec3 p{means[3 * i], means[3 * i + 1], means[3 * i + 2]};

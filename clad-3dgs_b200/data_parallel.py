@@ -271,6 +271,12 @@ class ShardedAdam:
     def zero_grad(self):
         self.grad_slab.zero_()
 
+    def zero_accumulated(self):
+        """Zeroes only the gradient arrays the rasterizer backward accumulates
+        into (positions, opacity); it writes the others outright."""
+        self.grads["xyz"].zero_()
+        self.grads["opacity"].zero_()
+
     def _barrier(self):
         dist.all_reduce(self._flag, group=self.group)
 
@@ -381,8 +387,7 @@ class DataParallelTrainer:
         dev = self.adam.device
         self.bg = torch.tensor(bg, dtype=torch.float32, device=dev)
         z = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)
-        self.scratch_grads = dict(mean2d=z(n, 3), colors=z(n, 3), cov=z(n, 6), conic=z(n, 4),
-                                  invdepth=z(n, 1))
+        self.scratch_grads = dict(mean2d=z(n, 3), colors=z(n, 3), cov=z(n, 6), conic=z(n, 4))
         self.radii = torch.zeros(n, dtype=torch.int32, device=dev)
         self.loss = z(1)
         self.buffers = _Scratch(dev)
@@ -407,10 +412,12 @@ class DataParallelTrainer:
             self.image = torch.empty(3, H, W, dtype=torch.float32, device=a.device)
             self.dimage = torch.empty_like(self.image)
             self.invdepth = torch.empty(1, H, W, dtype=torch.float32, device=a.device)
-            self.dinvdepth = torch.zeros(1, H, W, dtype=torch.float32, device=a.device)
-        a.zero_grad()
-        for t in self.scratch_grads.values():
-            t.zero_()
+        # Only atomically accumulated arrays need clearing: the positions'
+        # and opacity gradients and the pixel backward's per-Gaussian targets
+        # (the SH, scale, rotation and covariance adjoints are written outright).
+        a.zero_accumulated()
+        for name in ("mean2d", "colors", "conic"):
+            self.scratch_grads[name].zero_()
         self.loss.zero_()
         act = a.activate()
         p = a.params
@@ -435,13 +442,13 @@ class DataParallelTrainer:
             None, act["opacity"].data_ptr(), act["scaling"].data_ptr(), 1.0,
             act["rotation"].data_ptr(), None, camera.view.data_ptr(), camera.proj.data_ptr(),
             camera.tan_x, camera.tan_y, H, W, self.dimage.data_ptr(),
-            self.dinvdepth.data_ptr(), p["sh"].data_ptr(), None, None,
+            None, p["sh"].data_ptr(), None, None,
             camera.campos.data_ptr(), geom.data_ptr(), rendered.value,
             binning.data_ptr() if binning is not None else None, image.data_ptr(), 0,
             s["mean2d"].data_ptr(), s["colors"].data_ptr(), g["opacity"].data_ptr(),
             g["xyz"].data_ptr(), s["cov"].data_ptr(), g["sh"].data_ptr(),
             g["scaling"].data_ptr(), g["rotation"].data_ptr(), s["conic"].data_ptr(),
-            s["invdepth"].data_ptr(), self.mode, 0, None, None, None, None, None, None,
+            None, self.mode, 0, None, None, None, None, None, None,
             native.TorchAdamConfig(1.0, 1.0), None, None, 0.0, native.TorchAdamConfig(1.0, 1.0),
             stream), "rasterize (backward)")
         return self.loss, rendered.value
