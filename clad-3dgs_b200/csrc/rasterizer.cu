@@ -748,6 +748,167 @@ __global__ void __launch_bounds__(kTilePixels)
   }
 }
 
+// Mode 2 with two pixels per thread: rows y and y + 8 of the tile. A thread
+// keeps both pixels' back-to-front state; per Gaussian it adds the two pixels'
+// adjoints before the warp reduction, so each reduction covers 64 pixels.
+constexpr int kPairThreads = kTilePixels / 2;
+
+struct PixelState {
+  bool inside;
+  float fx, fy, T, T_final, dpix[3], dinv, bg_dot;
+  uint32_t last, contributor;
+  float acc[3], acc_inv, last_alpha, last_rgb[3], last_inv;
+};
+
+__device__ __forceinline__ void pixel_setup(PixelState& s, int px, int py, int width,
+                                            int height, const float* __restrict__ final_t,
+                                            const uint32_t* __restrict__ n_contrib,
+                                            const float* __restrict__ dpixels,
+                                            const float* __restrict__ dinvdepth_pixels,
+                                            const float* __restrict__ bg) {
+  s.inside = px < width && py < height;
+  const int pix = py * width + px, hw = width * height;
+  s.fx = (float)px;
+  s.fy = (float)py;
+  s.T_final = s.inside ? final_t[pix] : 0.f;
+  s.T = s.T_final;
+  s.last = s.inside ? n_contrib[pix] : 0;
+  s.dpix[0] = s.dpix[1] = s.dpix[2] = 0.f;
+  s.dinv = 0.f;
+  if (s.inside) {
+    s.dpix[0] = dpixels[pix];
+    s.dpix[1] = dpixels[hw + pix];
+    s.dpix[2] = dpixels[2 * hw + pix];
+    if (dinvdepth_pixels) s.dinv = dinvdepth_pixels[pix];
+  }
+  s.bg_dot = bg[0] * s.dpix[0] + bg[1] * s.dpix[1] + bg[2] * s.dpix[2];
+  s.acc[0] = s.acc[1] = s.acc[2] = 0.f;
+  s.acc_inv = 0.f;
+  s.last_alpha = 0.f;
+  s.last_rgb[0] = s.last_rgb[1] = s.last_rgb[2] = 0.f;
+  s.last_inv = 0.f;
+}
+
+// One (pixel, Gaussian) step of the walk: the same arithmetic as the one-pixel
+// kernel, adding the pixel's ten adjoints into f; returns whether it contributed.
+__device__ __forceinline__ bool pixel_step(PixelState& s, float2 xy, float4 co,
+                                           const float* rgb3, float inv, float ddx,
+                                           float ddy, float f[16]) {
+  --s.contributor;
+  bool contrib = s.inside && s.contributor < s.last;
+  const float dx = xy.x - s.fx, dy = xy.y - s.fy;
+  const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
+  contrib = contrib && power <= 0.f;
+  const float G = __expf(power);
+  const float alpha = fminf(kMaxAlpha, co.w * G);
+  contrib = contrib && alpha >= kMinAlpha;
+  if (contrib) {
+    const float inv_keep = 1.f / (1.f - alpha);
+    s.T = s.T * inv_keep;
+    const float w = alpha * s.T;
+    float dl_dalpha = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const float cc = rgb3[ch];
+      s.acc[ch] = s.last_alpha * s.last_rgb[ch] + (1.f - s.last_alpha) * s.acc[ch];
+      s.last_rgb[ch] = cc;
+      dl_dalpha += (cc - s.acc[ch]) * s.dpix[ch];
+      f[ch] += w * s.dpix[ch];
+    }
+    s.acc_inv = s.last_alpha * s.last_inv + (1.f - s.last_alpha) * s.acc_inv;
+    s.last_inv = inv;
+    dl_dalpha += (inv - s.acc_inv) * s.dinv;
+    f[9] += w * s.dinv;
+    dl_dalpha *= s.T;
+    s.last_alpha = alpha;
+    dl_dalpha += (-s.T_final * inv_keep) * s.bg_dot;
+    const float dl_dg = co.w * dl_dalpha;
+    const float gdx = G * dx, gdy = G * dy;
+    const float dg_ddx = -gdx * co.x - gdy * co.y;
+    const float dg_ddy = -gdy * co.z - gdx * co.y;
+    f[3] += dl_dg * dg_ddx * ddx;
+    f[4] += dl_dg * dg_ddy * ddy;
+    f[5] += -0.5f * gdx * dx * dl_dg;
+    f[6] += -0.5f * gdx * dy * dl_dg;
+    f[7] += -0.5f * gdy * dy * dl_dg;
+    f[8] += G * dl_dalpha;
+  }
+  return contrib;
+}
+
+__global__ void __launch_bounds__(kPairThreads)
+    render_backward_pairs_kernel(const uint2* __restrict__ ranges,
+                                 const uint32_t* __restrict__ point_list, int width,
+                                 int height, int grid_x, const float* __restrict__ bg,
+                                 const float2* __restrict__ mean2d,
+                                 const float4* __restrict__ conic_opacity,
+                                 const float* __restrict__ rgb, const float* __restrict__ depth,
+                                 const float* __restrict__ final_t,
+                                 const uint32_t* __restrict__ n_contrib,
+                                 const float* __restrict__ dpixels,
+                                 const float* __restrict__ dinvdepth_pixels, PixelGrads out) {
+  const int tile = blockIdx.y * grid_x + blockIdx.x;
+  const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
+  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;  // rows 0..7 of the tile
+  const int lane = threadIdx.x & 31;
+  const uint2 range = ranges[tile];
+  __shared__ uint32_t s_id[kBatch];
+  __shared__ uint32_t s_last_max;
+  __shared__ float2 s_xy[kBatch];
+  __shared__ float4 s_co[kBatch];
+  __shared__ float s_rgb[3 * kBatch];
+  __shared__ float s_inv[kBatch];
+  PixelState a, b;
+  pixel_setup(a, px, py, width, height, final_t, n_contrib, dpixels, dinvdepth_pixels, bg);
+  pixel_setup(b, px, py + kTileY / 2, width, height, final_t, n_contrib, dpixels,
+              dinvdepth_pixels, bg);
+  // Start at the tile's largest last-contributor index (see the one-pixel kernel).
+  if (threadIdx.x == 0) s_last_max = 0;
+  __syncthreads();
+  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, max(a.last, b.last));
+  if (lane == 0) atomicMax(&s_last_max, warp_max);
+  __syncthreads();
+  const int todo = int(s_last_max);
+  a.contributor = b.contributor = todo;
+  const float ddx = 0.5f * width, ddy = 0.5f * height;
+  const int nf = out.dinvdepth ? 10 : 9;
+  for (int base = 0; base < todo; base += kBatch) {
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int slot = threadIdx.x + h * kPairThreads;
+      const int k = base + slot;
+      if (k < todo) {
+        const uint32_t id = point_list[range.x + todo - k - 1];
+        s_id[slot] = id;
+        s_xy[slot] = mean2d[id];
+        s_co[slot] = conic_opacity[id];
+        s_rgb[3 * slot] = rgb[3 * id];
+        s_rgb[3 * slot + 1] = rgb[3 * id + 1];
+        s_rgb[3 * slot + 2] = rgb[3 * id + 2];
+        s_inv[slot] = 1.f / depth[id];
+      }
+    }
+    __syncthreads();
+    const int count = min(kBatch, todo - base);
+    for (int j = 0; j < count; ++j) {
+      float f[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) f[q] = 0.f;
+      const float2 xy = s_xy[j];
+      const float4 co = s_co[j];
+      const float* rgb3 = s_rgb + 3 * j;
+      const float inv = s_inv[j];
+      const bool ca = pixel_step(a, xy, co, rgb3, inv, ddx, ddy, f);
+      const bool cb = pixel_step(b, xy, co, rgb3, inv, ddx, ddy, f);
+      if (!__any_sync(0xffffffffu, ca || cb)) continue;
+      const float total = transpose_reduce(f, lane);
+      const int q = (lane >> 1) & 15;
+      if ((lane & 1) == 0 && q < nf) atomicAdd(field_address(out, s_id[j], q), total);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Geometry backward: one thread per Gaussian.
 
@@ -1179,7 +1340,7 @@ extern "C" int clad3dgs_raster_render_backward(
         img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   else
-    render_backward_kernel<2><<<grid, kTilePixels, 0, stream>>>(
+    render_backward_pairs_kernel<<<grid, kPairThreads, 0, stream>>>(
         img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   return status_of(cudaPeekAtLastError(), "pixel backward");
