@@ -748,10 +748,15 @@ __global__ void __launch_bounds__(kTilePixels)
   }
 }
 
-// Mode 2 with two pixels per thread: rows y and y + 8 of the tile. A thread
-// keeps both pixels' back-to-front state; per Gaussian it adds the two pixels'
-// adjoints before the warp reduction, so each reduction covers 64 pixels.
-constexpr int kPairThreads = kTilePixels / 2;
+// Mode 2 with kPixelsPerThread pixels per thread: rows y, y + 16/k, ... of the
+// tile. A thread keeps every pixel's back-to-front state; per Gaussian it adds
+// its pixels' adjoints before the warp reduction, so each reduction covers
+// 32 k pixels.
+#ifndef CLAD3DGS_PIXELS_PER_THREAD
+#define CLAD3DGS_PIXELS_PER_THREAD 4
+#endif
+constexpr int kPixelsPerThread = CLAD3DGS_PIXELS_PER_THREAD;
+constexpr int kPairThreads = kTilePixels / kPixelsPerThread;
 
 struct PixelState {
   bool inside;
@@ -849,7 +854,7 @@ __global__ void __launch_bounds__(kPairThreads)
                                  const float* __restrict__ dinvdepth_pixels, PixelGrads out) {
   const int tile = blockIdx.y * grid_x + blockIdx.x;
   const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
-  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;  // rows 0..7 of the tile
+  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;  // first row of this thread
   const int lane = threadIdx.x & 31;
   const uint2 range = ranges[tile];
   __shared__ uint32_t s_id[kBatch];
@@ -858,24 +863,29 @@ __global__ void __launch_bounds__(kPairThreads)
   __shared__ float4 s_co[kBatch];
   __shared__ float s_rgb[3 * kBatch];
   __shared__ float s_inv[kBatch];
-  PixelState a, b;
-  pixel_setup(a, px, py, width, height, final_t, n_contrib, dpixels, dinvdepth_pixels, bg);
-  pixel_setup(b, px, py + kTileY / 2, width, height, final_t, n_contrib, dpixels,
-              dinvdepth_pixels, bg);
+  PixelState st[kPixelsPerThread];
+  uint32_t my_last = 0;
+#pragma unroll
+  for (int r = 0; r < kPixelsPerThread; ++r) {
+    pixel_setup(st[r], px, py + r * (kTileY / kPixelsPerThread), width, height, final_t,
+                n_contrib, dpixels, dinvdepth_pixels, bg);
+    my_last = max(my_last, st[r].last);
+  }
   // Start at the tile's largest last-contributor index (see the one-pixel kernel).
   if (threadIdx.x == 0) s_last_max = 0;
   __syncthreads();
-  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, max(a.last, b.last));
+  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, my_last);
   if (lane == 0) atomicMax(&s_last_max, warp_max);
   __syncthreads();
   const int todo = int(s_last_max);
-  a.contributor = b.contributor = todo;
+#pragma unroll
+  for (int r = 0; r < kPixelsPerThread; ++r) st[r].contributor = todo;
   const float ddx = 0.5f * width, ddy = 0.5f * height;
   const int nf = out.dinvdepth ? 10 : 9;
   for (int base = 0; base < todo; base += kBatch) {
     __syncthreads();
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < kPixelsPerThread; ++h) {
       const int slot = threadIdx.x + h * kPairThreads;
       const int k = base + slot;
       if (k < todo) {
@@ -899,9 +909,11 @@ __global__ void __launch_bounds__(kPairThreads)
       const float4 co = s_co[j];
       const float* rgb3 = s_rgb + 3 * j;
       const float inv = s_inv[j];
-      const bool ca = pixel_step(a, xy, co, rgb3, inv, ddx, ddy, f);
-      const bool cb = pixel_step(b, xy, co, rgb3, inv, ddx, ddy, f);
-      if (!__any_sync(0xffffffffu, ca || cb)) continue;
+      bool any = false;
+#pragma unroll
+      for (int r = 0; r < kPixelsPerThread; ++r)
+        any = pixel_step(st[r], xy, co, rgb3, inv, ddx, ddy, f) || any;
+      if (!__any_sync(0xffffffffu, any)) continue;
       const float total = transpose_reduce(f, lane);
       const int q = (lane >> 1) & 15;
       if ((lane & 1) == 0 && q < nf) atomicAdd(field_address(out, s_id[j], q), total);
