@@ -73,7 +73,7 @@ _SIGNATURES = {
                                                    _P]),
     "clad3dgs_raster_geom_bytes": (c_size_t, [c_int]),
     "clad3dgs_raster_image_bytes": (c_size_t, [c_int, c_int]),
-    "clad3dgs_raster_binning_bytes": (c_size_t, [c_int]),
+    "clad3dgs_raster_binning_bytes": (c_size_t, [c_int] * 4),
     "clad3dgs_raster_forward": (c_int, [c_int, c_int] + [_P] * 5 + [c_float] + [_P] * 4
                                 + [c_float, c_float, c_int, c_int] + [_P] * 4
                                 + [c_int, _P, _P, _P, _P, _P, POINTER(c_int), _P]),

@@ -4,9 +4,10 @@
 //
 // Pipeline (forward): preprocess (one thread per Gaussian: camera transform,
 // 3D covariance from scale and rotation, EWA screen covariance, conic, radius,
-// tiles touched, SH colour and its clamp flags) -> inclusive scan of tiles
-// touched -> one (tile << 32 | depth) key per touched tile -> radix sort ->
-// per-tile ranges -> compositing (one 16x16 CTA per tile, Gaussians staged in
+// the tiles its alpha >= 1/255 footprint reaches, SH colour and its clamp
+// flags) -> depth order -> per-tile lists of Gaussian ids in depth order,
+// built from (tile row, depth rank) pairs without sorting per-instance keys
+// (see "Binning") -> compositing (one 16x16 CTA per tile, Gaussians staged in
 // shared memory in batches of 256).
 //
 // Pixel backward: the same traversal back to front, starting at the tile's
@@ -65,8 +66,10 @@ struct GeomState {
   float* cov3d;          // [P][6]
   float4* conic_opacity; // conic (a, b, c), opacity x antialias factor
   float* rgb;            // [P][3]
-  uint32_t* tiles;       // tiles touched
-  uint32_t* offsets;     // inclusive scan of tiles touched, in depth order
+  uint32_t* tiles;       // tiles touched (footprint)
+  uint32_t* rows;        // rows of the tile rectangle (0 without tiles)
+  uint32_t* offsets;     // inclusive scan of rows, in depth order
+  uint32_t* totals;      // [2]: tile instances, row pairs
   uint32_t* depth_keys;  // depth bits (then tiles touched in depth order)
   uint32_t* ids;         // 0..P-1
   uint32_t* depth_sorted;
@@ -78,9 +81,10 @@ struct GeomState {
 };
 
 size_t scan_temp_bytes(int P) {
-  size_t bytes = 0;
-  cub::DeviceScan::InclusiveSum(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr, P);
-  return bytes;
+  size_t scan = 0, sum = 0;
+  cub::DeviceScan::InclusiveSum(nullptr, scan, (uint32_t*)nullptr, (uint32_t*)nullptr, P);
+  cub::DeviceReduce::Sum(nullptr, sum, (uint32_t*)nullptr, (uint32_t*)nullptr, P);
+  return scan > sum ? scan : sum;
 }
 
 size_t order_temp_bytes(int P) {
@@ -99,7 +103,7 @@ size_t geom_bytes(int P) {
   s += aligned<float>(sizeof(float) * 6 * P);
   s += aligned<float4>(sizeof(float4) * P);
   s += aligned<float>(sizeof(float) * 3 * P);
-  s += 6 * aligned<uint32_t>(sizeof(uint32_t) * P);
+  s += 7 * aligned<uint32_t>(sizeof(uint32_t) * P) + aligned<uint32_t>(8);
   s += aligned<char>(scan_temp_bytes(P));
   s += aligned<char>(order_temp_bytes(P));
   return s + 128;
@@ -121,7 +125,9 @@ GeomState geom_from(char* base, int P) {
   g.conic_opacity = reinterpret_cast<float4*>(take(sizeof(float4) * P));
   g.rgb = reinterpret_cast<float*>(take(sizeof(float) * 3 * P));
   g.tiles = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.rows = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
   g.offsets = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
+  g.totals = reinterpret_cast<uint32_t*>(take(8));
   g.depth_keys = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
   g.ids = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
   g.depth_sorted = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * P));
@@ -155,38 +161,84 @@ ImageState image_from(char* base, int pixels, int tiles) {
   return s;
 }
 
-// Tile instances: tile id keys and Gaussian id values, before and after the
-// stable sort by tile.
+// Binning buffer: the point list (Gaussian ids grouped by tile, in depth order)
+// first, so the backward finds it at the start; then the forward's scratch.
 struct BinningState {
-  uint32_t* keys_unsorted;
-  uint32_t* values_unsorted;
-  uint32_t* keys;
-  uint32_t* values;
+  uint32_t* values;          // [n]
+  uint32_t* pair_rows;       // [m] row pairs: key tile row, value packed span
+  uint32_t* pair_rows_sorted;
+  uint64_t* pair_spans;
+  uint64_t* pair_spans_sorted;
   void* sort_tmp;
   size_t sort_bytes;
+  uint32_t* row_start;       // [grid_y + 1]
+  uint32_t* chunk_first;     // [grid_y + 1]
+  uint32_t* chunk_counts;    // [max_chunks][grid_x]
+  uint32_t* tile_total;      // [tiles]
+  uint32_t* tile_start;      // [tiles]
+  void* scan_tmp;
+  size_t scan_bytes;
+  uint32_t max_chunks;
 };
 
-size_t sort_temp_bytes(int n) {
+// Row pairs per chunk of the binning passes.
+constexpr int kRowChunk = 2048;
+
+uint32_t max_chunks(uint32_t m, int grid_y) {
+  return m / uint32_t(kRowChunk) + uint32_t(grid_y) + 1u;
+}
+
+size_t pair_sort_bytes(uint32_t m) {
   size_t bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr,
-                                  (uint32_t*)nullptr, (uint32_t*)nullptr, n, 0, 32);
+                                  (uint64_t*)nullptr, (uint64_t*)nullptr, int(m), 0, 32);
   return bytes;
 }
 
-size_t binning_bytes(int n) {
-  return 4 * aligned<uint32_t>(4 * size_t(n)) + aligned<char>(sort_temp_bytes(n)) + 128;
+size_t tile_scan_bytes(int tiles) {
+  size_t bytes = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, bytes, (uint32_t*)nullptr, (uint32_t*)nullptr, tiles);
+  return bytes;
 }
 
-BinningState binning_from(char* base, int n) {
+size_t binning_bytes(uint32_t n, uint32_t m, int grid_x, int grid_y) {
+  const int tiles = grid_x * grid_y;
+  return aligned<uint32_t>(4 * size_t(n)) + 2 * aligned<uint32_t>(4 * size_t(m)) +
+         2 * aligned<uint64_t>(8 * size_t(m)) +
+         aligned<char>(pair_sort_bytes(m)) + 2 * aligned<uint32_t>(4 * size_t(grid_y + 1)) +
+         aligned<uint32_t>(4 * size_t(max_chunks(m, grid_y)) * grid_x) +
+         2 * aligned<uint32_t>(4 * size_t(tiles)) + aligned<char>(tile_scan_bytes(tiles)) + 128;
+}
+
+uint32_t* point_list_from(const void* base) {
+  return reinterpret_cast<uint32_t*>((reinterpret_cast<uintptr_t>(base) + 127) &
+                                     ~uintptr_t(127));
+}
+
+BinningState binning_from(char* base, uint32_t n, uint32_t m, int grid_x, int grid_y) {
   BinningState b;
-  char* c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(base) + 127) & ~uintptr_t(127));
-  uint32_t** arrays[4] = {&b.keys_unsorted, &b.keys, &b.values_unsorted, &b.values};
-  for (uint32_t** a : arrays) {
-    *a = reinterpret_cast<uint32_t*>(c);
-    c += aligned<uint32_t>(4 * size_t(n));
-  }
-  b.sort_tmp = c;
-  b.sort_bytes = sort_temp_bytes(n);
+  const int tiles = grid_x * grid_y;
+  char* c = reinterpret_cast<char*>(point_list_from(base));
+  auto take = [&](size_t bytes) {
+    char* r = c;
+    c += aligned<char>(bytes);
+    return r;
+  };
+  b.values = reinterpret_cast<uint32_t*>(take(4 * size_t(n)));
+  b.pair_rows = reinterpret_cast<uint32_t*>(take(4 * size_t(m)));
+  b.pair_rows_sorted = reinterpret_cast<uint32_t*>(take(4 * size_t(m)));
+  b.pair_spans = reinterpret_cast<uint64_t*>(take(8 * size_t(m)));
+  b.pair_spans_sorted = reinterpret_cast<uint64_t*>(take(8 * size_t(m)));
+  b.sort_bytes = pair_sort_bytes(m);
+  b.sort_tmp = take(b.sort_bytes);
+  b.row_start = reinterpret_cast<uint32_t*>(take(4 * size_t(grid_y + 1)));
+  b.chunk_first = reinterpret_cast<uint32_t*>(take(4 * size_t(grid_y + 1)));
+  b.max_chunks = max_chunks(m, grid_y);
+  b.chunk_counts = reinterpret_cast<uint32_t*>(take(4 * size_t(b.max_chunks) * grid_x));
+  b.tile_total = reinterpret_cast<uint32_t*>(take(4 * size_t(tiles)));
+  b.tile_start = reinterpret_cast<uint32_t*>(take(4 * size_t(tiles)));
+  b.scan_bytes = tile_scan_bytes(tiles);
+  b.scan_tmp = take(b.scan_bytes);
   return b;
 }
 
@@ -275,6 +327,7 @@ __global__ void preprocess_kernel(int P, int degree, const float* __restrict__ m
   if (i >= P) return;
   g.radii[i] = 0;
   g.tiles[i] = 0;
+  g.rows[i] = 0;
   radii_out[i] = 0;
   const Vec3 p{means[3 * i], means[3 * i + 1], means[3 * i + 2]};
   const Vec3 t = affine3(cam.view, p);
@@ -338,14 +391,33 @@ __global__ void preprocess_kernel(int P, int degree, const float* __restrict__ m
   g.conic_opacity[i] = co;
   // Instances only for the tiles some pixel of which the Gaussian can reach
   // (see Footprint); the radius and everything else keep the 3-sigma rule.
-  g.tiles[i] = footprint_tiles(make_footprint(px, py, co, radius, cam.grid_x, cam.grid_y));
+  const Footprint f = make_footprint(px, py, co, radius, cam.grid_x, cam.grid_y);
+  const uint32_t n = footprint_tiles(f);
+  g.tiles[i] = n;
+  g.rows[i] = n ? uint32_t(f.y1 - f.y0) : 0u;
 }
 
-// Binning. The Gaussians are first ordered by depth (a stable sort of P
-// depth keys), each Gaussian then writes its tile instances in that order, and
-// the instances are stable-sorted by tile id alone: within a tile they come out
-// by depth, ties by Gaussian index, the order a stable sort of
-// (tile << 32 | depth) keys gives, for a fraction of the sort traffic.
+// Binning. Every tile's instance list is its Gaussians in depth order (ties by
+// Gaussian index), which is what a stable sort of one (tile << 32 | depth) key
+// per instance gives; here no per-instance key is sorted:
+//  1. the Gaussians are ordered by depth (a stable sort of P depth keys);
+//  2. each Gaussian, in depth order, writes one pair per row of its tile
+//     rectangle: key = tile row, value = (Gaussian id, first and one-past-last
+//     tile of its footprint in that row, see Footprint); the pairs are
+//     stable-sorted by row (a 7-bit key at 1080p: one radix pass);
+//  3. each row's pairs are cut into chunks of kRowChunk; a first pass counts
+//     every chunk's instances per tile (difference array in shared memory);
+//  4. per tile the chunk counts become chunk offsets and the tile totals are
+//     scanned into tile starts (and the ranges);
+//  5. a second pass expands each chunk's pairs into their instances, groups
+//     them by tile with a stable block radix sort and writes every tile's run
+//     of Gaussian ids contiguously.
+constexpr int kBinThreads = 256;
+
+__device__ __forceinline__ uint64_t pack_pair(uint32_t id, int lo, int hi) {
+  return uint64_t(id) | (uint64_t(uint32_t(lo)) << 32) | (uint64_t(uint32_t(hi)) << 48);
+}
+
 __global__ void depth_key_kernel(int P, GeomState g) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
@@ -355,111 +427,35 @@ __global__ void depth_key_kernel(int P, GeomState g) {
   g.ids[i] = uint32_t(i);
 }
 
-__global__ void gather_counts_kernel(int P, GeomState g) {
+// Tile-rectangle rows of the Gaussians in depth order (to be scanned).
+__global__ void gather_rows_kernel(int P, GeomState g) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
-  g.depth_keys[i] = g.tiles[g.order[i]];
+  g.depth_keys[i] = g.rows[g.order[i]];
 }
 
-// Tile instances of one Gaussian (footprint f, slots [start, start + cap)),
-// written by the whole warp: the lanes take up to 32 tile rows at a time, each
-// finds its row's span, a warp scan places the spans end to end, and the lanes
-// then write consecutive instances, so the stores coalesce. Warp-uniform
-// control flow throughout (every lane takes part in every shuffle).
-__device__ __forceinline__ void emit_instances(const Footprint& f, uint32_t id, uint32_t cap,
-                                               uint32_t start, int grid_x, int lane,
-                                               uint32_t* keys, uint32_t* values) {
-  uint32_t done = 0;
-  for (int row0 = f.y0; row0 < f.y1; row0 += 32) {
-    const int ty = row0 + lane;
-    int lo = 0, hi = 0;
-    if (ty < f.y1) row_span(f, ty, lo, hi);
-    const uint32_t n = hi > lo ? uint32_t(hi - lo) : 0u;
-    uint32_t incl = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    for (uint32_t base = 0; base < total; base += 32) {
-      const uint32_t j = base + lane;
-      // The row holding instance j: the first lane whose inclusive sum exceeds
-      // j (at most lane 31).
-      int r = 0;
-#pragma unroll
-      for (int step = 16; step > 0; step >>= 1) {
-        const uint32_t probe = __shfl_sync(0xffffffffu, incl, r + step - 1);
-        if (probe <= j) r += step;
-      }
-      const uint32_t r_incl = __shfl_sync(0xffffffffu, incl, r);
-      const uint32_t r_n = __shfl_sync(0xffffffffu, n, r);
-      const int r_lo = __shfl_sync(0xffffffffu, lo, r);
-      const uint32_t x = uint32_t(r_lo) + (j - (r_incl - r_n));
-      if (j < total && done + j < cap) {
-        keys[start + done + j] = uint32_t(row0 + r) * uint32_t(grid_x) + x;
-        values[start + done + j] = id;
-      }
-    }
-    done += total;
-  }
-  // Never past this Gaussian's slots; slots left over (none when the count
-  // and this walk agree, as they do) get a key that sorts after every tile.
-  for (uint32_t k = done + lane; k < cap; k += 32) {
-    keys[start + k] = 0xffffffffu;
-    values[start + k] = id;
+__global__ void emit_rows_kernel(int P, GeomState g, int grid_x, int grid_y,
+                                 uint32_t* __restrict__ rows_out,
+                                 uint64_t* __restrict__ spans_out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  const uint32_t id = g.order[i];
+  const uint32_t n = g.rows[id];
+  if (n == 0) return;
+  const uint32_t start = i == 0 ? 0u : g.offsets[i - 1];
+  const float2 m = g.mean2d[id];
+  const Footprint f = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x,
+                                     grid_y);
+  for (uint32_t r = 0; r < n; ++r) {
+    const int ty = f.y0 + int(r);
+    int lo, hi;
+    row_span(f, ty, lo, hi);
+    if (hi < lo) hi = lo;
+    rows_out[start + r] = uint32_t(ty);
+    spans_out[start + r] = pack_pair(id, lo, hi);
   }
 }
 
-// One warp per 32 consecutive Gaussians of the depth order. Each lane gathers
-// one Gaussian's header (id, slot count, first slot, footprint), so the
-// dependent loads of 32 Gaussians overlap; the warp then emits them one at a
-// time from registers.
-__global__ void duplicate_kernel(int P, GeomState g, int grid_x, int grid_y, uint32_t* keys,
-                                 uint32_t* values) {
-  const int lane = threadIdx.x & 31;
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int base = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; base < P;
-       base += warps * 32) {
-    const int i = base + lane;
-    uint32_t id = 0, cap = 0, start = 0;
-    Footprint mine{};
-    if (i < P) {
-      id = g.order[i];
-      cap = g.tiles[id];
-      if (cap) {
-        start = i == 0 ? 0u : g.offsets[i - 1];
-        const float2 m = g.mean2d[id];
-        mine = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x, grid_y);
-      }
-    }
-    uint32_t pending = __ballot_sync(0xffffffffu, cap != 0);
-    while (pending) {
-      const int src = __ffs(pending) - 1;
-      pending &= pending - 1;
-      Footprint f;
-      f.mx = __shfl_sync(0xffffffffu, mine.mx, src);
-      f.my = __shfl_sync(0xffffffffu, mine.my, src);
-      f.B = __shfl_sync(0xffffffffu, mine.B, src);
-      f.invA = __shfl_sync(0xffffffffu, mine.invA, src);
-      f.at = __shfl_sync(0xffffffffu, mine.at, src);
-      f.detc = __shfl_sync(0xffffffffu, mine.detc, src);
-      f.ymax = __shfl_sync(0xffffffffu, mine.ymax, src);
-      f.dyr = __shfl_sync(0xffffffffu, mine.dyr, src);
-      f.any = __shfl_sync(0xffffffffu, int(mine.any), src) != 0;
-      f.ellipse = __shfl_sync(0xffffffffu, int(mine.ellipse), src) != 0;
-      f.x0 = __shfl_sync(0xffffffffu, mine.x0, src);
-      f.y0 = __shfl_sync(0xffffffffu, mine.y0, src);
-      f.x1 = __shfl_sync(0xffffffffu, mine.x1, src);
-      f.y1 = __shfl_sync(0xffffffffu, mine.y1, src);
-      emit_instances(f, __shfl_sync(0xffffffffu, id, src), __shfl_sync(0xffffffffu, cap, src),
-                     __shfl_sync(0xffffffffu, start, src), grid_x, lane, keys, values);
-    }
-  }
-}
-
-// Per-tile [first, last) instance ranges of the tile-sorted keys: one thread
-// per tile, two binary searches (tiles without instances get an empty range).
 __device__ __forceinline__ uint32_t lower_bound(const uint32_t* keys, uint32_t n,
                                                 uint32_t value) {
   uint32_t lo = 0, hi = n;
@@ -471,12 +467,218 @@ __device__ __forceinline__ uint32_t lower_bound(const uint32_t* keys, uint32_t n
   return lo;
 }
 
-__global__ void ranges_kernel(uint32_t n, int tiles, const uint32_t* __restrict__ keys,
-                              uint2* __restrict__ ranges) {
+// First pair of every tile row (row_start[grid_y] = m) and the first chunk of
+// every row (chunk_first[grid_y] = number of chunks). One block.
+__global__ void row_layout_kernel(uint32_t m, int grid_y, const uint32_t* __restrict__ rows,
+                                  uint32_t* __restrict__ row_start,
+                                  uint32_t* __restrict__ chunk_first) {
+  for (int ty = threadIdx.x; ty <= grid_y; ty += blockDim.x)
+    row_start[ty] = ty == grid_y ? m : lower_bound(rows, m, uint32_t(ty));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t c = 0;
+    for (int ty = 0; ty < grid_y; ++ty) {
+      chunk_first[ty] = c;
+      c += (row_start[ty + 1] - row_start[ty] + kRowChunk - 1) / kRowChunk;
+    }
+    chunk_first[grid_y] = c;
+  }
+}
+
+// The tile row of chunk c: the last row whose first chunk is <= c.
+__device__ __forceinline__ int chunk_row(const uint32_t* chunk_first, int grid_y, uint32_t c) {
+  int lo = 0, hi = grid_y - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (chunk_first[mid] <= c) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kBinThreads)
+    tile_count_kernel(int grid_x, int grid_y, const uint64_t* __restrict__ spans,
+                      const uint32_t* __restrict__ row_start,
+                      const uint32_t* __restrict__ chunk_first,
+                      uint32_t* __restrict__ chunk_counts) {
+  extern __shared__ int diff[];  // grid_x + 1
+  const uint32_t c = blockIdx.x;
+  if (c >= chunk_first[grid_y]) return;  // whole block
+  const int ty = chunk_row(chunk_first, grid_y, c);
+  const uint32_t begin = row_start[ty] + (c - chunk_first[ty]) * kRowChunk;
+  const uint32_t end = min(row_start[ty + 1], begin + kRowChunk);
+  for (int x = threadIdx.x; x <= grid_x; x += blockDim.x) diff[x] = 0;
+  __syncthreads();
+  for (uint32_t p = begin + threadIdx.x; p < end; p += blockDim.x) {
+    const uint64_t v = spans[p];
+    const int lo = int((v >> 32) & 0xffffu), hi = int(v >> 48);
+    if (hi > lo) {
+      atomicAdd(&diff[lo], 1);
+      atomicAdd(&diff[hi], -1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int running = 0;
+    for (int x = 0; x < grid_x; ++x) {
+      running += diff[x];
+      chunk_counts[size_t(c) * grid_x + x] = uint32_t(running);
+    }
+  }
+}
+
+// Per tile: chunk counts -> offsets of each chunk within the tile, and the total.
+__global__ void tile_totals_kernel(int grid_x, int grid_y, const uint32_t* __restrict__ chunk_first,
+                                   uint32_t* __restrict__ chunk_counts,
+                                   uint32_t* __restrict__ tile_total) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= grid_x * grid_y) return;
+  const int ty = t / grid_x, x = t - ty * grid_x;
+  uint32_t running = 0;
+  for (uint32_t c = chunk_first[ty]; c < chunk_first[ty + 1]; ++c) {
+    const uint32_t v = chunk_counts[size_t(c) * grid_x + x];
+    chunk_counts[size_t(c) * grid_x + x] = running;
+    running += v;
+  }
+  tile_total[t] = running;
+}
+
+__global__ void tile_ranges_kernel(int tiles, const uint32_t* __restrict__ tile_start,
+                                   const uint32_t* __restrict__ tile_total,
+                                   uint2* __restrict__ ranges) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= tiles) return;
-  ranges[t] = make_uint2(lower_bound(keys, n, uint32_t(t)),
-                         lower_bound(keys, n, uint32_t(t) + 1));
+  ranges[t] = make_uint2(tile_start[t], tile_start[t] + tile_total[t]);
+}
+
+// Second pass: per chunk, the pairs' instances in pair order (each pair expands
+// to its row span), kPlaceWindow at a time: every thread takes kPlaceItems
+// consecutive instances, a stable block radix sort by tile groups them (pair
+// order kept within a tile), and each tile's run is written contiguously after
+// the runs that earlier windows and chunks wrote.
+#ifndef CLAD3DGS_PLACE_ITEMS
+#define CLAD3DGS_PLACE_ITEMS 8
+#endif
+#ifndef CLAD3DGS_PLACE_BLOCKS
+#define CLAD3DGS_PLACE_BLOCKS 4
+#endif
+constexpr int kPlaceItems = CLAD3DGS_PLACE_ITEMS;
+constexpr int kPlaceWindow = kBinThreads * kPlaceItems;
+
+__device__ __forceinline__ int bit_width_device(uint32_t v) { return v ? 32 - __clz(v) : 0; }
+
+__global__ void __launch_bounds__(kBinThreads, CLAD3DGS_PLACE_BLOCKS)
+    place_kernel(int grid_x, int grid_y, uint32_t n, const uint64_t* __restrict__ spans,
+                 const uint32_t* __restrict__ row_start,
+                 const uint32_t* __restrict__ chunk_first,
+                 const uint32_t* __restrict__ chunk_offsets,
+                 const uint32_t* __restrict__ tile_start, uint32_t* __restrict__ values) {
+  using Sort = cub::BlockRadixSort<uint32_t, kBinThreads, kPlaceItems, uint32_t>;
+  using Scan = cub::BlockScan<uint32_t, kBinThreads>;
+  __shared__ union {
+    typename Sort::TempStorage sort;
+    typename Scan::TempStorage scan;
+  } tmp;
+  __shared__ uint32_t pair_begin[kRowChunk + 1];  // first instance of each pair
+  __shared__ uint32_t pair_id[kRowChunk];
+  __shared__ uint16_t pair_lo[kRowChunk];
+  __shared__ uint32_t first_key[kBinThreads];
+  extern __shared__ uint32_t dyn[];
+  uint32_t* running = dyn;        // grid_x: next free slot of each tile
+  uint32_t* head = dyn + grid_x;  // grid_x: first window index of each tile
+  const uint32_t c = blockIdx.x;
+  if (c >= chunk_first[grid_y]) return;  // whole block
+  const int ty = chunk_row(chunk_first, grid_y, c);
+  const uint32_t begin = row_start[ty] + (c - chunk_first[ty]) * kRowChunk;
+  const uint32_t count = min(row_start[ty + 1], begin + kRowChunk) - begin;
+  for (int x = threadIdx.x; x < grid_x; x += blockDim.x) {
+    running[x] = tile_start[ty * grid_x + x] + chunk_offsets[size_t(c) * grid_x + x];
+    head[x] = 0xffffffffu;
+  }
+  // Pair spans and their first instances (a block scan in pair order).
+  constexpr int kPer = kRowChunk / kBinThreads;
+  uint32_t width[kPer], mine = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const uint32_t p = threadIdx.x * kPer + k;
+    width[k] = 0;
+    if (p < count) {
+      const uint64_t v = spans[begin + p];
+      const uint32_t lo = uint32_t(v >> 32) & 0xffffu, hi = uint32_t(v >> 48);
+      pair_id[p] = uint32_t(v);
+      pair_lo[p] = uint16_t(lo);
+      width[k] = hi > lo ? hi - lo : 0u;
+    }
+    mine += width[k];
+  }
+  uint32_t offset, chunk_total;
+  Scan(tmp.scan).ExclusiveSum(mine, offset, chunk_total);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const uint32_t p = threadIdx.x * kPer + k;
+    if (p < count) pair_begin[p] = offset;
+    offset += width[k];
+  }
+  if (threadIdx.x == 0) pair_begin[count] = chunk_total;
+  const int end_bit = bit_width_device(uint32_t(grid_x));  // the sentinel grid_x sorts last
+  for (uint32_t w0 = 0; w0 < chunk_total; w0 += kPlaceWindow) {  // the same trips everywhere
+    __syncthreads();  // pair arrays written / the previous window's shared state used
+    uint32_t keys[kPlaceItems], ids[kPlaceItems];
+    const uint32_t j0 = w0 + threadIdx.x * kPlaceItems;
+    // The pair holding instance j0: the last pair whose first instance is <= j0
+    // (pairs without instances share their successor's first instance).
+    uint32_t lo = 0, hi = count;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) / 2;
+      if (pair_begin[mid] <= j0) lo = mid;
+      else hi = mid;
+    }
+    uint32_t p = lo;
+#pragma unroll
+    for (int i = 0; i < kPlaceItems; ++i) {
+      const uint32_t j = j0 + i;
+      keys[i] = uint32_t(grid_x);
+      ids[i] = 0;
+      if (j < chunk_total) {
+        while (pair_begin[p + 1] <= j) ++p;
+        keys[i] = uint32_t(pair_lo[p]) + (j - pair_begin[p]);
+        ids[i] = pair_id[p];
+      }
+    }
+    Sort(tmp.sort).Sort(keys, ids, 0, end_bit);
+    // Blocked arrangement: thread t holds sorted items [k t, k t + k), k = kPlaceItems.
+    first_key[threadIdx.x] = keys[0];
+#pragma unroll
+    for (int i = 0; i < kPlaceItems; ++i) {
+      const uint32_t x = keys[i];
+      if (x < uint32_t(grid_x) && (i == 0 || keys[i - 1] != x))
+        atomicMin(&head[x], threadIdx.x * kPlaceItems + i);
+    }
+    __syncthreads();
+    uint32_t advance[kPlaceItems];
+#pragma unroll
+    for (int i = 0; i < kPlaceItems; ++i) {
+      const uint32_t idx = threadIdx.x * kPlaceItems + i;
+      const uint32_t x = keys[i];
+      advance[i] = 0;
+      if (x < uint32_t(grid_x)) {
+        const uint32_t pos = running[x] + (idx - head[x]);
+        if (pos < n) values[pos] = ids[i];
+        const uint32_t next = i + 1 < kPlaceItems
+                                  ? keys[i + 1]
+                                  : (threadIdx.x + 1 < kBinThreads ? first_key[threadIdx.x + 1]
+                                                                   : 0xffffffffu);
+        if (next != x) advance[i] = idx - head[x] + 1;  // last item of tile x's run
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPlaceItems; ++i)
+      if (advance[i]) {
+        running[keys[i]] += advance[i];
+        head[keys[i]] = 0xffffffffu;
+      }
+  }
 }
 
 __global__ void __launch_bounds__(kTilePixels)
@@ -1198,45 +1400,62 @@ int bits_for(uint32_t v) {
   return b;
 }
 
-// Depth order, instance counts and their scan (see duplicate_kernel); reads
-// the instance total back to the host. Needs g.depth, g.tiles, g.mean2d, g.radii.
-int order_and_count(int P, GeomState& g, uint32_t& total, cudaStream_t stream) {
+// Depth order, row counts and their scan; reads the totals (tile instances,
+// row pairs) back to the host. Needs g.depth, g.tiles, g.rows.
+int order_and_count(int P, GeomState& g, uint32_t& instances, uint32_t& pairs,
+                    cudaStream_t stream) {
   const int blocks = (P + 255) / 256;
   depth_key_kernel<<<blocks, 256, 0, stream>>>(P, g);
   cudaError_t e = cub::DeviceRadixSort::SortPairs(g.order_tmp, g.order_bytes, g.depth_keys,
                                                   g.depth_sorted, g.ids, g.order, P, 0, 32,
                                                   stream);
   if (e != cudaSuccess) return status_of(e, "depth order");
-  gather_counts_kernel<<<blocks, 256, 0, stream>>>(P, g);
+  gather_rows_kernel<<<blocks, 256, 0, stream>>>(P, g);
   e = cub::DeviceScan::InclusiveSum(g.scan_tmp, g.scan_bytes, g.depth_keys, g.offsets, P,
                                     stream);
-  if (e != cudaSuccess) return status_of(e, "tile scan");
-  total = 0;
-  e = cudaMemcpyAsync(&total, g.offsets + P - 1, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                      stream);
+  if (e != cudaSuccess) return status_of(e, "row scan");
+  e = cub::DeviceReduce::Sum(g.scan_tmp, g.scan_bytes, g.tiles, g.totals, P, stream);
+  if (e != cudaSuccess) return status_of(e, "instance count");
+  e = cudaMemcpyAsync(g.totals + 1, g.offsets + P - 1, sizeof(uint32_t),
+                      cudaMemcpyDeviceToDevice, stream);
+  uint32_t host[2] = {0, 0};
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(host, g.totals, sizeof(host), cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return status_of(e, "reading the instance count");
+  instances = host[0];
+  pairs = host[1];
   return CLAD3DGS_OK;
 }
 
-// Instances in depth order, stable-sorted by tile, and the per-tile ranges.
-int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t total,
+// Per-tile lists and ranges from the depth order (see "Binning" above).
+int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t n, uint32_t m,
                   const BinningState& b, const ImageState& img, cudaStream_t stream) {
-  const int warps_per_block = 8;
-  const long long warps_needed = (P + 31) / 32;  // one warp per 32 Gaussians
-  const int blocks = int(std::min<long long>(
-      (warps_needed + warps_per_block - 1) / warps_per_block, 148LL * 64));
-  duplicate_kernel<<<blocks, 32 * warps_per_block, 0, stream>>>(P, g, grid_x, grid_y,
-                                                               b.keys_unsorted,
-                                                               b.values_unsorted);
-  size_t sort_bytes = b.sort_bytes;
-  const cudaError_t e = cub::DeviceRadixSort::SortPairs(
-      b.sort_tmp, sort_bytes, b.keys_unsorted, b.keys, b.values_unsorted, b.values,
-      int(total), 0, bits_for(uint32_t(grid_x * grid_y)), stream);
-  if (e != cudaSuccess) return status_of(e, "tile sort");
+  if (grid_x > 0xffff) return fail(CLAD3DGS_INVALID_ARGUMENT, "image too wide for binning");
   const int tiles = grid_x * grid_y;
-  ranges_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(total, tiles, b.keys, img.ranges);
-  return CLAD3DGS_OK;
+  emit_rows_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, grid_x, grid_y, b.pair_rows,
+                                                        b.pair_spans);
+  size_t sort_bytes = b.sort_bytes;
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(
+      b.sort_tmp, sort_bytes, b.pair_rows, b.pair_rows_sorted, b.pair_spans,
+      b.pair_spans_sorted, int(m), 0, bits_for(uint32_t(grid_y)), stream);
+  if (e != cudaSuccess) return status_of(e, "row sort");
+  row_layout_kernel<<<1, 1024, 0, stream>>>(m, grid_y, b.pair_rows_sorted, b.row_start,
+                                            b.chunk_first);
+  tile_count_kernel<<<b.max_chunks, kBinThreads, (grid_x + 1) * sizeof(int), stream>>>(
+      grid_x, grid_y, b.pair_spans_sorted, b.row_start, b.chunk_first, b.chunk_counts);
+  tile_totals_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(grid_x, grid_y, b.chunk_first,
+                                                              b.chunk_counts, b.tile_total);
+  size_t scan_bytes = b.scan_bytes;
+  e = cub::DeviceScan::ExclusiveSum(b.scan_tmp, scan_bytes, b.tile_total, b.tile_start, tiles,
+                                    stream);
+  if (e != cudaSuccess) return status_of(e, "tile scan");
+  tile_ranges_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(tiles, b.tile_start,
+                                                              b.tile_total, img.ranges);
+  place_kernel<<<b.max_chunks, kBinThreads, 2 * grid_x * sizeof(uint32_t), stream>>>(
+      grid_x, grid_y, n, b.pair_spans_sorted, b.row_start, b.chunk_first, b.chunk_counts,
+      b.tile_start, b.values);
+  return status_of(cudaPeekAtLastError(), "binning");
 }
 
 Camera make_camera(const float* view, const float* proj, const float* campos, int width,
@@ -1263,8 +1482,11 @@ extern "C" size_t clad3dgs_raster_image_bytes(int width, int height) {
   const int tiles = ((width + kTileX - 1) / kTileX) * ((height + kTileY - 1) / kTileY);
   return image_bytes(width * height, tiles);
 }
-extern "C" size_t clad3dgs_raster_binning_bytes(int instances) {
-  return instances > 0 ? binning_bytes(instances) : 0;
+extern "C" size_t clad3dgs_raster_binning_bytes(int instances, int row_pairs, int width,
+                                                int height) {
+  if (instances <= 0 || row_pairs <= 0 || width <= 0 || height <= 0) return 0;
+  return binning_bytes(uint32_t(instances), uint32_t(row_pairs), (width + kTileX - 1) / kTileX,
+                       (height + kTileY - 1) / kTileY);
 }
 
 // Forward. The view-space / projection matrices, campos and bg are device
@@ -1299,17 +1521,18 @@ extern "C" int clad3dgs_raster_forward(
     preprocess_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
         P, degree, means, scales, scale_modifier, rotations, opacities, colors_precomp,
         cov3d_precomp, sh, cam, antialiasing != 0, g, radii);
-    uint32_t total = 0;
-    int status = order_and_count(P, g, total, stream);
+    uint32_t total = 0, pairs = 0;
+    int status = order_and_count(P, g, total, pairs, stream);
     if (status != CLAD3DGS_OK) return status;
-    if (total > uint32_t(INT32_MAX))
+    if (total > uint32_t(INT32_MAX) || pairs > uint32_t(INT32_MAX))
       return fail(CLAD3DGS_INVALID_ARGUMENT, "more than 2^31 - 1 tile instances");
     *num_rendered = int(total);
     if (total > 0) {
-      char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
+      char* bin_base =
+          alloc(alloc_ctx, 2, binning_bytes(total, pairs, cam.grid_x, cam.grid_y));
       if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
-      BinningState b = binning_from(bin_base, int(total));
-      status = bin_instances(P, g, cam.grid_x, cam.grid_y, total, b, img, stream);
+      BinningState b = binning_from(bin_base, total, pairs, cam.grid_x, cam.grid_y);
+      status = bin_instances(P, g, cam.grid_x, cam.grid_y, total, pairs, b, img, stream);
       if (status != CLAD3DGS_OK) return status;
       render_forward_kernel<<<dim3(cam.grid_x, cam.grid_y), kTilePixels, 0, stream>>>(
           img.ranges, b.values, width, height, cam.grid_x, g.mean2d, g.rgb,
@@ -1339,21 +1562,20 @@ extern "C" int clad3dgs_raster_render_backward(
   GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
   ImageState img = image_from(static_cast<char*>(const_cast<void*>(image_buffer)),
                               width * height, gx * gy);
-  BinningState b = binning_from(static_cast<char*>(const_cast<void*>(binning_buffer)),
-                                num_rendered);
+  const uint32_t* point_list = point_list_from(binning_buffer);
   PixelGrads o{dmean2d, dconic, dopacity, dcolor, dinvdepth};
   const dim3 grid(gx, gy);
   if (mode == 0)
     render_backward_kernel<0><<<grid, kTilePixels, 0, stream>>>(
-        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        img.ranges, point_list, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   else if (mode == 1)
     render_backward_kernel<1><<<grid, kTilePixels, 0, stream>>>(
-        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        img.ranges, point_list, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   else
     render_backward_pairs_kernel<<<grid, kPairThreads, 0, stream>>>(
-        img.ranges, b.values, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
+        img.ranges, point_list, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   return status_of(cudaPeekAtLastError(), "pixel backward");
 }
@@ -1435,9 +1657,10 @@ __global__ void fill_2d_kernel(int P, const float* __restrict__ mean2d,
   g.rgb[3 * i + 2] = rgb[3 * i + 2];
   g.depth[i] = depth[i];
   g.radii[i] = r;
-  g.tiles[i] = r > 0 ? footprint_tiles(make_footprint(px, py, g.conic_opacity[i], r, grid_x,
-                                                      grid_y))
-                     : 0u;
+  const Footprint f = make_footprint(px, py, g.conic_opacity[i], r, grid_x, grid_y);
+  const uint32_t n = r > 0 ? footprint_tiles(f) : 0u;
+  g.tiles[i] = n;
+  g.rows[i] = n ? uint32_t(f.y1 - f.y0) : 0u;
 }
 }  // namespace raster
 }  // namespace clad3dgs
@@ -1467,17 +1690,17 @@ extern "C" int clad3dgs_raster_forward_2d(int P, const float* mean2d,
   if (e != cudaSuccess) return status_of(e, "clearing tile ranges");
   fill_2d_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, mean2d, conic_opacity, rgb, depth,
                                                       radii, gx, gy, g);
-  uint32_t total = 0;
-  int status = order_and_count(P, g, total, stream);
+  uint32_t total = 0, pairs = 0;
+  int status = order_and_count(P, g, total, pairs, stream);
   if (status != CLAD3DGS_OK) return status;
-  if (total > uint32_t(INT32_MAX))
+  if (total > uint32_t(INT32_MAX) || pairs > uint32_t(INT32_MAX))
     return fail(CLAD3DGS_INVALID_ARGUMENT, "more than 2^31 - 1 tile instances");
   *num_rendered = int(total);
   if (total == 0) return CLAD3DGS_OK;
-  char* bin_base = alloc(alloc_ctx, 2, binning_bytes(int(total)));
+  char* bin_base = alloc(alloc_ctx, 2, binning_bytes(total, pairs, gx, gy));
   if (!bin_base) return fail(CLAD3DGS_INVALID_ARGUMENT, "binning buffer allocation failed");
-  BinningState b = binning_from(bin_base, int(total));
-  status = bin_instances(P, g, gx, gy, total, b, img, stream);
+  BinningState b = binning_from(bin_base, total, pairs, gx, gy);
+  status = bin_instances(P, g, gx, gy, total, pairs, b, img, stream);
   if (status != CLAD3DGS_OK) return status;
   render_forward_kernel<<<dim3(gx, gy), kTilePixels, 0, stream>>>(
       img.ranges, b.values, width, height, gx, g.mean2d, g.rgb, g.conic_opacity, g.depth, bg,

@@ -228,7 +228,10 @@ typedef char* (*clad3dgs_alloc_fn)(void* ctx, int which, size_t bytes);
 
 size_t clad3dgs_raster_geom_bytes(int P);
 size_t clad3dgs_raster_image_bytes(int width, int height);
-size_t clad3dgs_raster_binning_bytes(int instances);
+/* Binning buffer for `instances` tile instances and `row_pairs` (Gaussian,
+ * tile row) pairs at the given image size: the point list followed by the
+ * forward's binning scratch. */
+size_t clad3dgs_raster_binning_bytes(int instances, int row_pairs, int width, int height);
 
 /* Forward rasterization of P Gaussians (the renderer's
  * rasterize_gaussians, called at adapter.py:45-48 and check.py:768-774):
