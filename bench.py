@@ -67,6 +67,8 @@ def parse():
                     help="fused-step line without the attached training-step measurement")
     ap.add_argument("--train-gaussians", type=int, default=6_000_000,
                     help="train-step: replicated Gaussians (smaller cases are for profiling)")
+    ap.add_argument("--view-offset", type=int, default=0,
+                    help="train-step: rank r renders orbit camera (r + offset) mod 8")
     ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
                     help="train-step: gradient exchange (default: peer memory on >1 GPU)")
     ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
@@ -315,7 +317,7 @@ def native_arm(args):
     train = None
     if not args.no_train_step:
         torch.cuda.empty_cache()
-        train = measure_train_step(args, steps=20, warmup=3, with_e2e=False)
+        train = measure_train_step(args, steps=24, warmup=8, with_e2e=False)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -511,8 +513,8 @@ def pixel_backward_arm(args):
                                "T stop 1e-4, dL/dpixel N(0,1e-3)",
                    "tile_instances": num, "accumulation_mode": modes[0],
                    "ms_per_mode": {names[m]: results[m] for m in modes}},
-        "roofline": {"bound": "hbm", "limiter": "instruction issue (the ncu summary of this "
-                                                "kernel: issue-active ~85%, DRAM <1%)",
+        "roofline": {"bound": "hbm", "limiter": "instruction issue and latency (the ncu "
+                                                "summary of this kernel: DRAM < 1% of peak)",
                      "achieved": algorithmic / (ms / 1e3) / 1e9,
                      "peak": peak, "unit": "GB/s",
                      "frac": algorithmic / (ms / 1e3) / 1e9 / peak,
@@ -581,9 +583,25 @@ def measure_train_step(args, steps, warmup, with_e2e):
     values = train_values(n, device)
     trainer = DataParallelTrainer(values, exchange=args.exchange, device=device)
     del values
-    cam = orbit_camera(rank % 8, 8, width=TRAIN_W, height=TRAIN_H, device=device)
-    gen = torch.Generator(device=device).manual_seed(100 + rank)
-    target = torch.rand(3, TRAIN_H, TRAIN_W, generator=gen, device=device)
+    # The 8 orbit cameras and a fixed random target per camera. Like a trainer
+    # walking its cameras, step k on rank r renders camera (r + k N) mod 8, so
+    # every GPU count sees the same mix of views (the diagonal views cost more).
+    cams = [orbit_camera(v, 8, width=TRAIN_W, height=TRAIN_H, device=device) for v in range(8)]
+    targets = []
+    for v in range(8):
+        gen = torch.Generator(device=device).manual_seed(100 + v)
+        targets.append(torch.rand(3, TRAIN_H, TRAIN_W, generator=gen, device=device))
+    counter = [0]
+
+    def view():
+        v = (rank + args.view_offset + counter[0] * world) % 8
+        counter[0] += 1
+        return v
+
+    def step_once(target=None):
+        v = view()
+        return trainer.step(cams[v], targets[v] if target is None else target(v))
+
     stream = torch.cuda.current_stream()
 
     per_rank = {}
@@ -610,24 +628,29 @@ def measure_train_step(args, steps, warmup, with_e2e):
     instances = 0
     with ClockSampler(local) as clocks:
         for k in range(warmup):
-            loss, instances = trainer.step(cam, target)
+            loss, instances = step_once()
             if k == 0:
                 first_loss = float(loss.item())
         bracket()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         ev[0].record(stream)
         for _ in range(steps):
-            loss, instances = trainer.step(cam, target)
+            loss, instances = step_once()
         ev[1].record(stream)
         bracket()
     step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps, "step_ms")
     last_loss = float(loss.item())
     # The exchange + update alone (gradients of a real backward in place).
     exchange_steps = max(3, min(steps, 20))
-    total = 0.0
+    total = backward_total = 0.0
     for _ in range(exchange_steps):
-        trainer.backward(cam, target)
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        v = view()
+        trainer.backward(cams[v], targets[v])
+        b1.record(stream)
         bracket()
+        backward_total += b0.elapsed_time(b1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         trainer.adam.step()
@@ -635,6 +658,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
         torch.cuda.synchronize()
         total += e0.elapsed_time(e1)
     exchange_ms = max_over_ranks(total / exchange_steps, "exchange_ms")
+    max_over_ranks(backward_total / exchange_steps, "render_and_backward_ms")
     adam = trainer.adam
     baseline_ms = None
     if world > 1 and adam.exchange == "peer":
@@ -658,22 +682,26 @@ def measure_train_step(args, steps, warmup, with_e2e):
     # loss goes back to the host.
     e2e = None
     if with_e2e:
-        host_target = target.cpu().pin_memory()
-        dev_target = torch.empty_like(target)
+        host_targets = [t.cpu().pin_memory() for t in targets]
+        dev_target = torch.empty_like(targets[0])
         loss_host = torch.empty(1, pin_memory=True)
+
+        def staged(v):
+            dev_target.copy_(host_targets[v], non_blocking=True)
+            return dev_target
+
         e2e_steps = max(3, min(steps, 20))
         bracket()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(e2e_steps):
-            dev_target.copy_(host_target, non_blocking=True)
-            loss, _ = trainer.step(cam, dev_target)
+            loss, _ = step_once(staged)
             loss_host.copy_(loss, non_blocking=True)
         e1.record(stream)
         bracket()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
         e2e = {"value": world / (e2e_ms / 1e3), "unit": "views/s",
-               "h2d_bytes_per_step": host_target.numel() * 4, "d2h_bytes_per_step": 4,
+               "h2d_bytes_per_step": host_targets[0].numel() * 4, "d2h_bytes_per_step": 4,
                "ms_per_step": e2e_ms}
     inst = torch.tensor([float(instances)], device=device, dtype=torch.float64)
     if world > 1:
@@ -714,7 +742,8 @@ def measure_train_step(args, steps, warmup, with_e2e):
         "vs_baseline": None, "dtype": "f32+f64",
         "data": "synthetic (seeded; 6M Gaussians of the 8-view configuration, random targets)",
         "config": {"workload": f"{n:,} Gaussians SH degree 3 replicated, one {TRAIN_W}x{TRAIN_H} "
-                               "view per GPU on a radius-4 orbit (fov 60), L1 loss, rasterizer "
+                               "view per GPU per step from 8 cameras on a radius-4 orbit (fov "
+                               "60; step k, rank r: camera (r + kN) mod 8), L1 loss, rasterizer "
                                "backward, exchange + sharded torch-fused Adam",
                    "exchange": adam.exchange, "padded_gaussians": padded,
                    "share_per_gpu": share, "tile_instances_rank0": instances,

@@ -184,9 +184,125 @@ __global__ void __launch_bounds__(kThreads, R <= 2 ? 4 : 3)
   if (R > 1) __threadfence_system();
 }
 
+// One float4 chunk of the owned spans: where it lives and everything loaded
+// for it (every source's gradients, the parameters, both moments, the saved
+// activation value).
+template <int R>
+struct Chunk {
+  int g;
+  int64_t elem, melem;  // index into full arrays / into the moments
+  float4 t[R], p, m, v, s;
+};
+
+template <int R>
+__device__ __forceinline__ void load_chunk(const ShardParams& a, int64_t c, int64_t n,
+                                           Chunk<R>& x) {
+  // Chunk boundaries of the five groups (float4 chunks of the owned spans).
+  const int64_t c0 = n * 3 / 4, c1 = c0 + n * 12, c2 = c1 + n * 3 / 4, c3 = c2 + n;
+  int64_t local;
+  if (c < c0) {
+    x.g = 0, local = c;
+  } else if (c < c1) {
+    x.g = 1, local = c - c0;
+  } else if (c < c2) {
+    x.g = 2, local = c - c1;
+  } else if (c < c3) {
+    x.g = 3, local = c - c2;
+  } else {
+    x.g = 4, local = c - c3;
+  }
+  const int k = group_width(x.g);
+  x.elem = a.begin * k + 4 * local;
+  x.melem = 4 * local;
+  const int64_t gelem = x.elem - a.grad_origin * k;
+#pragma unroll
+  for (int q = 0; q < R; ++q)
+    x.t[q] = __ldcs(reinterpret_cast<const float4*>(a.grads[q][x.g] + gelem));
+  x.p = *reinterpret_cast<const float4*>(a.params[a.local][x.g] + x.elem);
+  x.m = *reinterpret_cast<const float4*>(a.first[x.g] + x.melem);
+  x.v = *reinterpret_cast<const float4*>(a.second[x.g] + x.melem);
+  if (x.g == 2) x.s = *reinterpret_cast<const float4*>(a.saved_scaling + x.elem);
+  else if (x.g == 4) x.s = *reinterpret_cast<const float4*>(a.saved_opacity + x.elem);
+  else if (x.g == 3) x.s.x = a.saved_norm[x.elem / 4];
+}
+
+template <int R>
+__device__ __forceinline__ void update_chunk(const ShardParams& a, const Chunk<R>& x) {
+  // The sum in rank order.
+  float4 grad = x.t[0];
+#pragma unroll
+  for (int q = 1; q < R; ++q) grad = add4(grad, x.t[q]);
+  // Activation VJPs (controls/ManualActivations.cu:20-36, 94-100) with the
+  // values saved by the forward activation.
+  if (x.g == 2) {
+    grad = make_float4(x.s.x * grad.x, x.s.y * grad.y, x.s.z * grad.z, x.s.w * grad.w);
+  } else if (x.g == 4) {
+    const float4 s = x.s;
+    grad = make_float4((s.x * (1.f - s.x)) * grad.x, (s.y * (1.f - s.y)) * grad.y,
+                       (s.z * (1.f - s.z)) * grad.z, (s.w * (1.f - s.w)) * grad.w);
+  } else if (x.g == 3) {
+    const float q[4] = {x.p.x, x.p.y, x.p.z, x.p.w};
+    const float sd[4] = {grad.x, grad.y, grad.z, grad.w};
+    float out[4];
+    quaternion_vjp(q, sd, x.s.x, out);
+    grad = make_float4(out[0], out[1], out[2], out[3]);
+  }
+  const float gv[4] = {grad.x, grad.y, grad.z, grad.w};
+  float pv[4] = {x.p.x, x.p.y, x.p.z, x.p.w}, mv[4] = {x.m.x, x.m.y, x.m.z, x.m.w},
+        vv[4] = {x.v.x, x.v.y, x.v.z, x.v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float step;
+    if (x.g == 1)
+      step = (x.elem + j) % 48 < 3 ? a.step[1] : a.step[2];
+    else
+      step = a.step[x.g == 0 ? 0 : x.g + 1];
+    torch_adam(pv[j], mv[j], vv[j], gv[j], step, a.inv_bias2);
+  }
+  *reinterpret_cast<float4*>(a.first[x.g] + x.melem) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+  *reinterpret_cast<float4*>(a.second[x.g] + x.melem) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+  const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
+#pragma unroll
+  for (int q = 0; q < R; ++q) __stcs(reinterpret_cast<float4*>(a.params[q][x.g] + x.elem), out);
+}
+
+// With peers: grid-stride over the chunks, each thread loading its next chunk
+// before it updates the current one, so the loads over NVLink stay in flight
+// during the Adam arithmetic (measured faster with 2 GPUs; on one GPU the
+// plain kernel above, with more resident threads, is faster).
+template <int R>
+__global__ void __launch_bounds__(kThreads, R <= 4 ? 3 : 2)
+    shard_update_prefetch_kernel(const __grid_constant__ ShardParams a) {
+  const int64_t n = a.end - a.begin;  // a multiple of 4
+  const int64_t chunks = n * 59 / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= chunks) return;
+  Chunk<R> cur;
+  load_chunk<R>(a, c, n, cur);
+  for (;;) {
+    const int64_t next = c + stride;
+    if (next < chunks) {
+      Chunk<R> nx;
+      load_chunk<R>(a, next, n, nx);
+      update_chunk<R>(a, cur);
+      cur = nx;
+      c = next;
+    } else {
+      update_chunk<R>(a, cur);
+      break;
+    }
+  }
+  // Make the peer stores visible system-wide before the kernel retires.
+  if (R > 1) __threadfence_system();
+}
+
 template <int R>
 cudaError_t launch_shard_update(const ShardParams& p, int64_t chunks, cudaStream_t stream) {
-  shard_update_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
+  if constexpr (R == 1)
+    shard_update_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
+  else
+    shard_update_prefetch_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
