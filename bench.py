@@ -541,11 +541,12 @@ def train_values(n, device, seed=3):
 
 
 TRAIN_GAUSSIANS, TRAIN_W, TRAIN_H = 6_000_000, 1920, 1080
-# Kernels of ours per training step: activate, preprocess, depth keys, count
-# gather, duplicate, ranges, render forward, L1 loss, render backward, SH backward,
-# preprocess backward, shard update (CUB's scans and sorts and NCCL's barriers
-# are library launches).
-TRAIN_LAUNCHES_PER_STEP = 12
+# Kernels of ours per training step: activate, preprocess, SH colour, depth keys,
+# row gather, row emission, row layout, tile counts, tile totals, tile ranges,
+# instance placement, render forward, L1 loss, render backward, preprocess
+# backward, SH backward, shard update (CUB's scans, sorts and reductions and
+# NCCL's barriers are library launches).
+TRAIN_LAUNCHES_PER_STEP = 17
 
 
 def train_step_arm(args):

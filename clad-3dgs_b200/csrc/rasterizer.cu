@@ -261,8 +261,8 @@ struct RowSource {
   __device__ __forceinline__ const float* term(int, int j) const { return row + 3 * j; }
 };
 
-template <int J>
-__device__ __forceinline__ void colour_terms(const Direction& d, const ShSource& sh, int i,
+template <int J, class Source>
+__device__ __forceinline__ void colour_terms(const Direction& d, const Source& sh, int i,
                                              int nterms, float rgb[3]) {
   if constexpr (J < 16) {
     if (J < nterms) {
@@ -315,13 +315,13 @@ struct Camera {
 // ---------------------------------------------------------------------------
 // Forward kernels.
 
-__global__ void preprocess_kernel(int P, int degree, const float* __restrict__ means,
+__global__ void preprocess_kernel(int P, const float* __restrict__ means,
                                   const float* __restrict__ scales, float scale_modifier,
                                   const float* __restrict__ rotations,
                                   const float* __restrict__ opacities,
                                   const float* __restrict__ colors_precomp,
-                                  const float* __restrict__ cov3d_precomp, ShSource sh,
-                                  Camera cam, bool antialiasing, GeomState g,
+                                  const float* __restrict__ cov3d_precomp, Camera cam,
+                                  bool antialiasing, GeomState g,
                                   int* __restrict__ radii_out) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
@@ -368,20 +368,10 @@ __global__ void preprocess_kernel(int P, int degree, const float* __restrict__ m
   tile_rect(px, py, radius, cam.grid_x, cam.grid_y, x0, y0, x1, y1);
   const int touched = (x1 - x0) * (y1 - y0);
   if (touched == 0) return;
+  // SH colours come from sh_colour_kernel (coalesced coefficient reads).
   if (colors_precomp) {
 #pragma unroll
     for (int k = 0; k < 3; ++k) g.rgb[3 * i + k] = colors_precomp[3 * i + k];
-  } else {
-    const Direction d = make_direction(p.x, p.y, p.z, cam.campos[0], cam.campos[1],
-                                       cam.campos[2]);
-    float rgb[3] = {0.f, 0.f, 0.f};
-    colour_terms<0>(d, sh, i, (degree + 1) * (degree + 1), rgb);
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      const float v = rgb[k] + 0.5f;
-      g.clamped[3 * i + k] = v < 0.f;
-      g.rgb[3 * i + k] = fmaxf(v, 0.f);
-    }
   }
   g.depth[i] = t.z;
   g.radii[i] = radius;
@@ -434,6 +424,8 @@ __global__ void gather_rows_kernel(int P, GeomState g) {
   g.depth_keys[i] = g.rows[g.order[i]];
 }
 
+// One thread per Gaussian in depth order, so the pairs are written contiguously
+// (emitting in id order, with coalesced reads but scattered writes, was slower).
 __global__ void emit_rows_kernel(int P, GeomState g, int grid_x, int grid_y,
                                  uint32_t* __restrict__ rows_out,
                                  uint64_t* __restrict__ spans_out) {
@@ -796,6 +788,7 @@ __device__ __forceinline__ float transpose_reduce(float v[16], int lane) {
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
+// Modes 0 and 1, one pixel per thread (mode 2 is render_backward_pairs_kernel).
 template <int Mode>
 __global__ void __launch_bounds__(kTilePixels)
     render_backward_kernel(const uint2* __restrict__ ranges,
@@ -873,13 +866,8 @@ __global__ void __launch_bounds__(kTilePixels)
       const float alpha = fminf(kMaxAlpha, co.w * G);
       contrib = contrib && alpha >= kMinAlpha;
       float f[16];
-      if constexpr (Mode == 2) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) f[q] = 0.f;
-      } else {
-        if (!contrib) continue;
-      }
-      if (contrib) {
+      if (!contrib) continue;
+      {
         const float inv_keep = 1.f / (1.f - alpha);  // one reciprocal for T and the bg term
         T = T * inv_keep;
         const float w = alpha * T;
@@ -924,7 +912,7 @@ __global__ void __launch_bounds__(kTilePixels)
         atomicAdd(out.dconic + 4 * size_t(id) + 3, f[7]);
         atomicAdd(out.dopacity + id, f[8]);
         if (out.dinvdepth) atomicAdd(out.dinvdepth + id, f[9]);
-      } else if constexpr (Mode == 1) {
+      } else {
         // The reference's helper: whole warp on one Gaussian -> reduce, else
         // per-lane atomics.
         const bool full = __match_any_sync(__activemask(), id) == 0xffffffffu;
@@ -938,13 +926,6 @@ __global__ void __launch_bounds__(kTilePixels)
             atomicAdd(field_address(out, id, q), v);
           }
         }
-      } else {
-        // Per-lane atomics for warps with only a few contributing pixels
-        // measured slower than this reduction (L2 contention), at any cut-off.
-        if (!__any_sync(0xffffffffu, contrib)) continue;
-        const float total = transpose_reduce(f, lane);
-        const int q = (lane >> 1) & 15;
-        if ((lane & 1) == 0 && q < nf) atomicAdd(field_address(out, id, q), total);
       }
     }
   }
@@ -1321,14 +1302,57 @@ __global__ void preprocess_backward_kernel(
   }
 }
 
-// SH colour -> coefficients and view direction, 32 Gaussians per warp: the
-// warp stages its block of coefficients in shared memory with coalesced loads,
-// each lane works in its own row (reading coefficient j before overwriting it
-// with dL/dsh_j), and the warp stores the dL/dsh block coalesced. The direction
-// adjoint is added into dmeans after the geometry backward's share (dmeans is
-// zeroed by the caller, so the sum rounds as the single sum would).
-constexpr int kShRow = 49;  // 48 floats + 1: rows start in distinct banks
+// The SH kernels work on 32 Gaussians per warp: the warp stages its block of
+// coefficients in shared memory with coalesced loads (rows of 48 floats + 1,
+// so rows start in distinct banks) and each lane works in its own row.
+constexpr int kShRow = 49;
 constexpr int kShWarps = 4;
+
+__device__ __forceinline__ void stage_coefficients(const ShSource& sh, int i0, int n, int lane,
+                                                   float* blk) {
+  if (sh.packed) {
+    const float* src = sh.packed + 48 * size_t(i0);
+    for (int e = lane; e < n * 48; e += 32) blk[(e / 48) * kShRow + e % 48] = src[e];
+  } else {
+    const float* dc = sh.dc + 3 * size_t(i0);
+    const float* rest = sh.rest + 45 * size_t(i0);
+    for (int e = lane; e < n * 3; e += 32) blk[(e / 3) * kShRow + e % 3] = dc[e];
+    for (int e = lane; e < n * 45; e += 32) blk[(e / 45) * kShRow + 3 + e % 45] = rest[e];
+  }
+}
+
+// SH colour of every drawn Gaussian (radius > 0): colour + 0.5, clamped at 0,
+// with the clamp flags the backward reads.
+__global__ void __launch_bounds__(32 * kShWarps)
+    sh_colour_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
+                     const float* __restrict__ campos, GeomState g) {
+  __shared__ float rows[kShWarps][32 * kShRow];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* blk = rows[warp];
+  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
+  if (i0 >= P) return;  // whole warp
+  const int n = min(32, P - i0);
+  stage_coefficients(sh, i0, n, lane, blk);
+  __syncwarp();
+  const int i = i0 + lane;
+  if (lane >= n || g.radii[i] <= 0) return;
+  const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
+                                     campos[0], campos[1], campos[2]);
+  float rgb[3] = {0.f, 0.f, 0.f};
+  colour_terms<0>(d, RowSource{blk + lane * kShRow}, i, (degree + 1) * (degree + 1), rgb);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float v = rgb[k] + 0.5f;
+    g.clamped[3 * i + k] = v < 0.f;
+    g.rgb[3 * i + k] = fmaxf(v, 0.f);
+  }
+}
+
+// SH colour -> coefficients and view direction: each lane reads coefficient j
+// of its row before overwriting it with dL/dsh_j, and the warp stores the
+// dL/dsh block coalesced. The direction adjoint is added into dmeans after the
+// geometry backward's share (dmeans is zeroed by the caller, so the sum rounds
+// as the single sum would).
 
 __global__ void __launch_bounds__(32 * kShWarps)
     sh_backward_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
@@ -1341,15 +1365,7 @@ __global__ void __launch_bounds__(32 * kShWarps)
   const int i0 = (blockIdx.x * kShWarps + warp) * 32;
   if (i0 >= P) return;  // whole warp
   const int n = min(32, P - i0);
-  if (sh.packed) {
-    const float* src = sh.packed + 48 * size_t(i0);
-    for (int e = lane; e < n * 48; e += 32) blk[(e / 48) * kShRow + e % 48] = src[e];
-  } else {
-    const float* dc = sh.dc + 3 * size_t(i0);
-    const float* rest = sh.rest + 45 * size_t(i0);
-    for (int e = lane; e < n * 3; e += 32) blk[(e / 3) * kShRow + e % 3] = dc[e];
-    for (int e = lane; e < n * 45; e += 32) blk[(e / 45) * kShRow + 3 + e % 45] = rest[e];
-  }
+  stage_coefficients(sh, i0, n, lane, blk);
   __syncwarp();
   float* row = blk + lane * kShRow;
   const int i = i0 + lane;
@@ -1519,8 +1535,13 @@ extern "C" int clad3dgs_raster_forward(
     GeomState g = geom_from(geom_base, P);
     const ShSource sh{sh_packed, sh_dc, sh_rest};
     preprocess_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
-        P, degree, means, scales, scale_modifier, rotations, opacities, colors_precomp,
-        cov3d_precomp, sh, cam, antialiasing != 0, g, radii);
+        P, means, scales, scale_modifier, rotations, opacities, colors_precomp, cov3d_precomp,
+        cam, antialiasing != 0, g, radii);
+    if (!colors_precomp) {
+      const int warps = (P + 31) / 32;
+      sh_colour_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
+          P, degree, means, sh, campos, g);
+    }
     uint32_t total = 0, pairs = 0;
     int status = order_and_count(P, g, total, pairs, stream);
     if (status != CLAD3DGS_OK) return status;
