@@ -399,9 +399,9 @@ __global__ void preprocess_kernel(int P, const float* __restrict__ means,
 //     every chunk's instances per tile (difference array in shared memory);
 //  4. per tile the chunk counts become chunk offsets and the tile totals are
 //     scanned into tile starts (and the ranges);
-//  5. a second pass expands each chunk's pairs into their instances, groups
-//     them by tile with a stable block radix sort and writes every tile's run
-//     of Gaussian ids contiguously.
+//  5. a second pass ranks each chunk's instances within their tiles from lane
+//     masks of the pairs covering each tile (pair order kept) and writes every
+//     tile's run of Gaussian ids contiguously.
 constexpr int kBinThreads = 256;
 
 __device__ __forceinline__ uint64_t pack_pair(uint32_t id, int lo, int hi) {
@@ -510,29 +510,53 @@ __global__ void __launch_bounds__(kBinThreads)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int running = 0;
-    for (int x = 0; x < grid_x; ++x) {
-      running += diff[x];
-      chunk_counts[size_t(c) * grid_x + x] = uint32_t(running);
+  if (threadIdx.x < 32) {  // inclusive scan of the differences, 32 tiles at a time
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int x0 = 0; x0 < grid_x; x0 += 32) {
+      const int x = x0 + lane;
+      int v = x < grid_x ? diff[x] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (x < grid_x) chunk_counts[size_t(c) * grid_x + x] = uint32_t(carry + v);
+      carry += __shfl_sync(0xffffffffu, v, 31);
     }
   }
 }
 
 // Per tile: chunk counts -> offsets of each chunk within the tile, and the total.
-__global__ void tile_totals_kernel(int grid_x, int grid_y, const uint32_t* __restrict__ chunk_first,
-                                   uint32_t* __restrict__ chunk_counts,
-                                   uint32_t* __restrict__ tile_total) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= grid_x * grid_y) return;
-  const int ty = t / grid_x, x = t - ty * grid_x;
+// A block takes one tile row and 32 tiles (lane = tile); the row's chunks are
+// split into one contiguous segment per warp, each warp sums its segment, and
+// after the segment sums are known each warp rewrites its counts as offsets.
+constexpr int kBinWarps = kBinThreads / 32;
+
+__global__ void __launch_bounds__(kBinThreads)
+    tile_totals_kernel(int grid_x, const uint32_t* __restrict__ chunk_first,
+                       uint32_t* __restrict__ chunk_counts, uint32_t* __restrict__ tile_total) {
+  __shared__ uint32_t segment[kBinWarps][32];
+  const int ty = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int x = blockIdx.x * 32 + lane;
+  const uint32_t c0 = chunk_first[ty], chunks = chunk_first[ty + 1] - c0;
+  const uint32_t per = (chunks + kBinWarps - 1) / kBinWarps;
+  const uint32_t a = c0 + min(chunks, uint32_t(warp) * per);
+  const uint32_t e = c0 + min(chunks, uint32_t(warp + 1) * per);
+  uint32_t sum = 0;
+  if (x < grid_x)
+    for (uint32_t c = a; c < e; ++c) sum += chunk_counts[size_t(c) * grid_x + x];
+  segment[warp][lane] = sum;
+  __syncthreads();
+  if (x >= grid_x) return;
   uint32_t running = 0;
-  for (uint32_t c = chunk_first[ty]; c < chunk_first[ty + 1]; ++c) {
+  for (int w = 0; w < warp; ++w) running += segment[w][lane];
+  for (uint32_t c = a; c < e; ++c) {
     const uint32_t v = chunk_counts[size_t(c) * grid_x + x];
     chunk_counts[size_t(c) * grid_x + x] = running;
     running += v;
   }
-  tile_total[t] = running;
+  if (warp == kBinWarps - 1) tile_total[ty * grid_x + x] = running;
 }
 
 __global__ void tile_ranges_kernel(int tiles, const uint32_t* __restrict__ tile_start,
@@ -543,133 +567,90 @@ __global__ void tile_ranges_kernel(int tiles, const uint32_t* __restrict__ tile_
   ranges[t] = make_uint2(tile_start[t], tile_start[t] + tile_total[t]);
 }
 
-// Second pass: per chunk, the pairs' instances in pair order (each pair expands
-// to its row span), kPlaceWindow at a time: every thread takes kPlaceItems
-// consecutive instances, a stable block radix sort by tile groups them (pair
-// order kept within a tile), and each tile's run is written contiguously after
-// the runs that earlier windows and chunks wrote.
-#ifndef CLAD3DGS_PLACE_ITEMS
-#define CLAD3DGS_PLACE_ITEMS 8
-#endif
-#ifndef CLAD3DGS_PLACE_BLOCKS
-#define CLAD3DGS_PLACE_BLOCKS 4
-#endif
-constexpr int kPlaceItems = CLAD3DGS_PLACE_ITEMS;
-constexpr int kPlaceWindow = kBinThreads * kPlaceItems;
+// Second pass: per chunk, rounds of 256 pairs (one pair per thread, 32 per
+// warp). Each warp marks its pairs' spans in a per-tile lane mask (the XOR of a
+// lane bit at lo and at hi, prefix-XORed across the tiles gives, for every tile,
+// the lanes whose span covers it), so an instance's slot is its tile's next free
+// slot plus the instances of that tile in earlier warps of the round plus the
+// popcount of the earlier lanes in its warp's mask: pair order (= depth order)
+// is kept within every tile.
+__host__ __device__ constexpr int cover_index(int x) { return x + (x >> 5); }  // bank skew
 
-__device__ __forceinline__ int bit_width_device(uint32_t v) { return v ? 32 - __clz(v) : 0; }
+size_t place_shared_bytes(int grid_x) {
+  return sizeof(uint32_t) * (size_t(kBinWarps) * (cover_index(grid_x) + 1) +
+                             size_t(kBinWarps) * grid_x + size_t(grid_x));
+}
 
-__global__ void __launch_bounds__(kBinThreads, CLAD3DGS_PLACE_BLOCKS)
+__global__ void __launch_bounds__(kBinThreads)
     place_kernel(int grid_x, int grid_y, uint32_t n, const uint64_t* __restrict__ spans,
                  const uint32_t* __restrict__ row_start,
                  const uint32_t* __restrict__ chunk_first,
                  const uint32_t* __restrict__ chunk_offsets,
                  const uint32_t* __restrict__ tile_start, uint32_t* __restrict__ values) {
-  using Sort = cub::BlockRadixSort<uint32_t, kBinThreads, kPlaceItems, uint32_t>;
-  using Scan = cub::BlockScan<uint32_t, kBinThreads>;
-  __shared__ union {
-    typename Sort::TempStorage sort;
-    typename Scan::TempStorage scan;
-  } tmp;
-  __shared__ uint32_t pair_begin[kRowChunk + 1];  // first instance of each pair
-  __shared__ uint32_t pair_id[kRowChunk];
-  __shared__ uint16_t pair_lo[kRowChunk];
-  __shared__ uint32_t first_key[kBinThreads];
   extern __shared__ uint32_t dyn[];
-  uint32_t* running = dyn;        // grid_x: next free slot of each tile
-  uint32_t* head = dyn + grid_x;  // grid_x: first window index of each tile
+  const int G = grid_x, stride = cover_index(G) + 1;
+  uint32_t* cover_all = dyn;                       // [warps][cover_index(G) + 1] lane masks
+  uint32_t* slot_all = cover_all + kBinWarps * stride;  // [warps][G] first slot of the warp
+  uint32_t* next = slot_all + kBinWarps * G;       // [G] the tile's next free slot
   const uint32_t c = blockIdx.x;
   if (c >= chunk_first[grid_y]) return;  // whole block
   const int ty = chunk_row(chunk_first, grid_y, c);
   const uint32_t begin = row_start[ty] + (c - chunk_first[ty]) * kRowChunk;
   const uint32_t count = min(row_start[ty + 1], begin + kRowChunk) - begin;
-  for (int x = threadIdx.x; x < grid_x; x += blockDim.x) {
-    running[x] = tile_start[ty * grid_x + x] + chunk_offsets[size_t(c) * grid_x + x];
-    head[x] = 0xffffffffu;
-  }
-  // Pair spans and their first instances (a block scan in pair order).
-  constexpr int kPer = kRowChunk / kBinThreads;
-  uint32_t width[kPer], mine = 0;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const uint32_t p = threadIdx.x * kPer + k;
-    width[k] = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t* cover = cover_all + warp * stride;
+  const uint32_t* slot = slot_all + warp * G;
+  for (int x = threadIdx.x; x < kBinWarps * stride; x += kBinThreads) cover_all[x] = 0;
+  for (int x = threadIdx.x; x < G; x += kBinThreads)
+    next[x] = tile_start[ty * G + x] + chunk_offsets[size_t(c) * G + x];
+  // Each lane prefix-XORs a contiguous run of tiles.
+  const int per = (G + 31) / 32;
+  const int s0 = min(G, lane * per), s1 = min(G, s0 + per);
+  const uint32_t bit = 1u << lane, earlier = bit - 1u;
+  for (uint32_t r0 = 0; r0 < count; r0 += kBinThreads) {  // the same trips everywhere
+    __syncthreads();  // the previous round's shared state consumed
+    const uint32_t p = r0 + threadIdx.x;
+    uint32_t id = 0, lo = 0, hi = 0;
     if (p < count) {
       const uint64_t v = spans[begin + p];
-      const uint32_t lo = uint32_t(v >> 32) & 0xffffu, hi = uint32_t(v >> 48);
-      pair_id[p] = uint32_t(v);
-      pair_lo[p] = uint16_t(lo);
-      width[k] = hi > lo ? hi - lo : 0u;
+      id = uint32_t(v);
+      hi = min(uint32_t(v >> 48), uint32_t(G));
+      lo = min(uint32_t(v >> 32) & 0xffffu, hi);
     }
-    mine += width[k];
-  }
-  uint32_t offset, chunk_total;
-  Scan(tmp.scan).ExclusiveSum(mine, offset, chunk_total);
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const uint32_t p = threadIdx.x * kPer + k;
-    if (p < count) pair_begin[p] = offset;
-    offset += width[k];
-  }
-  if (threadIdx.x == 0) pair_begin[count] = chunk_total;
-  const int end_bit = bit_width_device(uint32_t(grid_x));  // the sentinel grid_x sorts last
-  for (uint32_t w0 = 0; w0 < chunk_total; w0 += kPlaceWindow) {  // the same trips everywhere
-    __syncthreads();  // pair arrays written / the previous window's shared state used
-    uint32_t keys[kPlaceItems], ids[kPlaceItems];
-    const uint32_t j0 = w0 + threadIdx.x * kPlaceItems;
-    // The pair holding instance j0: the last pair whose first instance is <= j0
-    // (pairs without instances share their successor's first instance).
-    uint32_t lo = 0, hi = count;
-    while (hi - lo > 1) {
-      const uint32_t mid = (lo + hi) / 2;
-      if (pair_begin[mid] <= j0) lo = mid;
-      else hi = mid;
+    if (hi > lo) {
+      atomicXor(&cover[cover_index(lo)], bit);
+      atomicXor(&cover[cover_index(hi)], bit);
     }
-    uint32_t p = lo;
+    __syncwarp();
+    uint32_t acc = 0;
+    for (int x = s0; x < s1; ++x) acc ^= cover[cover_index(x)];
+    uint32_t inc = acc;
 #pragma unroll
-    for (int i = 0; i < kPlaceItems; ++i) {
-      const uint32_t j = j0 + i;
-      keys[i] = uint32_t(grid_x);
-      ids[i] = 0;
-      if (j < chunk_total) {
-        while (pair_begin[p + 1] <= j) ++p;
-        keys[i] = uint32_t(pair_lo[p]) + (j - pair_begin[p]);
-        ids[i] = pair_id[p];
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc ^= t;
+    }
+    uint32_t run = inc ^ acc;
+    for (int x = s0; x < s1; ++x) {
+      run ^= cover[cover_index(x)];
+      cover[cover_index(x)] = run;
+    }
+    __syncthreads();  // every warp's masks ready
+    for (int x = threadIdx.x; x < G; x += kBinThreads) {
+      uint32_t at = next[x];
+      for (int w = 0; w < kBinWarps; ++w) {
+        slot_all[w * G + x] = at;
+        at += __popc(cover_all[w * stride + cover_index(x)]);
       }
+      next[x] = at;
     }
-    Sort(tmp.sort).Sort(keys, ids, 0, end_bit);
-    // Blocked arrangement: thread t holds sorted items [k t, k t + k), k = kPlaceItems.
-    first_key[threadIdx.x] = keys[0];
-#pragma unroll
-    for (int i = 0; i < kPlaceItems; ++i) {
-      const uint32_t x = keys[i];
-      if (x < uint32_t(grid_x) && (i == 0 || keys[i - 1] != x))
-        atomicMin(&head[x], threadIdx.x * kPlaceItems + i);
+    __syncthreads();  // slots ready
+    for (uint32_t x = lo; x < hi; ++x) {
+      const uint32_t pos = slot[x] + __popc(cover[cover_index(x)] & earlier);
+      if (pos < n) values[pos] = id;
     }
-    __syncthreads();
-    uint32_t advance[kPlaceItems];
-#pragma unroll
-    for (int i = 0; i < kPlaceItems; ++i) {
-      const uint32_t idx = threadIdx.x * kPlaceItems + i;
-      const uint32_t x = keys[i];
-      advance[i] = 0;
-      if (x < uint32_t(grid_x)) {
-        const uint32_t pos = running[x] + (idx - head[x]);
-        if (pos < n) values[pos] = ids[i];
-        const uint32_t next = i + 1 < kPlaceItems
-                                  ? keys[i + 1]
-                                  : (threadIdx.x + 1 < kBinThreads ? first_key[threadIdx.x + 1]
-                                                                   : 0xffffffffu);
-        if (next != x) advance[i] = idx - head[x] + 1;  // last item of tile x's run
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kPlaceItems; ++i)
-      if (advance[i]) {
-        running[keys[i]] += advance[i];
-        head[keys[i]] = 0xffffffffu;
-      }
+    __syncwarp();  // the warp's masks used
+    for (int x = lane; x < stride; x += 32) cover[x] = 0;
   }
 }
 
@@ -1449,6 +1430,21 @@ int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t n,
                   const BinningState& b, const ImageState& img, cudaStream_t stream) {
   if (grid_x > 0xffff) return fail(CLAD3DGS_INVALID_ARGUMENT, "image too wide for binning");
   const int tiles = grid_x * grid_y;
+  const size_t place_bytes = place_shared_bytes(grid_x);
+  {
+    int device = 0, limit = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e != cudaSuccess) return status_of(e, "device attributes");
+    if (place_bytes + 1024 > size_t(limit))
+      return fail(CLAD3DGS_INVALID_ARGUMENT, "image too wide for binning");
+    if (place_bytes > 48 * 1024) {
+      e = cudaFuncSetAttribute(place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(place_bytes));
+      if (e != cudaSuccess) return status_of(e, "placement shared memory");
+    }
+  }
   emit_rows_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, grid_x, grid_y, b.pair_rows,
                                                         b.pair_spans);
   size_t sort_bytes = b.sort_bytes;
@@ -1460,15 +1456,15 @@ int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t n,
                                             b.chunk_first);
   tile_count_kernel<<<b.max_chunks, kBinThreads, (grid_x + 1) * sizeof(int), stream>>>(
       grid_x, grid_y, b.pair_spans_sorted, b.row_start, b.chunk_first, b.chunk_counts);
-  tile_totals_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(grid_x, grid_y, b.chunk_first,
-                                                              b.chunk_counts, b.tile_total);
+  tile_totals_kernel<<<dim3((grid_x + 31) / 32, grid_y), kBinThreads, 0, stream>>>(
+      grid_x, b.chunk_first, b.chunk_counts, b.tile_total);
   size_t scan_bytes = b.scan_bytes;
   e = cub::DeviceScan::ExclusiveSum(b.scan_tmp, scan_bytes, b.tile_total, b.tile_start, tiles,
                                     stream);
   if (e != cudaSuccess) return status_of(e, "tile scan");
   tile_ranges_kernel<<<(tiles + 255) / 256, 256, 0, stream>>>(tiles, b.tile_start,
                                                               b.tile_total, img.ranges);
-  place_kernel<<<b.max_chunks, kBinThreads, 2 * grid_x * sizeof(uint32_t), stream>>>(
+  place_kernel<<<b.max_chunks, kBinThreads, place_bytes, stream>>>(
       grid_x, grid_y, n, b.pair_spans_sorted, b.row_start, b.chunk_first, b.chunk_counts,
       b.tile_start, b.values);
   return status_of(cudaPeekAtLastError(), "binning");
