@@ -71,6 +71,9 @@ def parse():
                     help="train-step: rank r renders orbit camera (r + offset) mod 8")
     ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
                     help="train-step: gradient exchange (default: peer memory on >1 GPU)")
+    ap.add_argument("--sh-exchange", choices=["seeds", "grads"], default=None,
+                    help="train-step: what a view publishes for the SH coefficients "
+                         "(default: colour seeds unless the exchange is collective)")
     ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
                     help="pixel-backward: 2D Gaussians (smaller cases are for profiling only)")
     ap.add_argument("--pixel-modes", default="2,1,0",
@@ -544,9 +547,10 @@ TRAIN_GAUSSIANS, TRAIN_W, TRAIN_H = 6_000_000, 1920, 1080
 # Kernels of ours per training step: activate, preprocess, SH colour, depth keys,
 # row gather, row emission, row layout, tile counts, tile totals, tile ranges,
 # instance placement, render forward, L1 loss, render backward, preprocess
-# backward, SH backward, shard update (CUB's scans, sorts and reductions and
-# NCCL's barriers are library launches).
-TRAIN_LAUNCHES_PER_STEP = 17
+# backward, then with SH gradients: SH backward, shard update; with colour
+# seeds: seeds, SH + position update, shard update of the other groups (CUB's
+# scans, sorts and reductions and NCCL's barriers are library launches).
+TRAIN_LAUNCHES_PER_STEP = {"grads": 17, "seeds": 18}
 
 
 def train_step_arm(args):
@@ -582,7 +586,8 @@ def measure_train_step(args, steps, warmup, with_e2e):
 
     n = args.train_gaussians
     values = train_values(n, device)
-    trainer = DataParallelTrainer(values, exchange=args.exchange, device=device)
+    trainer = DataParallelTrainer(values, exchange=args.exchange, device=device,
+                                  sh_exchange=args.sh_exchange)
     del values
     # The 8 orbit cameras and a fixed random target per camera. Like a trainer
     # walking its cameras, step k on rank r renders camera (r + k N) mod 8, so
@@ -717,10 +722,14 @@ def measure_train_step(args, steps, warmup, with_e2e):
     if rank != 0:
         return None
     # Exchange roofline: bytes that must cross NVLink per GPU and direction
-    # (the other ranks' gradients of this share in, this share's parameters out
-    # to the other ranks), against the measured 770 GB/s peer copy; with one GPU
-    # the update is HBM-bound (grads, params, moments read; params, moments written).
+    # (this share's parameters out to the other ranks, 236 B per Gaussian and
+    # peer; in: their gradients, 236 B, or in seed form their colour seeds and
+    # geometry gradients, 60 B), against the measured 770 GB/s peer copy; with
+    # one GPU the update is HBM-bound (inputs, params, moments read; params,
+    # moments written).
     floats = 59
+    seeded = adam.sh_exchange == "seeds"
+    inputs = (16 + 11 * 4) if seeded else floats * 4  # per Gaussian and view
     if world > 1:
         link = (world - 1) * share * floats * 4
         exchange_roof = {"bound": "nvlink", "achieved": link / (exchange_ms / 1e3) / 1e9,
@@ -729,7 +738,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
                          "bytes_per_direction": link,
                          "peak_kind": "measured peer copy per direction"}
     else:
-        hbm = share * floats * 4 * 7  # grads, params, 2 moments read; params, 2 moments written
+        hbm = share * (inputs + floats * 4 * 6)
         peak, peak_kind = measured_peaks()
         exchange_roof = {"bound": "hbm", "achieved": hbm / (exchange_ms / 1e3) / 1e9,
                          "peak": peak, "unit": "GB/s",
@@ -746,7 +755,8 @@ def measure_train_step(args, steps, warmup, with_e2e):
                                "view per GPU per step from 8 cameras on a radius-4 orbit (fov "
                                "60; step k, rank r: camera (r + kN) mod 8), L1 loss, rasterizer "
                                "backward, exchange + sharded torch-fused Adam",
-                   "exchange": adam.exchange, "padded_gaussians": padded,
+                   "exchange": adam.exchange, "sh_exchange": adam.sh_exchange,
+                   "padded_gaussians": padded,
                    "share_per_gpu": share, "tile_instances_rank0": instances,
                    "l2": "parameters 1.4 GB per replica exceed the 126 MB L2"},
         "loss": {"first": first_loss, "last": last_loss},
@@ -755,7 +765,7 @@ def measure_train_step(args, steps, warmup, with_e2e):
                      "roofline": exchange_roof},
         "clocks": clocks.summary(),
         "e2e": e2e,
-        "gpu_launches": TRAIN_LAUNCHES_PER_STEP * steps,
+        "gpu_launches": TRAIN_LAUNCHES_PER_STEP[adam.sh_exchange] * steps,
         "device_fault_word": fault,
     }
     return line

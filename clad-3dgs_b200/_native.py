@@ -38,7 +38,9 @@ class ShardUpdateArgs(ctypes.Structure):
                 ("first", c_void_p * SHARD_GROUPS), ("second", c_void_p * SHARD_GROUPS),
                 ("saved_scaling", c_void_p), ("saved_opacity", c_void_p),
                 ("saved_norm", c_void_p), ("rates", c_double * (SHARD_GROUPS + 1)),
-                ("bias1", c_float), ("bias2_sqrt", c_float)]
+                ("bias1", c_float), ("bias2_sqrt", c_float),
+                ("seeds", c_void_p * MAX_RANKS), ("cameras", c_void_p * MAX_RANKS),
+                ("degree", c_int)]
 
 
 _P = c_void_p
@@ -84,6 +86,8 @@ _SIGNATURES = {
                                  + [_P] * 2 + [c_int] + [_P] * 10 + [c_int, c_int]
                                  + [_P] * 6 + [TorchAdamConfig, _P, _P, c_double,
                                                TorchAdamConfig, _P]),
+    "clad3dgs_raster_sh_backward": (c_int, [c_int, c_int] + [_P] * 11),
+    "clad3dgs_raster_sh_seeds": (c_int, [c_int] + [_P] * 5),
     "clad3dgs_raster_forward_2d": (c_int, [c_int] + [_P] * 5 + [c_int, c_int, _P, _P, _P,
                                                                _P, _P, POINTER(c_int), _P]),
     "clad3dgs_gaussian_step_host_static": (c_int, [c_int64, c_int] + [_P] * 12

@@ -34,6 +34,7 @@ FLAGS = {
     "gaussian_step.cu": ["-fmad=false"],
     "host_step.cu": [],
     "rasterizer.cu": [],
+    "sh_backward.cu": ["-fmad=false"],
     "train_step.cu": ["-fmad=false"],
 }
 

@@ -173,12 +173,17 @@ constexpr double kOneMinusBeta2 = 1.0 - kBeta2;
 // rounding to float lands on the same value (division by a constant known in
 // advance; Brisebarre, Muller, Raina, IEEE Trans. Computers 53(8), 2004). The
 // oracle divides directly; the bit-exact tests compare the two.
+//
+// Every product and sum of the moment updates is rounded on its own (the _rn
+// intrinsics are never contracted into fused multiply-adds), so the results
+// do not depend on the translation unit's -fmad setting.
 __device__ __forceinline__ void torch_adam(float& p, float& m, float& v,
                                            float g, float step,
                                            double inv_bias2) {
   const double gd = (double)g;
-  m = (float)(kBeta1 * (double)m + kOneMinusBeta1 * gd);
-  v = (float)(kBeta2 * (double)v + (kOneMinusBeta2 * gd) * gd);
+  m = (float)__dadd_rn(__dmul_rn(kBeta1, (double)m), __dmul_rn(kOneMinusBeta1, gd));
+  v = (float)__dadd_rn(__dmul_rn(kBeta2, (double)v),
+                       __dmul_rn(__dmul_rn(kOneMinusBeta2, gd), gd));
   const float ratio = (float)((double)sqrtf(v) * inv_bias2);
   // fl32(ratio + 1e-15) equals ratio whenever ratio >= 2^-25: half an ulp of
   // such a ratio is at least 2^-49 (about 1.78e-15), more than 1e-15, even after

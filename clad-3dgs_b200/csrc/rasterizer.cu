@@ -40,6 +40,7 @@
 #include "clad3dgs_b200.h"
 #include "gaussian_math.cuh"
 #include "raster_math.cuh"
+#include "sh_colour.cuh"
 
 namespace clad3dgs {
 int fail(int code, const std::string& message);  // gaussian_step.cu
@@ -240,68 +241,6 @@ BinningState binning_from(char* base, uint32_t n, uint32_t m, int grid_x, int gr
   b.scan_bytes = tile_scan_bytes(tiles);
   b.scan_tmp = take(b.scan_bytes);
   return b;
-}
-
-// ---------------------------------------------------------------------------
-// SH colour access for packed [P][16][3] or split dc [P][3] + rest [P][45].
-
-struct ShSource {
-  const float* packed;
-  const float* dc;
-  const float* rest;
-  __device__ __forceinline__ const float* term(int i, int j) const {
-    if (packed) return packed + 48 * size_t(i) + 3 * j;
-    return j == 0 ? dc + 3 * size_t(i) : rest + 45 * size_t(i) + 3 * (j - 1);
-  }
-};
-
-// Coefficients of one Gaussian staged in a shared-memory row ([16][3]).
-struct RowSource {
-  float* row;
-  __device__ __forceinline__ const float* term(int, int j) const { return row + 3 * j; }
-};
-
-template <int J, class Source>
-__device__ __forceinline__ void colour_terms(const Direction& d, const Source& sh, int i,
-                                             int nterms, float rgb[3]) {
-  if constexpr (J < 16) {
-    if (J < nterms) {
-      float b, gx, gy, gz;
-      sh_basis<J>(d, b, gx, gy, gz);
-      const float* c = sh.term(i, J);
-      rgb[0] += b * c[0];
-      rgb[1] += b * c[1];
-      rgb[2] += b * c[2];
-      colour_terms<J + 1>(d, sh, i, nterms, rgb);
-    }
-  }
-}
-
-// SH backward for one Gaussian: d colour / d coefficients (optional) and the
-// adjoint of the view direction.
-template <int J, class Source>
-__device__ __forceinline__ void colour_adjoint_terms(const Direction& d, const Source& sh,
-                                                     int i, int nterms, const float g[3],
-                                                     float* dsh, float dd[3]) {
-  if constexpr (J < 16) {
-    float b, gx, gy, gz;
-    sh_basis<J>(d, b, gx, gy, gz);
-    if (J < nterms) {
-      const float* c = sh.term(i, J);
-      const float dot = c[0] * g[0] + c[1] * g[1] + c[2] * g[2];
-      dd[0] += gx * dot;
-      dd[1] += gy * dot;
-      dd[2] += gz * dot;
-      if (dsh) {
-        dsh[3 * J] = b * g[0];
-        dsh[3 * J + 1] = b * g[1];
-        dsh[3 * J + 2] = b * g[2];
-      }
-    } else if (dsh) {
-      dsh[3 * J] = dsh[3 * J + 1] = dsh[3 * J + 2] = 0.f;
-    }
-    colour_adjoint_terms<J + 1>(d, sh, i, nterms, g, dsh, dd);
-  }
 }
 
 struct Camera {
@@ -1092,21 +1031,18 @@ struct GeomGrads {
   const float* dmean2d;    // [P][3]
   const float* dconic;     // [P][4]
   float* dopacity;         // [P] in: w.r.t. scaled opacity; out: w.r.t. opacity
-  const float* dcolor;     // [P][3]
   const float* dinvdepth;  // [P] or null
   float* dmeans;           // [P][3] out
   float* dcov3d;           // [P][6] out
-  float* dsh;              // [P][16][3] out or null (SH adjoint consumed elsewhere)
   float* dscales;          // [P][3] out
   float* drotations;       // [P][4] out
 };
 
 __global__ void preprocess_backward_kernel(
-    int P, int degree, const float* __restrict__ means, const float* __restrict__ scales,
+    int P, const float* __restrict__ means, const float* __restrict__ scales,
     float scale_modifier, const float* __restrict__ rotations,
-    const float* __restrict__ opacities, const float* __restrict__ cov3d_precomp,
-    ShSource sh, Camera cam, bool antialiasing, const int* __restrict__ radii,
-    GeomState g, bool colours_from_sh, GeomGrads o) {
+    const float* __restrict__ opacities, const float* __restrict__ cov3d_precomp, Camera cam,
+    bool antialiasing, const int* __restrict__ radii, GeomState g, GeomGrads o) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
   if (radii[i] <= 0) {
@@ -1221,22 +1157,8 @@ __global__ void preprocess_backward_kernel(
                (cam.proj[4 * k + 1] * iw - pk3 * my) * gyn;
     }
   }
-  // SH colour -> coefficients and the view direction.
-  if (colours_from_sh) {
-    const Direction d = make_direction(p.x, p.y, p.z, cam.campos[0], cam.campos[1],
-                                       cam.campos[2]);
-    float gcol[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k) gcol[k] = g.clamped[3 * i + k] ? 0.f : o.dcolor[3 * i + k];
-    float dd[3] = {0.f, 0.f, 0.f};
-    colour_adjoint_terms<0>(d, sh, i, (degree + 1) * (degree + 1), gcol,
-                            o.dsh ? o.dsh + 48 * size_t(i) : nullptr, dd);
-    float om[3];
-    direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
-    dm[0] += om[0];
-    dm[1] += om[1];
-    dm[2] += om[2];
-  }
+  // (The SH colour's share of dmeans, the view direction's adjoint, is added
+  // by sh_backward_kernel afterwards.)
 #pragma unroll
   for (int k = 0; k < 3; ++k) o.dmeans[3 * i + k] += dm[k];
   // Sigma = M M^T, M = R diag(s): dM = 2 G M with G the symmetric adjoint.
@@ -1283,25 +1205,6 @@ __global__ void preprocess_backward_kernel(
   }
 }
 
-// The SH kernels work on 32 Gaussians per warp: the warp stages its block of
-// coefficients in shared memory with coalesced loads (rows of 48 floats + 1,
-// so rows start in distinct banks) and each lane works in its own row.
-constexpr int kShRow = 49;
-constexpr int kShWarps = 4;
-
-__device__ __forceinline__ void stage_coefficients(const ShSource& sh, int i0, int n, int lane,
-                                                   float* blk) {
-  if (sh.packed) {
-    const float* src = sh.packed + 48 * size_t(i0);
-    for (int e = lane; e < n * 48; e += 32) blk[(e / 48) * kShRow + e % 48] = src[e];
-  } else {
-    const float* dc = sh.dc + 3 * size_t(i0);
-    const float* rest = sh.rest + 45 * size_t(i0);
-    for (int e = lane; e < n * 3; e += 32) blk[(e / 3) * kShRow + e % 3] = dc[e];
-    for (int e = lane; e < n * 45; e += 32) blk[(e / 45) * kShRow + 3 + e % 45] = rest[e];
-  }
-}
-
 // SH colour of every drawn Gaussian (radius > 0): colour + 0.5, clamped at 0,
 // with the clamp flags the backward reads.
 __global__ void __launch_bounds__(32 * kShWarps)
@@ -1329,50 +1232,12 @@ __global__ void __launch_bounds__(32 * kShWarps)
   }
 }
 
-// SH colour -> coefficients and view direction: each lane reads coefficient j
-// of its row before overwriting it with dL/dsh_j, and the warp stores the
-// dL/dsh block coalesced. The direction adjoint is added into dmeans after the
-// geometry backward's share (dmeans is zeroed by the caller, so the sum rounds
-// as the single sum would).
-
-__global__ void __launch_bounds__(32 * kShWarps)
-    sh_backward_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
-                       const float* __restrict__ campos, GeomState g,
-                       const int* __restrict__ radii, const float* __restrict__ dcolor,
-                       float* __restrict__ dsh, float* __restrict__ dmeans) {
-  __shared__ float rows[kShWarps][32 * kShRow];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* blk = rows[warp];
-  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
-  if (i0 >= P) return;  // whole warp
-  const int n = min(32, P - i0);
-  stage_coefficients(sh, i0, n, lane, blk);
-  __syncwarp();
-  float* row = blk + lane * kShRow;
-  const int i = i0 + lane;
-  if (lane < n) {
-    if (radii[i] > 0) {
-      const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
-                                         campos[0], campos[1], campos[2]);
-      float gcol[3];
-#pragma unroll
-      for (int k = 0; k < 3; ++k) gcol[k] = g.clamped[3 * i + k] ? 0.f : dcolor[3 * i + k];
-      float dd[3] = {0.f, 0.f, 0.f};
-      colour_adjoint_terms<0>(d, RowSource{row}, i, (degree + 1) * (degree + 1), gcol, row, dd);
-      float om[3];
-      direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
-#pragma unroll
-      for (int k = 0; k < 3; ++k) dmeans[3 * i + k] += om[k];
-    } else {
-#pragma unroll
-      for (int k = 0; k < 48; ++k) row[k] = 0.f;
-    }
-  }
-  __syncwarp();
-  if (!dsh) return;  // direction adjoint only
-  float* dst = dsh + 48 * size_t(i0);
-  for (int e = lane; e < n * 48; e += 32) dst[e] = blk[(e / 48) * kShRow + e % 48];
-}
+// The SH backward (sh_backward.cu, compiled without contraction so that the
+// data-parallel exchange's seed form rounds exactly alike).
+cudaError_t launch_sh_backward(int P, int degree, const float* means, ShSource sh,
+                               const float* campos, const bool* clamped, const int* radii,
+                               const float* dcolor, float* dsh, float* dmeans,
+                               cudaStream_t stream);
 
 }  // namespace raster
 }  // namespace clad3dgs
@@ -1619,6 +1484,8 @@ extern "C" int clad3dgs_raster_backward(
     TorchAdamConfig xyz_config, cudaStream_t stream) {
   if (degree < 0 || degree > 3)
     return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
+  if (consume_sh < 0 || consume_sh > 2)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "consume_sh must be 0, 1 or 2");
   if (P <= 0) return CLAD3DGS_OK;
   int status = clad3dgs_raster_render_backward(
       P, width, height, bg, geom_buffer, binning_buffer, num_rendered, image_buffer, dpixels,
@@ -1628,21 +1495,20 @@ extern "C" int clad3dgs_raster_backward(
   const Camera cam = make_camera(view, proj, campos, width, height, tan_x, tan_y);
   GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
   const ShSource sh{sh_packed, sh_dc, sh_rest};
-  GeomGrads o{dmean2d, dconic_scratch, dopacity, dcolor,
-              dinvdepth_pixels ? dinvdepth_scratch : nullptr,
-              dmeans, dcov3d, consume_sh ? nullptr : dsh, dscales, drotations};
+  GeomGrads o{dmean2d, dconic_scratch, dopacity, dinvdepth_pixels ? dinvdepth_scratch : nullptr,
+              dmeans, dcov3d, dscales, drotations};
   const bool from_sh = colors_precomp == nullptr && !consume_sh;
   preprocess_backward_kernel<<<(P + 255) / 256, 256, 0, stream>>>(
-      P, degree, means, scales, scale_modifier, rotations, opacities, cov3d_precomp, sh, cam,
-      antialiasing != 0, radii, g, false, o);
+      P, means, scales, scale_modifier, rotations, opacities, cov3d_precomp, cam,
+      antialiasing != 0, radii, g, o);
   if (from_sh) {
-    const int warps = (P + 31) / 32;
-    sh_backward_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
-        P, degree, means, sh, campos, g, radii, dcolor, dsh, dmeans);
+    const cudaError_t e = launch_sh_backward(P, degree, means, sh, campos, g.clamped, radii,
+                                             dcolor, dsh, dmeans, stream);
+    if (e != cudaSuccess) return status_of(e, "SH backward");
   }
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) return status_of(e, "geometry backward");
-  if (consume_sh && colors_precomp == nullptr) {
+  if (consume_sh == 1 && colors_precomp == nullptr) {
     if (xyz_first)  // the positions' Adam too; means are updated after every read of them
       return clad3dgs_sh_consume_xyz(P, degree, const_cast<float*>(means), radii, sh_packed,
                                      g.clamped, campos, dcolor, dmeans, dc, rest, dc_first,
@@ -1653,6 +1519,56 @@ extern "C" int clad3dgs_raster_backward(
         dc_first, dc_second, rest_first, rest_second, config, stream);
   }
   return CLAD3DGS_OK;
+}
+
+namespace clad3dgs {
+namespace raster {
+__global__ void sh_seed_kernel(int P, const int* __restrict__ radii,
+                               const bool* __restrict__ clamped,
+                               const float* __restrict__ dcolor, float4* __restrict__ seeds) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (radii[i] > 0) {
+    s.x = clamped[3 * i] ? 0.f : dcolor[3 * i];
+    s.y = clamped[3 * i + 1] ? 0.f : dcolor[3 * i + 1];
+    s.z = clamped[3 * i + 2] ? 0.f : dcolor[3 * i + 2];
+    s.w = 1.f;
+  }
+  seeds[i] = s;
+}
+}  // namespace raster
+}  // namespace clad3dgs
+
+extern "C" int clad3dgs_raster_sh_backward(int P, int degree, const float* means,
+                                           const int* radii, const float* sh_packed,
+                                           const float* sh_dc, const float* sh_rest,
+                                           const float* campos, const bool* clamped,
+                                           const float* dcolor, float* dsh, float* dmeans,
+                                           cudaStream_t stream) {
+  if (degree < 0 || degree > 3)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
+  if (P <= 0) return CLAD3DGS_OK;
+  if (!means || !radii || !campos || !clamped || !dcolor || !dmeans ||
+      !(sh_packed || (sh_dc && sh_rest)))
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH backward: null pointer");
+  return status_of(launch_sh_backward(P, degree, means, ShSource{sh_packed, sh_dc, sh_rest},
+                                      campos, clamped, radii, dcolor, dsh, dmeans, stream),
+                   "SH backward");
+}
+
+extern "C" int clad3dgs_raster_sh_seeds(int P, const int* radii, const void* geom_buffer,
+                                        const float* dcolor, float* seeds,
+                                        cudaStream_t stream) {
+  if (P <= 0) return CLAD3DGS_OK;
+  if (!radii || !geom_buffer || !dcolor || !seeds)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH seeds: null pointer");
+  if (reinterpret_cast<uintptr_t>(seeds) & 15u)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "SH seeds: the seed array must be 16-byte aligned");
+  const GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
+  sh_seed_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, radii, g.clamped, dcolor,
+                                                      reinterpret_cast<float4*>(seeds));
+  return status_of(cudaPeekAtLastError(), "SH seeds");
 }
 
 namespace clad3dgs {

@@ -1,0 +1,308 @@
+// The SH backward, in its two forms, in one translation unit compiled without
+// multiply-add contraction (every product and sum rounded on its own, in
+// source order), so that both forms give the same bits:
+//
+// * the rasterizer's, per view (sh_backward_kernel): d colour / d
+//   coefficients and the view direction's adjoint of every drawn Gaussian;
+// * the seed form of the data-parallel exchange for the SH and position
+//   groups (shard_seed_kernel), below.
+//
+// Seed form. Every rank renders its own view. Instead of the 48 SH gradients of every
+// Gaussian, a rank publishes the colour seed of its view (dL/dcolour with the
+// clamped channels zeroed and a drawn flag: 16 bytes) plus the geometry part
+// of its position gradient. The owner of a share evaluates, for each of its
+// Gaussians and each view q in rank order, the SH backward of view q's colour
+// (sh_colour.cuh, the rasterizer's own arithmetic) and the view direction's
+// adjoint, sums them as the per-view gradients would be
+// summed, and runs torch-fused Adam on the 48 coefficients and 3 positions,
+// storing the parameters into every replica. The other groups (scaling,
+// rotation, opacity) go through the chunked update of train_step.cu.
+//
+// One warp per 32 Gaussians: the warp stages its coefficient block and its
+// gradient sums in shared memory (rows of 48 floats + 1, so each lane's row
+// starts in its own bank), each lane works through its Gaussian's views, and
+// the Adam pass over the block is coalesced.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "clad3dgs_b200.h"
+#include "gaussian_math.cuh"
+#include "sh_colour.cuh"
+
+namespace clad3dgs {
+int fail(int code, const std::string& message);  // gaussian_step.cu
+}
+
+namespace clad3dgs {
+namespace raster {
+
+// Per view: each lane reads coefficient j of its row before overwriting it
+// with dL/dsh_j, and the warp stores the dL/dsh block coalesced. The direction
+// adjoint is added into dmeans after the geometry backward's share (dmeans is
+// zeroed by the caller, so the sum rounds as the single sum would).
+__global__ void __launch_bounds__(32 * kShWarps)
+    sh_backward_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
+                       const float* __restrict__ campos, const bool* __restrict__ clamped,
+                       const int* __restrict__ radii, const float* __restrict__ dcolor,
+                       float* __restrict__ dsh, float* __restrict__ dmeans) {
+  __shared__ float rows[kShWarps][32 * kShRow];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* blk = rows[warp];
+  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
+  if (i0 >= P) return;  // whole warp
+  const int n = min(32, P - i0);
+  stage_coefficients(sh, i0, n, lane, blk);
+  __syncwarp();
+  float* row = blk + lane * kShRow;
+  const int i = i0 + lane;
+  if (lane < n) {
+    if (radii[i] > 0) {
+      const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
+                                         campos[0], campos[1], campos[2]);
+      float gcol[3];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) gcol[k] = clamped[3 * i + k] ? 0.f : dcolor[3 * i + k];
+      float dd[3] = {0.f, 0.f, 0.f};
+      colour_adjoint_terms<0>(d, RowSource{row}, i, (degree + 1) * (degree + 1), gcol,
+                              CoefficientStore{row}, dd);
+      float om[3];
+      direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dmeans[3 * i + k] = dmeans[3 * i + k] + om[k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 48; ++k) row[k] = 0.f;
+    }
+  }
+  __syncwarp();
+  if (!dsh) return;  // direction adjoint only
+  float* dst = dsh + 48 * size_t(i0);
+  for (int e = lane; e < n * 48; e += 32) dst[e] = blk[(e / 48) * kShRow + e % 48];
+}
+
+cudaError_t launch_sh_backward(int P, int degree, const float* means, ShSource sh,
+                               const float* campos, const bool* clamped, const int* radii,
+                               const float* dcolor, float* dsh, float* dmeans,
+                               cudaStream_t stream) {
+  const int warps = (P + 31) / 32;
+  sh_backward_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
+      P, degree, means, sh, campos, clamped, radii, dcolor, dsh, dmeans);
+  return cudaGetLastError();
+}
+
+}  // namespace raster
+
+namespace train {
+
+constexpr int kSeedWarps = 2;  // shared memory per warp: 12.5 KB (6.3 KB with one view)
+constexpr int kSeedRow = raster::kShRow;
+constexpr int kSeedRanks = CLAD3DGS_MAX_RANKS;
+
+struct SeedParams {
+  int64_t begin, end;
+  int local, nterms;
+  const float4* seeds[kSeedRanks];
+  const float* cameras[kSeedRanks];
+  const float* geo_xyz[kSeedRanks];  // geometry part of each view's position gradient
+  float* sh[kSeedRanks];             // parameter replicas [N][48]
+  float* xyz[kSeedRanks];            // parameter replicas [N][3]
+  float* sh_first;                   // moments of the share
+  float* sh_second;
+  float* xyz_first;
+  float* xyz_second;
+  float step_xyz, step_dc, step_rest;
+  double inv_bias2;
+};
+
+// With one view the gradient row overwrites the coefficient row in place
+// (each term's coefficients are read before its gradients are written) and
+// the Adam pass reloads the parameters: half the shared memory, twice the
+// resident warps.
+template <int R>
+__global__ void __launch_bounds__(32 * kSeedWarps)
+    shard_seed_kernel(const __grid_constant__ SeedParams a) {
+  constexpr bool kInPlace = R == 1;
+  __shared__ float rows[kSeedWarps][(kInPlace ? 1 : 2) * 32 * kSeedRow];
+  __shared__ float cams[R][3];
+  using raster::CoefficientSum;
+  using raster::RowSource;
+  if (threadIdx.x < 3 * R) {
+    const int q = threadIdx.x / 3, k = threadIdx.x % 3;
+    cams[q][k] = a.cameras[q][k];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = a.begin + (int64_t(blockIdx.x) * kSeedWarps + warp) * 32;
+  if (i0 >= a.end) return;  // whole warp
+  const int n = int(a.end - i0 < 32 ? a.end - i0 : 32);
+  float* cb = rows[warp];
+  float* sb = kInPlace ? cb : cb + 32 * kSeedRow;
+  // The block's coefficients, as float4 chunks (a chunk never straddles two
+  // Gaussians: 48 = 12 x 4), every load independent.
+  const int chunks = n * 12;
+  const float4* src = reinterpret_cast<const float4*>(a.sh[a.local] + 48 * i0);
+  for (int c = lane; c < chunks; c += 32) {
+    const float4 v = src[c];
+    float* dst = cb + (c / 12) * kSeedRow + 4 * (c % 12);
+    dst[0] = v.x;
+    dst[1] = v.y;
+    dst[2] = v.z;
+    dst[3] = v.w;
+  }
+  __syncwarp();
+  if (lane < n) {
+    const int64_t i = i0 + lane;
+    const float* row = cb + lane * kSeedRow;
+    float* sum = sb + lane * kSeedRow;
+    float pos[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) pos[k] = a.xyz[a.local][3 * i + k];
+    // Every view's loads first (independent, many in flight over NVLink).
+    float4 seed[R];
+    float geo[R][3];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      seed[q] = a.seeds[q][i];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) geo[q][k] = a.geo_xyz[q][3 * i + k];
+    }
+    float x[3];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      float xq[3];
+      if (seed[q].w != 0.f) {
+        const Direction d = make_direction(pos[0], pos[1], pos[2], cams[q][0], cams[q][1],
+                                           cams[q][2]);
+        const float g3[3] = {seed[q].x, seed[q].y, seed[q].z};
+        float dd[3] = {0.f, 0.f, 0.f};
+        raster::colour_adjoint_terms<0>(d, RowSource{row}, int(i), a.nterms, g3,
+                                        CoefficientSum{sum, q == 0}, dd);
+        float om[3];
+        direction_vjp(d, dd[0], dd[1], dd[2], om[0], om[1], om[2]);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) xq[k] = geo[q][k] + om[k];
+      } else {
+        // Not drawn in view q: its SH gradient is zero and its position
+        // gradient the geometry part alone.
+        for (int k = 0; k < 48; ++k) sum[k] = q == 0 ? 0.f : sum[k] + 0.f;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) xq[k] = geo[q][k];
+      }
+#pragma unroll
+      for (int k = 0; k < 3; ++k) x[k] = q == 0 ? xq[k] : x[k] + xq[k];
+    }
+    const int64_t mx = 3 * (i - a.begin);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float p = pos[k], m = a.xyz_first[mx + k], v = a.xyz_second[mx + k];
+      torch_adam(p, m, v, x[k], a.step_xyz, a.inv_bias2);
+      a.xyz_first[mx + k] = m;
+      a.xyz_second[mx + k] = v;
+#pragma unroll
+      for (int q = 0; q < R; ++q) __stcs(a.xyz[q] + 3 * i + k, p);
+    }
+  }
+  __syncwarp();
+  // Adam over the block's coefficients in float4 chunks, coalesced; each
+  // lane loads its next chunk's moments before updating the current one.
+  float4* first = reinterpret_cast<float4*>(a.sh_first + 48 * (i0 - a.begin));
+  float4* second = reinterpret_cast<float4*>(a.sh_second + 48 * (i0 - a.begin));
+  float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = m4, p4 = m4;
+  if (lane < chunks) {
+    m4 = first[lane];
+    v4 = second[lane];
+    if (kInPlace) p4 = src[lane];
+  }
+  for (int c = lane; c < chunks; c += 32) {
+    float4 m_next = m4, v_next = v4, p_next = p4;
+    if (c + 32 < chunks) {
+      m_next = first[c + 32];
+      v_next = second[c + 32];
+      if (kInPlace) p_next = src[c + 32];
+    }
+    const int j = 4 * (c % 12), at = (c / 12) * kSeedRow + j;
+    float p[4];
+    if (kInPlace) {
+      p[0] = p4.x, p[1] = p4.y, p[2] = p4.z, p[3] = p4.w;
+    } else {
+      p[0] = cb[at], p[1] = cb[at + 1], p[2] = cb[at + 2], p[3] = cb[at + 3];
+    }
+    float m[4] = {m4.x, m4.y, m4.z, m4.w}, v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      torch_adam(p[t], m[t], v[t], sb[at + t], j + t < 3 ? a.step_dc : a.step_rest,
+                 a.inv_bias2);
+    first[c] = make_float4(m[0], m[1], m[2], m[3]);
+    second[c] = make_float4(v[0], v[1], v[2], v[3]);
+    const float4 out = make_float4(p[0], p[1], p[2], p[3]);
+#pragma unroll
+    for (int q = 0; q < R; ++q) __stcs(reinterpret_cast<float4*>(a.sh[q] + 48 * i0) + c, out);
+    m4 = m_next;
+    v4 = v_next;
+    p4 = p_next;
+  }
+  // Make the peer stores visible system-wide before the kernel retires.
+  if (R > 1) __threadfence_system();
+}
+
+template <int R>
+cudaError_t launch_seed(const SeedParams& p, cudaStream_t stream) {
+  const int64_t warps = (p.end - p.begin + 31) / 32;
+  const int64_t blocks = (warps + kSeedWarps - 1) / kSeedWarps;
+  shard_seed_kernel<R><<<unsigned(blocks), 32 * kSeedWarps, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* p);  // train_step.cu
+
+// The SH and position groups of clad3dgs_shard_update in seed form (the
+// arguments are validated by the caller, except the seed fields).
+int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream) {
+  if (x.degree < 0 || x.degree > 3)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard update: SH degree must be 0..3");
+  if (x.grad_origin != 0)
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "shard update: the seed form needs full gradient arrays (grad_origin 0)");
+  SeedParams p{};
+  p.begin = x.begin;
+  p.end = x.end;
+  p.local = x.local;
+  p.nterms = (x.degree + 1) * (x.degree + 1);
+  for (int q = 0; q < x.ranks; ++q) {
+    if (!x.seeds[q] || !x.cameras[q] || !aligned16(x.seeds[q]))
+      return fail(CLAD3DGS_INVALID_ARGUMENT,
+                  "shard update: every rank needs a 16-byte aligned seed array and a camera");
+    p.seeds[q] = reinterpret_cast<const float4*>(x.seeds[q]);
+    p.cameras[q] = x.cameras[q];
+    p.geo_xyz[q] = x.grads[q][0];
+    p.sh[q] = x.params[q][1];
+    p.xyz[q] = x.params[q][0];
+  }
+  p.sh_first = x.first[1];
+  p.sh_second = x.second[1];
+  p.xyz_first = x.first[0];
+  p.xyz_second = x.second[0];
+  p.step_xyz = float(x.rates[0] / double(x.bias1));
+  p.step_dc = float(x.rates[1] / double(x.bias1));
+  p.step_rest = float(x.rates[2] / double(x.bias1));
+  p.inv_bias2 = 1.0 / double(x.bias2_sqrt);
+  cudaError_t e = cudaSuccess;
+  switch (x.ranks) {
+    case 1: e = launch_seed<1>(p, stream); break;
+    case 2: e = launch_seed<2>(p, stream); break;
+    case 3: e = launch_seed<3>(p, stream); break;
+    case 4: e = launch_seed<4>(p, stream); break;
+    case 5: e = launch_seed<5>(p, stream); break;
+    case 6: e = launch_seed<6>(p, stream); break;
+    case 7: e = launch_seed<7>(p, stream); break;
+    default: e = launch_seed<8>(p, stream); break;
+  }
+  return e == cudaSuccess ? CLAD3DGS_OK
+                          : fail(CLAD3DGS_CUDA_ERROR, std::string("shard update (seeds): ") +
+                                                          cudaGetErrorString(e));
+}
+
+}  // namespace train
+}  // namespace clad3dgs

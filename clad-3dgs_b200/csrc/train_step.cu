@@ -96,6 +96,7 @@ int blocks_for(int64_t work);
 
 struct ShardParams {
   int64_t begin, end, grad_origin;
+  int64_t chunk_begin;  // first float4 chunk updated here (past xyz and SH in seed form)
   int ranks, local;
   const float* grads[kMaxRanks][kGroups];
   float* params[kMaxRanks][kGroups];
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, R <= 2 ? 4 : 3)
   // Chunk boundaries of the five groups (float4 chunks of the owned spans).
   const int64_t c0 = n * 3 / 4, c1 = c0 + n * 12, c2 = c1 + n * 3 / 4, c3 = c2 + n,
                 c4 = c3 + n / 4;
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < c4;
+  for (int64_t c = a.chunk_begin + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < c4;
        c += (int64_t)gridDim.x * blockDim.x) {
     int g;
     int64_t local;
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, R <= 4 ? 3 : 2)
   const int64_t n = a.end - a.begin;  // a multiple of 4
   const int64_t chunks = n * 59 / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  int64_t c = a.chunk_begin + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= chunks) return;
   Chunk<R> cur;
   load_chunk<R>(a, c, n, cur);
@@ -299,10 +300,11 @@ __global__ void __launch_bounds__(kThreads, R <= 4 ? 3 : 2)
 
 template <int R>
 cudaError_t launch_shard_update(const ShardParams& p, int64_t chunks, cudaStream_t stream) {
+  const int blocks = blocks_for(chunks - p.chunk_begin);
   if constexpr (R == 1)
-    shard_update_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
+    shard_update_kernel<R><<<blocks, kThreads, 0, stream>>>(p);
   else
-    shard_update_prefetch_kernel<R><<<blocks_for(chunks), kThreads, 0, stream>>>(p);
+    shard_update_prefetch_kernel<R><<<blocks, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -316,6 +318,8 @@ int blocks_for(int64_t work) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream);  // shard_sh.cu
 
 }  // namespace train
 }  // namespace clad3dgs
@@ -371,6 +375,7 @@ extern "C" int clad3dgs_shard_update(const clad3dgs_shard_update_args* args,
   if (!(x.bias1 > 0.f) || !(x.bias2_sqrt > 0.f))
     return fail(CLAD3DGS_INVALID_ARGUMENT, "shard update: bias corrections must be positive");
   if (x.end == x.begin) return CLAD3DGS_OK;
+  const bool seeded = x.seeds[0] != nullptr;
   ShardParams p{};
   p.begin = x.begin;
   p.end = x.end;
@@ -379,7 +384,8 @@ extern "C" int clad3dgs_shard_update(const clad3dgs_shard_update_args* args,
   p.local = x.local;
   for (int g = 0; g < kGroups; ++g) {
     for (int q = 0; q < x.ranks; ++q) {
-      if (!x.grads[q][g] || !x.params[q][g] || !aligned16(x.grads[q][g]) ||
+      const bool unused = seeded && g == 1;  // the SH gradients come from the seeds
+      if ((!unused && (!x.grads[q][g] || !aligned16(x.grads[q][g]))) || !x.params[q][g] ||
           !aligned16(x.params[q][g]))
         return fail(CLAD3DGS_INVALID_ARGUMENT,
                     "shard update: gradient and parameter arrays must be non-null and "
@@ -402,7 +408,13 @@ extern "C" int clad3dgs_shard_update(const clad3dgs_shard_update_args* args,
   p.saved_norm = x.saved_norm;
   for (int r = 0; r < kGroups + 1; ++r) p.step[r] = float(x.rates[r] / double(x.bias1));
   p.inv_bias2 = 1.0 / double(x.bias2_sqrt);
-  const int64_t chunks = (x.end - x.begin) * 59 / 4;
+  const int64_t n = x.end - x.begin;
+  const int64_t chunks = n * 59 / 4;
+  if (seeded) {
+    const int status = shard_seed_update(x, stream);
+    if (status != CLAD3DGS_OK) return status;
+    p.chunk_begin = n * 3 / 4 + n * 12;  // past the xyz and SH chunks
+  }
   cudaError_t e = cudaSuccess;
   switch (x.ranks) {
     case 1: e = launch_shard_update<1>(p, chunks, stream); break;

@@ -23,6 +23,19 @@ per-Gaussian update path. Per step on every rank:
      parameter group through torch.distributed (the NCCL baseline; gloo in the
      CPU tests).
 
+   What a rank publishes for the SH coefficients (``sh_exchange``):
+
+   * ``"seeds"`` (default on CUDA unless the exchange is the collective one
+     with more than one rank): the rasterizer backward stops before the SH
+     backward (consume_sh = 2) and the rank publishes its view's colour seeds
+     (dL/dcolour with clamped channels zeroed, and a drawn flag: 16 B per
+     Gaussian instead of 192 B of SH gradients) and its camera position; the
+     owner of a share evaluates every view's SH backward and view-direction
+     adjoint inside the update, summed in rank order, bit-identical to the
+     gradient form.
+   * ``"grads"``: each rank writes its full SH gradients and the update sums
+     them (the form a collective reduce-scatter needs).
+
 Barriers are one-element all-reduces on the compute stream, so they order the
 GPUs' streams without a host wait.
 
@@ -105,6 +118,9 @@ class ShardStep(NamedTuple):
     rates: tuple      # 6 rates: xyz, f_dc, f_rest, scaling, rotation, opacity
     bias1: float
     bias2_sqrt: float
+    seeds: list = None    # seed form: [ranks] colour seed arrays [N][4]
+    cameras: list = None  # seed form: [ranks] camera positions (3 floats)
+    degree: int = 3       # seed form: SH degree
 
 
 def _address(x):
@@ -129,6 +145,11 @@ def native_update(s: ShardStep, stream=None):
     for r, rate in enumerate(s.rates):
         args.rates[r] = float(rate)
     args.bias1, args.bias2_sqrt = float(s.bias1), float(s.bias2_sqrt)
+    if s.seeds is not None:
+        for q in range(len(s.seeds)):
+            args.seeds[q] = _address(s.seeds[q])
+            args.cameras[q] = _address(s.cameras[q])
+        args.degree = int(s.degree)
     native.check(native.library().clad3dgs_shard_update(ctypes.byref(args),
                                                         native.stream_handle(stream)),
                  "shard update")
@@ -140,11 +161,13 @@ class ShardedAdam:
 
     Attributes: `params` / `grads` (dicts of [padded, k] views, replicated /
     this rank's view), `first` / `second` (moments of the share [begin, end)),
-    `saved` (activated scaling / rotation / opacity and |q|, [padded, .]).
+    `saved` (activated scaling / rotation / opacity and |q|, [padded, .]); in
+    seed form `seeds` ([padded, 4], this rank's view) and `camera` (its
+    position, 3 floats), written before each step.
     """
 
     def __init__(self, n, rates=None, *, group=None, exchange=None, device=None,
-                 update=None):
+                 update=None, sh_exchange=None, degree=3):
         self.group = group
         self.distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if self.distributed else 1
@@ -158,6 +181,17 @@ class ShardedAdam:
         if exchange == "peer" and self.device.type != "cuda":
             raise ValueError("the peer exchange needs CUDA devices")
         self.exchange = exchange
+        if sh_exchange is None:
+            collective = exchange == "collective" and self.world > 1
+            sh_exchange = "seeds" if self.device.type == "cuda" and not collective else "grads"
+        if sh_exchange not in ("seeds", "grads"):
+            raise ValueError("sh_exchange must be 'seeds' or 'grads'")
+        if sh_exchange == "seeds" and exchange == "collective" and self.world > 1:
+            raise ValueError("the collective exchange reduces SH gradients: use 'grads'")
+        if sh_exchange == "seeds" and self.device.type != "cuda":
+            raise ValueError("the seed form needs CUDA devices")
+        self.sh_exchange = sh_exchange
+        self.degree = int(degree)
         self.rates = dict(DEFAULT_RATES if rates is None else rates)
         missing = [r for r in RATE_NAMES if r not in self.rates]
         if missing:
@@ -171,15 +205,30 @@ class ShardedAdam:
         total = FLOATS_PER_GAUSSIAN * self.padded
         self._own = []
         self._peers = []
+        # Seed slab: the camera position (4 floats, so the seeds stay 16-byte
+        # aligned), then [padded, 4] seeds; padding Gaussians keep zero seeds.
+        seed_total = 4 + 4 * self.padded if sh_exchange == "seeds" else 0
         if exchange == "peer" and self.world > 1:
             param_slab, param_handle = self._ipc_slab(total)
             grad_slab, grad_handle = self._ipc_slab(total)
+            seed_slab, seed_handle = (self._ipc_slab(seed_total) if seed_total
+                                      else (None, None))
         else:
             param_slab = torch.zeros(total, dtype=torch.float32, device=self.device)
             grad_slab = torch.zeros(total, dtype=torch.float32, device=self.device)
-        self.param_slab, self.grad_slab = param_slab, grad_slab
+            seed_slab = (torch.zeros(seed_total, dtype=torch.float32, device=self.device)
+                         if seed_total else None)
+            seed_handle = None
+        self.param_slab, self.grad_slab, self.seed_slab = param_slab, grad_slab, seed_slab
         self.params = carve(param_slab, self.padded)
         self.grads = carve(grad_slab, self.padded)
+        if seed_slab is not None:
+            if exchange == "peer" and self.world > 1:
+                seed_slab.zero_()
+            self.camera = seed_slab[:3]
+            self.seeds = seed_slab[4:].view(self.padded, 4)
+        else:
+            self.camera = self.seeds = None
         zeros = lambda *s: torch.zeros(s, dtype=torch.float32, device=self.device)
         self.first = carve(zeros(FLOATS_PER_GAUSSIAN * self.share), self.share)
         self.second = carve(zeros(FLOATS_PER_GAUSSIAN * self.share), self.share)
@@ -189,7 +238,7 @@ class ShardedAdam:
             self.reduced = carve(zeros(FLOATS_PER_GAUSSIAN * self.share), self.share)
         self._flag = zeros(1)
         if exchange == "peer" and self.world > 1:
-            self._open_peers(param_handle, grad_handle)
+            self._open_peers(param_handle, grad_handle, seed_handle)
 
     # -- CUDA IPC memory -------------------------------------------------
     def _ipc_slab(self, count):
@@ -201,20 +250,23 @@ class ShardedAdam:
         tensor = torch.as_tensor(_DeviceArray(address.value, count), device=self.device)
         return tensor, bytes(handle)
 
-    def _open_peers(self, param_handle, grad_handle):
-        mine = torch.tensor(list(param_handle + grad_handle), dtype=torch.uint8,
-                            device=self.device)
+    def _open_peers(self, param_handle, grad_handle, seed_handle=None):
+        handles = [param_handle, grad_handle] + ([seed_handle] if seed_handle else [])
+        mine = torch.tensor(list(b"".join(handles)), dtype=torch.uint8, device=self.device)
         every = torch.empty(self.world * mine.numel(), dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(every, mine, group=self.group)
-        every = every.view(self.world, 2, native.IPC_HANDLE_BYTES).cpu()
+        every = every.view(self.world, len(handles), native.IPC_HANDLE_BYTES).cpu()
         offsets = group_offsets(self.padded)
         self.peer_params, self.peer_grads = [], []
+        self.peer_seeds, self.peer_cameras = [], []
         for q in range(self.world):
             if q == self.rank:
-                bases = (self.param_slab.data_ptr(), self.grad_slab.data_ptr())
+                bases = [self.param_slab.data_ptr(), self.grad_slab.data_ptr()]
+                if seed_handle:
+                    bases.append(self.seed_slab.data_ptr())
             else:
                 bases = []
-                for which in range(2):
+                for which in range(len(handles)):
                     handle = (ctypes.c_ubyte * native.IPC_HANDLE_BYTES)(
                         *every[q, which].tolist())
                     address = ctypes.c_void_p()
@@ -225,6 +277,9 @@ class ShardedAdam:
                     bases.append(address.value)
             self.peer_params.append([bases[0] + 4 * offsets[name] for name, _ in GROUPS])
             self.peer_grads.append([bases[1] + 4 * offsets[name] for name, _ in GROUPS])
+            if seed_handle:
+                self.peer_cameras.append(bases[2])
+                self.peer_seeds.append(bases[2] + 16)
 
     def close(self):
         """Unmaps the peers' memory and frees this rank's (collective call)."""
@@ -239,8 +294,8 @@ class ShardedAdam:
         self._peers = []
         if self.distributed and self.world > 1:
             dist.barrier(group=self.group)
-        self.params = self.grads = None
-        self.param_slab = self.grad_slab = None
+        self.params = self.grads = self.seeds = self.camera = None
+        self.param_slab = self.grad_slab = self.seed_slab = None
         for address in self._own:
             native.check(native.library().clad3dgs_ipc_free(address), "ipc free")
         self._own = []
@@ -280,7 +335,7 @@ class ShardedAdam:
     def _barrier(self):
         dist.all_reduce(self._flag, group=self.group)
 
-    def _shard_step(self, grads, params, grad_origin, local):
+    def _shard_step(self, grads, params, grad_origin, local, seeds=None, cameras=None):
         t = self.t
         return ShardStep(
             begin=self.begin, end=self.end, grad_origin=grad_origin, grads=grads,
@@ -288,19 +343,25 @@ class ShardedAdam:
             second=[self.second[n] for n, _ in GROUPS], saved_scaling=self.saved["scaling"],
             saved_opacity=self.saved["opacity"], saved_norm=self.saved["norm"],
             rates=tuple(self.rates[r] for r in RATE_NAMES), bias1=1.0 - 0.9 ** t,
-            bias2_sqrt=math.sqrt(1.0 - 0.999 ** t))
+            bias2_sqrt=math.sqrt(1.0 - 0.999 ** t), seeds=seeds, cameras=cameras,
+            degree=self.degree)
 
     def step(self):
         """Sums the ranks' gradients of this rank's share, runs Adam on it and
         brings every replica up to date."""
         self.t += 1
         names = [n for n, _ in GROUPS]
+        seeded = self.sh_exchange == "seeds"
         if self.world == 1:
             self._update(self._shard_step([[self.grads[n] for n in names]],
-                                          [[self.params[n] for n in names]], 0, 0))
+                                          [[self.params[n] for n in names]], 0, 0,
+                                          [self.seeds] if seeded else None,
+                                          [self.camera] if seeded else None))
         elif self.exchange == "peer":
             self._barrier()
-            self._update(self._shard_step(self.peer_grads, self.peer_params, 0, self.rank))
+            self._update(self._shard_step(self.peer_grads, self.peer_params, 0, self.rank,
+                                          self.peer_seeds if seeded else None,
+                                          self.peer_cameras if seeded else None))
             self._barrier()
         else:
             for n in names:
@@ -378,9 +439,10 @@ class DataParallelTrainer:
     ranks exchange and update (ShardedAdam.step)."""
 
     def __init__(self, values, rates=None, *, degree=3, bg=(0.0, 0.0, 0.0), group=None,
-                 exchange=None, device=None, pixel_accumulation=2):
+                 exchange=None, device=None, pixel_accumulation=2, sh_exchange=None):
         n = int(values["xyz"].shape[0])
-        self.adam = ShardedAdam(n, rates, group=group, exchange=exchange, device=device)
+        self.adam = ShardedAdam(n, rates, group=group, exchange=exchange, device=device,
+                                sh_exchange=sh_exchange, degree=degree)
         self.adam.load(values)
         self.n, self.degree = n, int(degree)
         self.mode = int(pixel_accumulation)
@@ -414,7 +476,8 @@ class DataParallelTrainer:
             self.invdepth = torch.empty(1, H, W, dtype=torch.float32, device=a.device)
         # Only atomically accumulated arrays need clearing: the positions'
         # and opacity gradients and the pixel backward's per-Gaussian targets
-        # (the SH, scale, rotation and covariance adjoints are written outright).
+        # (the SH, scale, rotation and covariance adjoints and the seeds are
+        # written outright).
         a.zero_accumulated()
         for name in ("mean2d", "colors", "conic"):
             self.scratch_grads[name].zero_()
@@ -434,6 +497,7 @@ class DataParallelTrainer:
                                           self.dimage.data_ptr(), self.loss.data_ptr(),
                                           stream), "l1 loss")
         g, s = a.grads, self.scratch_grads
+        seeded = a.sh_exchange == "seeds"
         geom = self.buffers.tensors.get(0)
         image = self.buffers.tensors.get(1)
         binning = self.buffers.tensors.get(2)
@@ -448,7 +512,13 @@ class DataParallelTrainer:
             s["mean2d"].data_ptr(), s["colors"].data_ptr(), g["opacity"].data_ptr(),
             g["xyz"].data_ptr(), s["cov"].data_ptr(), g["sh"].data_ptr(),
             g["scaling"].data_ptr(), g["rotation"].data_ptr(), s["conic"].data_ptr(),
-            None, self.mode, 0, None, None, None, None, None, None,
+            None, self.mode, 2 if seeded else 0, None, None, None, None, None, None,
             native.TorchAdamConfig(1.0, 1.0), None, None, 0.0, native.TorchAdamConfig(1.0, 1.0),
             stream), "rasterize (backward)")
+        if seeded:
+            # This view's colour seeds and camera for the SH backward in the update.
+            native.check(lib.clad3dgs_raster_sh_seeds(
+                n, self.radii.data_ptr(), geom.data_ptr(), s["colors"].data_ptr(),
+                a.seeds.data_ptr(), stream), "SH seeds")
+            a.camera.copy_(camera.campos)
         return self.loss, rendered.value

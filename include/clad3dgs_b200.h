@@ -267,6 +267,9 @@ int clad3dgs_raster_render_backward(
  * With consume_sh and xyz_first non-null the same kernel also runs the
  * positions' Adam (clad3dgs_sh_consume_xyz): means are updated in place after
  * the geometry backward has read them; xyz_* are ignored otherwise.
+ * consume_sh = 2 defers the SH backward: neither dsh nor the view direction's
+ * share of dmeans is formed (dmeans gets the geometry part only); the colour
+ * adjoint dcolor is kept for clad3dgs_raster_sh_seeds.
  * Outputs are accumulated into zeroed tensors; dconic_scratch [P][4] and
  * dinvdepth_scratch [P] are zeroed scratch. */
 int clad3dgs_raster_backward(
@@ -283,6 +286,25 @@ int clad3dgs_raster_backward(
     float* dc_first, float* dc_second, float* rest_first, float* rest_second,
     TorchAdamConfig config, float* xyz_first, float* xyz_second, double xyz_rate,
     TorchAdamConfig xyz_config, cudaStream_t stream);
+
+/* The rasterizer's SH backward alone (its last stage, after the geometry
+ * backward): for every Gaussian with radii[i] > 0, dsh[i] (nullable, [P][48])
+ * = d colour / d coefficients applied to dcolor with the clamped channels
+ * ([P][3] bools) zeroed, and the view direction's adjoint added into
+ * dmeans[i]; dsh[i] = 0 for the others. Coefficients packed [P][16][3] or
+ * split dc [P][3] + rest [P][45]. */
+int clad3dgs_raster_sh_backward(int P, int degree, const float* means, const int* radii,
+                                const float* sh_packed, const float* sh_dc,
+                                const float* sh_rest, const float* campos,
+                                const bool* clamped, const float* dcolor, float* dsh,
+                                float* dmeans, cudaStream_t stream);
+
+/* Colour seeds of a deferred SH backward (consume_sh = 2), for the seed form
+ * of clad3dgs_shard_update: seeds[i] (16-byte aligned [P][4]) = dcolor[i]
+ * with the channels the forward clamped (geom_buffer) set to zero, then 1.0
+ * if radii[i] > 0, else all four zero. */
+int clad3dgs_raster_sh_seeds(int P, const int* radii, const void* geom_buffer,
+                             const float* dcolor, float* seeds, cudaStream_t stream);
 
 /* Binning + compositing of already projected 2D Gaussians (mean2d [P][2] px,
  * conic_opacity [P][4], rgb [P][3], depth [P], radii [P]); fills the buffers
@@ -362,7 +384,19 @@ int clad3dgs_l1_loss(int64_t n, const float* image, const float* target, float* 
  * share reduced by a collective); params and saved arrays start at Gaussian 0.
  * begin, end and grad_origin are multiples of 4; arrays are 16-byte aligned.
  * The caller orders the call after every source's gradients are complete and
- * before any replica is read again (a barrier on each side). */
+ * before any replica is read again (a barrier on each side).
+ *
+ * Seed form (seeds[0] non-null): instead of SH gradients, each rank q gives
+ * the colour seeds of its view, seeds[q] = [N][4] (dL/dcolour with clamped
+ * channels zeroed, then 1 if the Gaussian was drawn, else 0; written by
+ * clad3dgs_raster_sh_seeds) and its camera position cameras[q] (3 floats), and
+ * grads[q][0] holds only the geometry part of its position gradient (the
+ * rasterizer backward with consume_sh = 2). The update evaluates every view's
+ * SH backward (SH degree `degree`) for its share: the SH gradient is the sum
+ * over q of d colour_q / d coefficients and the position gradient the sum
+ * over q of (geometry part + view-direction adjoint), both in rank order and
+ * bit-identical to summing the per-view gradients that the full rasterizer
+ * backward writes. grads[q][1] is not read; grad_origin must be 0. */
 typedef struct clad3dgs_shard_update_args {
   int64_t begin, end, grad_origin;
   int ranks, local;
@@ -375,6 +409,9 @@ typedef struct clad3dgs_shard_update_args {
   const float* saved_norm;     /* |rotation_raw| [N] */
   double rates[CLAD3DGS_SHARD_GROUPS + 1];
   float bias1, bias2_sqrt;     /* 1 - 0.9^t, sqrt(1 - 0.999^t) */
+  const float* seeds[CLAD3DGS_MAX_RANKS];    /* seed form: [N][4] per rank, or null */
+  const float* cameras[CLAD3DGS_MAX_RANKS];  /* seed form: camera position per rank */
+  int degree;                                /* seed form: SH degree 0..3 */
 } clad3dgs_shard_update_args;
 
 int clad3dgs_shard_update(const clad3dgs_shard_update_args* args, cudaStream_t stream);

@@ -9,9 +9,15 @@
   rasterizer front end, torch activations and torch fused Adam (the path's
   tolerances: rtol 3e-5 / atol 2e-7, Adam step-1 sign flips of rounding-level
   gradients allowed);
-* on two GPUs (skipped with fewer): both exchanges (peer memory and NCCL
-  collectives), each rank's replica and moments bit-identical to the
-  emulation of the same gradients.
+* the seed form of the exchange (colour seeds per view, the SH backward
+  inside the update) bit-identical to the gradient form for 2 and 3 ranks'
+  views emulated on one GPU (the gradients formed from the same seeds by the
+  rasterizer's SH backward: two backward passes differ in the order of their
+  float atomics, so only shared inputs compare bit for bit); the trainer step
+  in both forms against the autograd path;
+* on two GPUs (skipped with fewer): both exchanges (peer memory, in seed and
+  gradient form, and NCCL collectives), each rank's replica and moments
+  bit-identical to the emulation of the same inputs.
 """
 
 import os
@@ -176,7 +182,8 @@ def _small_scene(n, cuda):
     return {k: t.to(cuda) for k, t in v.items()}
 
 
-def test_trainer_step_on_one_gpu_matches_autograd_path(cuda):
+@pytest.mark.parametrize("sh_exchange", ["seeds", "grads"])
+def test_trainer_step_on_one_gpu_matches_autograd_path(cuda, sh_exchange):
     import rasterizer
     from data_parallel import DataParallelTrainer, orbit_camera
 
@@ -185,9 +192,15 @@ def test_trainer_step_on_one_gpu_matches_autograd_path(cuda):
     cam = orbit_camera(1, 8, width=W, height=H, device=cuda)
     torch.manual_seed(1)
     target = torch.rand(3, H, W, device=cuda)
-    trainer = DataParallelTrainer(values, RATES, device=cuda)
+    trainer = DataParallelTrainer(values, RATES, device=cuda, sh_exchange=sh_exchange)
+    assert trainer.adam.sh_exchange == sh_exchange
     loss, rendered = trainer.step(cam, target)
     assert rendered > 0
+    if sh_exchange == "seeds":
+        # Drawn Gaussians carry flag 1; padding Gaussians have no seed.
+        flags = trainer.adam.seeds[:, 3]
+        assert ((flags == 0) | (flags == 1)).all() and (flags[:n] == 1).any()
+        assert (trainer.adam.seeds[n:] == 0).all()
     # The same step through the autograd front end and torch fused Adam.
     P = {k: torch.nn.Parameter(values[k].clone()) for k in ("xyz", "scaling", "rotation",
                                                              "opacity")}
@@ -233,13 +246,114 @@ def test_trainer_step_on_one_gpu_matches_autograd_path(cuda):
     trainer.close()
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_seed_form_matches_gradient_form_for_emulated_ranks(cuda, world):
+    """`world` views rendered on one GPU stand for the ranks. From each view's
+    seeds and geometry gradients, the rasterizer's own SH backward
+    (`clad3dgs_raster_sh_backward`, at the current parameters) forms the full
+    gradients; the seed-form update of every share then equals the
+    gradient-form update, bit for bit, over consecutive steps."""
+    import _native as native
+    from data_parallel import (DataParallelTrainer, ShardStep, carve, native_update,
+                               orbit_camera, plan)
+
+    n, W, H = 2400, 96, 64  # padded alike for 1, 2 and 3 ranks
+    padded, share = plan(n, world)
+    assert padded == plan(n, 1)[0]
+    values = _small_scene(n, cuda)
+    trainer = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="seeds")
+    a = trainer.adam
+    grads_s, seeds, cams = [], [], []
+    for q in range(world):
+        cam = orbit_camera(2 * q + 1, 8, width=W, height=H, device=cuda)
+        target = torch.rand(3, H, W, device=cuda,
+                            generator=torch.Generator(device=cuda).manual_seed(10 + q))
+        trainer.backward(cam, target)
+        grads_s.append(carve(a.grad_slab.clone(), padded))
+        seeds.append(a.seeds.clone())
+        cams.append(a.camera.clone())
+    names = GROUP_NAMES
+    replica_f = carve(a.param_slab.clone(), padded)
+    replica_s = carve(a.param_slab.clone(), padded)
+    saved = a.saved
+    zeros = lambda: {k: torch.zeros(share, w, device=cuda) for k, w in zip(names, WIDTHS)}
+    moments = [(zeros(), zeros(), zeros(), zeros()) for _ in range(world)]
+    clamped = torch.zeros(n, 3, dtype=torch.bool, device=cuda)
+
+    def gradient_form(q):
+        """View q's full gradients at the current parameters: SH gradients
+        and the direction adjoint from its seeds (drawn flag as radius,
+        nothing clamped) added to its geometry gradients."""
+        g_f = {k: v.clone() for k, v in grads_s[q].items()}
+        radii = (seeds[q][:n, 3] != 0).to(torch.int32)
+        dcolor = seeds[q][:n, :3].contiguous()
+        native.check(native.library().clad3dgs_raster_sh_backward(
+            n, 3, replica_f["xyz"].data_ptr(), radii.data_ptr(), replica_f["sh"].data_ptr(),
+            None, None, cams[q].data_ptr(), clamped.data_ptr(), dcolor.data_ptr(),
+            g_f["sh"].data_ptr(), g_f["xyz"].data_ptr(), native.stream_handle()),
+            "SH backward")
+        return g_f
+
+    for step in range(2):
+        b1, b2 = _bias(step + 1)
+        grads_f = [gradient_form(q) for q in range(world)]
+        for r in range(world):
+            m_f, v_f, m_s, v_s = moments[r]
+            common = dict(begin=r * share, end=(r + 1) * share, grad_origin=0, local=0,
+                          saved_scaling=saved["scaling"], saved_opacity=saved["opacity"],
+                          saved_norm=saved["norm"], rates=RATE_TUPLE, bias1=b1, bias2_sqrt=b2)
+            native_update(ShardStep(
+                grads=[[grads_f[q][k] for k in names] for q in range(world)],
+                params=[[replica_f[k] for k in names]] * world,
+                first=[m_f[k] for k in names], second=[v_f[k] for k in names], **common))
+            native_update(ShardStep(
+                grads=[[grads_s[q][k] for k in names] for q in range(world)],
+                params=[[replica_s[k] for k in names]] * world,
+                first=[m_s[k] for k in names], second=[v_s[k] for k in names],
+                seeds=seeds, cameras=cams, degree=3, **common))
+        torch.cuda.synchronize()
+        for r in range(world):
+            m_f, v_f, m_s, v_s = moments[r]
+            for k in names:
+                assert torch.equal(m_f[k], m_s[k]), (step, r, k)
+                assert torch.equal(v_f[k], v_s[k]), (step, r, k)
+        for k in names:
+            assert torch.equal(replica_f[k], replica_s[k]), (step, k)
+    # The updates moved the parameters, and SH gradients were not all zero.
+    assert not torch.equal(replica_s["sh"], a.params["sh"])
+    assert not torch.equal(replica_s["xyz"], a.params["xyz"])
+    assert sum(int((g["sh"] != 0).sum()) for g in grads_f) > 0
+    trainer.close()
+
+
+def test_seed_form_rejects_bad_arguments(cuda):
+    from data_parallel import DataParallelTrainer, ShardedAdam, native_update
+
+    with pytest.raises(ValueError):
+        ShardedAdam(64, RATES, device="cpu", sh_exchange="seeds")
+    with pytest.raises(ValueError):
+        ShardedAdam(64, RATES, device=cuda, sh_exchange="colours")
+    trainer = DataParallelTrainer(_small_scene(64, cuda), RATES, device=cuda)
+    a = trainer.adam
+    a.t = 1
+    step = a._shard_step([[a.grads[k] for k in GROUP_NAMES]],
+                         [[a.params[k] for k in GROUP_NAMES]], 0, 0, [a.seeds], [a.camera])
+    with pytest.raises(ValueError):
+        native_update(step._replace(degree=4))
+    with pytest.raises(ValueError):
+        native_update(step._replace(seeds=[a.seeds.view(-1)[1:]]))  # misaligned
+    with pytest.raises(ValueError):
+        native_update(step._replace(grad_origin=4, begin=4))
+    trainer.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _dp_worker(rank, world, port, exchange, out_dir):
+def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -254,9 +368,11 @@ def _dp_worker(rank, world, port, exchange, out_dir):
     try:
         n, W, H = 2003, 96, 64
         values = _small_scene(n, device)
-        trainer = DataParallelTrainer(values, RATES, exchange=exchange, device=device)
+        trainer = DataParallelTrainer(values, RATES, exchange=exchange, device=device,
+                                      sh_exchange=sh_exchange)
         a = trainer.adam
-        assert a.world == world and a.exchange == exchange
+        assert a.world == world and a.exchange == exchange and a.sh_exchange == sh_exchange
+        seeded = sh_exchange == "seeds"
         cam = orbit_camera(rank, 8, width=W, height=H, device=device)
         target = torch.rand(3, H, W, device=device,
                             generator=torch.Generator(device=device).manual_seed(rank))
@@ -267,6 +383,14 @@ def _dp_worker(rank, world, port, exchange, out_dir):
             every = torch.empty(world * mine.numel(), device=device)
             dist.all_gather_into_tensor(every, mine)
             every = every.view(world, -1)
+            seeds = cameras = None
+            if seeded:
+                mine = a.seed_slab.clone()
+                all_seeds = torch.empty(world * mine.numel(), device=device)
+                dist.all_gather_into_tensor(all_seeds, mine)
+                all_seeds = all_seeds.view(world, -1)
+                seeds = [all_seeds[q, 4:].view(-1, 4) for q in range(world)]
+                cameras = [all_seeds[q, :3] for q in range(world)]
             params = a.param_slab.clone()
             first = {k: v.clone() for k, v in a.first.items()}
             second = {k: v.clone() for k, v in a.second.items()}
@@ -283,7 +407,8 @@ def _dp_worker(rank, world, port, exchange, out_dir):
                                     [[replica[k] for k in names]] * world, 0,
                                     [first[k] for k in names],
                                     [second[k] for k in names], a.saved["scaling"],
-                                    a.saved["opacity"], a.saved["norm"], RATE_TUPLE, b1, b2))
+                                    a.saved["opacity"], a.saved["norm"], RATE_TUPLE, b1, b2,
+                                    seeds, cameras, 3))
             lo, hi = a.begin, a.end
             torch.cuda.synchronize()
             for k in names:
@@ -303,11 +428,13 @@ def _dp_worker(rank, world, port, exchange, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["peer", "collective"])
-def test_two_gpu_exchange_matches_emulation(cuda, exchange, tmp_path):
+@pytest.mark.parametrize("exchange,sh_exchange",
+                         [("peer", "seeds"), ("peer", "grads"), ("collective", "grads")])
+def test_two_gpu_exchange_matches_emulation(cuda, exchange, sh_exchange, tmp_path):
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.spawn(_dp_worker, args=(2, _free_port(), exchange, str(tmp_path)), nprocs=2)
+    mp.spawn(_dp_worker, args=(2, _free_port(), exchange, sh_exchange, str(tmp_path)),
+             nprocs=2)
     assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
