@@ -363,27 +363,62 @@ __global__ void gather_rows_kernel(int P, GeomState g) {
   g.depth_keys[i] = g.rows[g.order[i]];
 }
 
-// One thread per Gaussian in depth order, so the pairs are written contiguously
-// (emitting in id order, with coalesced reads but scattered writes, was slower).
-__global__ void emit_rows_kernel(int P, GeomState g, int grid_x, int grid_y,
-                                 uint32_t* __restrict__ rows_out,
-                                 uint64_t* __restrict__ spans_out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= P) return;
-  const uint32_t id = g.order[i];
-  const uint32_t n = g.rows[id];
-  if (n == 0) return;
-  const uint32_t start = i == 0 ? 0u : g.offsets[i - 1];
-  const float2 m = g.mean2d[id];
-  const Footprint f = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x,
-                                     grid_y);
-  for (uint32_t r = 0; r < n; ++r) {
-    const int ty = f.y0 + int(r);
-    int lo, hi;
-    row_span(f, ty, lo, hi);
-    if (hi < lo) hi = lo;
-    rows_out[start + r] = uint32_t(ty);
-    spans_out[start + r] = pack_pair(id, lo, hi);
+// A warp per 32 Gaussians in depth order: each lane builds one Gaussian's
+// footprint in shared memory, then the warp walks the 32 Gaussians' pairs
+// together, one pair per lane (the owner found by a search of the warp's pair
+// offsets). The Gaussians' pairs are consecutive in depth order, so the stores
+// are contiguous and no lane waits for a Gaussian with many rows. (Emitting in
+// Gaussian-id order, with coalesced reads but scattered writes, was slower.)
+constexpr int kEmitWarps = 8;
+
+__global__ void __launch_bounds__(32 * kEmitWarps)
+    emit_rows_kernel(int P, GeomState g, int grid_x, int grid_y,
+                     uint32_t* __restrict__ rows_out, uint64_t* __restrict__ spans_out) {
+  __shared__ Footprint s_fp[kEmitWarps][32];
+  __shared__ uint32_t s_id[kEmitWarps][32];
+  __shared__ uint32_t s_first[kEmitWarps][33];  // first pair of each lane's Gaussian; [32]: total
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i0 = (blockIdx.x * kEmitWarps + warp) * 32;
+  if (i0 >= P) return;  // whole warp
+  const int i = i0 + lane;
+  uint32_t n = 0;
+  if (i < P) {
+    const uint32_t id = g.order[i];
+    n = g.rows[id];
+    if (n) {
+      const float2 m = g.mean2d[id];
+      s_fp[warp][lane] = make_footprint(m.x, m.y, g.conic_opacity[id], g.radii[id], grid_x,
+                                        grid_y);
+    }
+    s_id[warp][lane] = id;
+  }
+  uint32_t inc = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  s_first[warp][lane] = inc - n;
+  if (lane == 31) s_first[warp][32] = inc;
+  const uint32_t base = i0 == 0 ? 0u : g.offsets[i0 - 1];  // the warp's first pair
+  __syncwarp();
+  const uint32_t total = s_first[warp][32];
+  for (uint32_t j = lane; j < total; j += 32) {
+    // Owner: the last lane whose first pair is at or before j (a lane without
+    // pairs shares its successor's first pair, so the last one has pairs).
+    int lo = 0, hi = 31;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_first[warp][mid] <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    const Footprint& f = s_fp[warp][lo];
+    const int ty = f.y0 + int(j - s_first[warp][lo]);
+    int x_lo, x_hi;
+    row_span(f, ty, x_lo, x_hi);
+    if (x_hi < x_lo) x_hi = x_lo;
+    rows_out[base + j] = uint32_t(ty);
+    spans_out[base + j] = pack_pair(s_id[warp][lo], x_lo, x_hi);
   }
 }
 
@@ -1310,8 +1345,9 @@ int bin_instances(int P, const GeomState& g, int grid_x, int grid_y, uint32_t n,
       if (e != cudaSuccess) return status_of(e, "placement shared memory");
     }
   }
-  emit_rows_kernel<<<(P + 255) / 256, 256, 0, stream>>>(P, g, grid_x, grid_y, b.pair_rows,
-                                                        b.pair_spans);
+  constexpr int kEmitThreads = 32 * kEmitWarps;
+  emit_rows_kernel<<<(P + kEmitThreads - 1) / kEmitThreads, kEmitThreads, 0, stream>>>(
+      P, g, grid_x, grid_y, b.pair_rows, b.pair_spans);
   size_t sort_bytes = b.sort_bytes;
   cudaError_t e = cub::DeviceRadixSort::SortPairs(
       b.sort_tmp, sort_bytes, b.pair_rows, b.pair_rows_sorted, b.pair_spans,

@@ -449,7 +449,12 @@ class DataParallelTrainer:
         dev = self.adam.device
         self.bg = torch.tensor(bg, dtype=torch.float32, device=dev)
         z = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)
-        self.scratch_grads = dict(mean2d=z(n, 3), colors=z(n, 3), cov=z(n, 6), conic=z(n, 4))
+        # The pixel backward's per-Gaussian targets (accumulated, so zeroed every
+        # step) are carved from one buffer: one fill clears them all.
+        self._accumulated = z(10 * n)
+        acc = self._accumulated
+        self.scratch_grads = dict(mean2d=acc[:3 * n].view(n, 3), colors=acc[3 * n:6 * n].view(n, 3),
+                                  conic=acc[6 * n:].view(n, 4), cov=z(n, 6))
         self.radii = torch.zeros(n, dtype=torch.int32, device=dev)
         self.loss = z(1)
         self.buffers = _Scratch(dev)
@@ -479,8 +484,7 @@ class DataParallelTrainer:
         # (the SH, scale, rotation and covariance adjoints and the seeds are
         # written outright).
         a.zero_accumulated()
-        for name in ("mean2d", "colors", "conic"):
-            self.scratch_grads[name].zero_()
+        self._accumulated.zero_()
         self.loss.zero_()
         act = a.activate()
         p = a.params
