@@ -25,6 +25,7 @@ import argparse
 import json
 import math
 import os
+import random
 import statistics
 import subprocess
 import sys
@@ -590,8 +591,10 @@ def measure_train_step(args, steps, warmup, with_e2e):
                                   sh_exchange=args.sh_exchange)
     del values
     # The 8 orbit cameras and a fixed random target per camera. Like a trainer
-    # walking its cameras, step k on rank r renders camera (r + k N) mod 8, so
-    # every GPU count sees the same mix of views (the diagonal views cost more).
+    # drawing its views from a shuffled stack, step k uses a seeded permutation
+    # of the 8 cameras (the same on every rank) and rank r renders its r-th
+    # camera: every step's views are distinct and every GPU count sees the same
+    # random mix of axis and diagonal views (the diagonal views cost more).
     cams = [orbit_camera(v, 8, width=TRAIN_W, height=TRAIN_H, device=device) for v in range(8)]
     targets = []
     for v in range(8):
@@ -600,7 +603,8 @@ def measure_train_step(args, steps, warmup, with_e2e):
     counter = [0]
 
     def view():
-        v = (rank + args.view_offset + counter[0] * world) % 8
+        order = random.Random(1000 + counter[0]).sample(range(8), 8)
+        v = (order[rank % 8] + args.view_offset) % 8
         counter[0] += 1
         return v
 
@@ -753,8 +757,9 @@ def measure_train_step(args, steps, warmup, with_e2e):
         "data": "synthetic (seeded; 6M Gaussians of the 8-view configuration, random targets)",
         "config": {"workload": f"{n:,} Gaussians SH degree 3 replicated, one {TRAIN_W}x{TRAIN_H} "
                                "view per GPU per step from 8 cameras on a radius-4 orbit (fov "
-                               "60; step k, rank r: camera (r + kN) mod 8), L1 loss, rasterizer "
-                               "backward, exchange + sharded torch-fused Adam",
+                               "60; step k: a seeded permutation of the cameras, rank r takes "
+                               "its r-th), L1 loss, rasterizer backward, exchange + sharded "
+                               "torch-fused Adam",
                    "exchange": adam.exchange, "sh_exchange": adam.sh_exchange,
                    "padded_gaussians": padded,
                    "share_per_gpu": share, "tile_instances_rank0": instances,
