@@ -10,8 +10,8 @@
   tolerances: rtol 3e-5 / atol 2e-7, Adam step-1 sign flips of rounding-level
   gradients allowed);
 * the seed form of the exchange (colour seeds per view, the SH backward
-  inside the update) bit-identical to the gradient form for 2 and 3 ranks'
-  views emulated on one GPU (the gradients formed from the same seeds by the
+  inside the update) bit-identical to the gradient form for 2, 3, 4 and 8
+  ranks' views emulated on one GPU (the gradients formed from the same seeds by the
   rasterizer's SH backward: two backward passes differ in the order of their
   float atomics, so only shared inputs compare bit for bit); the trainer step
   in both forms against the autograd path;
@@ -246,7 +246,7 @@ def test_trainer_step_on_one_gpu_matches_autograd_path(cuda, sh_exchange):
     trainer.close()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_seed_form_matches_gradient_form_for_emulated_ranks(cuda, world):
     """`world` views rendered on one GPU stand for the ranks. From each view's
     seeds and geometry gradients, the rasterizer's own SH backward
@@ -257,7 +257,7 @@ def test_seed_form_matches_gradient_form_for_emulated_ranks(cuda, world):
     from data_parallel import (DataParallelTrainer, ShardStep, carve, native_update,
                                orbit_camera, plan)
 
-    n, W, H = 2400, 96, 64  # padded alike for 1, 2 and 3 ranks
+    n, W, H = 2400, 96, 64  # padded alike for 1, 2, 3, 4 and 8 ranks
     padded, share = plan(n, world)
     assert padded == plan(n, 1)[0]
     values = _small_scene(n, cuda)
@@ -265,7 +265,7 @@ def test_seed_form_matches_gradient_form_for_emulated_ranks(cuda, world):
     a = trainer.adam
     grads_s, seeds, cams = [], [], []
     for q in range(world):
-        cam = orbit_camera(2 * q + 1, 8, width=W, height=H, device=cuda)
+        cam = orbit_camera((2 * q + 1) % 8, 8, width=W, height=H, device=cuda)
         target = torch.rand(3, H, W, device=cuda,
                             generator=torch.Generator(device=cuda).manual_seed(10 + q))
         trainer.backward(cam, target)
