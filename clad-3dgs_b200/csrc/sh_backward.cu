@@ -116,14 +116,63 @@ struct SeedParams {
   double inv_bias2;
 };
 
-// With one view the gradient row overwrites the coefficient row in place
-// (each term's coefficients are read before its gradients are written) and
-// the Adam pass reloads the parameters: half the shared memory, twice the
-// resident warps.
+// Several views, term-outer: for each term J every view's contribution to
+// d colour / d c_J is formed (views in rank order) and their sum overwrites c_J
+// once all views have read it; each view's direction adjoint accumulates in
+// dd[q] over the terms in order. The sums and the adjoints are those of the
+// view-outer form (one view's SH backward after another), bit for bit.
+__device__ __forceinline__ Direction direction_from(float4 u) {
+  Direction d;
+  d.x = u.x;
+  d.y = u.y;
+  d.z = u.z;
+  d.r = u.w;
+  d.xx = d.x * d.x;
+  d.yy = d.y * d.y;
+  d.zz = d.z * d.z;
+  d.xy = d.x * d.y;
+  d.yz = d.y * d.z;
+  d.xz = d.x * d.z;
+  return d;
+}
+
+template <int J, int R>
+__device__ __forceinline__ void views_adjoint_terms(const float4 (&dir)[R],
+                                                    const float4 (&seed)[R], float* row,
+                                                    int nterms, float (&dd)[R][3]) {
+  if constexpr (J < 16) {
+    float acc[3];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      float prod[3] = {0.f, 0.f, 0.f};
+      if (seed[q].w != 0.f && J < nterms) {
+        float b, gx, gy, gz;
+        sh_basis<J>(direction_from(dir[q]), b, gx, gy, gz);
+        const float* c = row + 3 * J;
+        const float dot = c[0] * seed[q].x + c[1] * seed[q].y + c[2] * seed[q].z;
+        dd[q][0] += gx * dot;
+        dd[q][1] += gy * dot;
+        dd[q][2] += gz * dot;
+        prod[0] = b * seed[q].x;
+        prod[1] = b * seed[q].y;
+        prod[2] = b * seed[q].z;
+      }
+#pragma unroll
+      for (int k = 0; k < 3; ++k) acc[k] = q == 0 ? prod[k] : acc[k] + prod[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) row[3 * J + k] = acc[k];
+    views_adjoint_terms<J + 1, R>(dir, seed, row, nterms, dd);
+  }
+}
+
+// The gradient row overwrites the coefficient row in place (each term's
+// coefficients are read, by every view, before its gradients are written) and
+// the Adam pass reloads the parameters: one row of shared memory per Gaussian.
 template <int R>
 __global__ void __launch_bounds__(32 * kSeedWarps)
     shard_seed_kernel(const __grid_constant__ SeedParams a) {
-  constexpr bool kInPlace = R == 1;
+  constexpr bool kInPlace = true;
   __shared__ float rows[kSeedWarps][(kInPlace ? 1 : 2) * 32 * kSeedRow];
   __shared__ float cams[R][3];
   using raster::CoefficientSum;
@@ -169,6 +218,34 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
       for (int k = 0; k < 3; ++k) geo[q][k] = a.geo_xyz[q][3 * i + k];
     }
     float x[3];
+    if constexpr (R > 1) {
+      float4 dir[R];
+      float dd[R][3];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        dir[q] = make_float4(0.f, 0.f, 0.f, 1.f);
+        if (seed[q].w != 0.f) {
+          const Direction d = make_direction(pos[0], pos[1], pos[2], cams[q][0], cams[q][1],
+                                             cams[q][2]);
+          dir[q] = make_float4(d.x, d.y, d.z, d.r);
+        }
+        dd[q][0] = dd[q][1] = dd[q][2] = 0.f;
+      }
+      views_adjoint_terms<0, R>(dir, seed, sum, a.nterms, dd);
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        float xq[3] = {geo[q][0], geo[q][1], geo[q][2]};
+        if (seed[q].w != 0.f) {
+          float om[3];
+          direction_vjp(direction_from(dir[q]), dd[q][0], dd[q][1], dd[q][2], om[0], om[1],
+                        om[2]);
+#pragma unroll
+          for (int k = 0; k < 3; ++k) xq[k] = geo[q][k] + om[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) x[k] = q == 0 ? xq[k] : x[k] + xq[k];
+      }
+    } else {
 #pragma unroll
     for (int q = 0; q < R; ++q) {
       float xq[3];
@@ -192,6 +269,7 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
       }
 #pragma unroll
       for (int k = 0; k < 3; ++k) x[k] = q == 0 ? xq[k] : x[k] + xq[k];
+    }
     }
     const int64_t mx = 3 * (i - a.begin);
 #pragma unroll
