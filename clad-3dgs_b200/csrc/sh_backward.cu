@@ -18,10 +18,11 @@
 // storing the parameters into every replica. The other groups (scaling,
 // rotation, opacity) go through the chunked update of train_step.cu.
 //
-// One warp per 32 Gaussians: the warp stages its coefficient block and its
-// gradient sums in shared memory (rows of 48 floats + 1, so each lane's row
-// starts in its own bank), each lane works through its Gaussian's views, and
-// the Adam pass over the block is coalesced.
+// One warp per 32 Gaussians: the warp stages its coefficient block in shared
+// memory (rows of 48 floats + 1, so each lane's row starts in its own bank),
+// each lane works through its Gaussian's views and leaves the gradient sums in
+// its row in place of the coefficients, and the Adam pass over the block is
+// coalesced.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -96,7 +97,7 @@ cudaError_t launch_sh_backward(int P, int degree, const float* means, ShSource s
 
 namespace train {
 
-constexpr int kSeedWarps = 2;  // shared memory per warp: 12.5 KB (6.3 KB with one view)
+constexpr int kSeedWarps = 2;  // 6.3 KB of shared memory per warp
 constexpr int kSeedRow = raster::kShRow;
 constexpr int kSeedRanks = CLAD3DGS_MAX_RANKS;
 
