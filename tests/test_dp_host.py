@@ -117,3 +117,44 @@ def test_collective_exchange_on_two_gloo_ranks(tmp_path):
         # Parameters moved, padding rows did not.
         assert not np.array_equal(got["p_xyz"][:n], initial_values(n)["xyz"].numpy())
         assert (got["p_xyz"][n:] == 0).all()
+
+
+def test_sh_exchange_form_choice_on_cpu():
+    """The seed form needs CUDA (its SH backward runs in the update kernel):
+    on the CPU the gradient form is the default and the seed form is refused;
+    an unknown form is refused everywhere."""
+    from data_parallel import ShardedAdam
+
+    adam = ShardedAdam(37, RATES, device="cpu", update=oracle_update)
+    assert adam.sh_exchange == "grads" and adam.seeds is None and adam.camera is None
+    with pytest.raises(ValueError):
+        ShardedAdam(37, RATES, device="cpu", update=oracle_update, sh_exchange="seeds")
+    with pytest.raises(ValueError):
+        ShardedAdam(37, RATES, device="cpu", update=oracle_update, sh_exchange="colours")
+
+
+def _collective_seeds_worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    from data_parallel import ShardedAdam
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        refused = False
+        try:
+            ShardedAdam(37, RATES, device="cpu", exchange="collective", sh_exchange="seeds")
+        except ValueError:
+            refused = True
+        with open(os.path.join(out_dir, f"refused{rank}"), "w") as f:
+            f.write(str(refused))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_collective_exchange_refuses_the_seed_form(tmp_path):
+    """A collective reduce-scatter sums gradients, so with more than one rank
+    the collective exchange cannot take colour seeds."""
+    mp.spawn(_collective_seeds_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2)
+    for rank in range(2):
+        assert (tmp_path / f"refused{rank}").read_text() == "True"
