@@ -1,126 +1,148 @@
-"""Dense-Adam SH consumer bound to the trainer's optimizer for one step
-(drop-in for the reference's adapter.py:1-389).
+"""SH coefficients updated inside the rasterizer backward (the trainer-facing
+`adapter` module; same public names, arguments and fallback reasons as the
+reference's adapter.py:1-389).
 
-On an eligible step `DenseSHConsumer.render` binds features_dc /
-features_rest, their Adam moments and step counters (`bind`), renders through
-the rasterizer extension, and in backward calls the extension's
-`rasterize_gaussians_backward_consume[_direct]`, which runs the pixel and
-geometry backward and then the fused SH VJP + torch-fused Adam kernel
-(sh_consumer_split_torch_adam): the SH coefficients and moments are updated
-in place, no SH gradient tensor exists, and the position adjoint of the view
-direction is added to dL/dmeans. The frame then advances both step counters
-and the autograd versions once and leaves `.grad` unset so the trainer's
-optimizer.step() skips the two SH groups. Ineligible steps return the native
-rasterizer's output and record the reason in `last_reason`; any change of
-ownership between forward and backward raises before a write.
+`DenseSHConsumer.render(...)` is the trainer's render call. On a step the
+policy allows, it claims the optimizer's f_dc / f_rest groups (their Adam
+moments and counters) and renders through `LifecycleRender`, whose backward
+calls the extension's `rasterize_gaussians_backward_consume[_direct]`: the
+pixel and geometry backward run, then one fused kernel applies the SH
+adjoint straight to torch-fused Adam on the coefficients and adds the view
+direction's adjoint to dL/dmeans. No SH gradient tensor exists; the groups'
+`.grad` stays None, so the trainer's `optimizer.step()` skips them, and the
+counters and autograd versions advance once. Any other step renders through
+the native rasterizer and records why in `last_reason`. A claim is checked
+again right before the kernel: any change of ownership raises before a write.
+Nothing is cached across steps, so checkpoint restore, densification and
+pruning need no hook.
 
-The cached state is nothing: every step binds the optimizer's current
-objects, so checkpoint restore, densification and pruning need no hook.
-
-`consume_position=True` (not in the reference, whose trainer leaves xyz to
-torch's Adam) also binds the optimizer's "xyz" group: once the direction
-adjoint is added dL/dmeans is the positions' complete gradient, so the same
-kernel runs their Adam, the backward returns no position gradient, and the
-frame advances the xyz counter with the SH ones. Only valid when the means feed
-nothing but this renderer; an ineligible xyz group leaves the positions to the
-optimizer (`position_reason` says why) and the SH groups are still consumed.
+`consume_position=True` (an addition; the reference leaves xyz to torch's
+Adam) also claims the "xyz" group: once the direction adjoint is added,
+dL/dmeans is complete, so the same kernel applies the positions' Adam and the
+backward returns no position gradient. An xyz group that cannot be claimed
+leaves the positions to the optimizer (`position_reason` says why) without
+affecting the SH groups.
 """
 
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass
+from dataclasses import dataclass, fields
 from types import SimpleNamespace
 
 import torch
 
-SH_OPTIONS = ("lr", "betas", "eps", "fused", "foreach", "weight_decay",
-              "amsgrad", "maximize", "capturable", "differentiable")
-STATE_KEYS = ("exp_avg", "exp_avg_sq", "step")
+from optimizer_claims import (ADAM_OPTIONS, STATE_KEYS, Claim, bias_corrections,
+                              dense_fp32_cuda, finite_rate, last_failure, overlapping,
+                              owns_only, plain_fused_adam, read_counters, reference_betas,
+                              settle, sole_group, state_or_fresh, state_problem, valid_counter)
+
+SH_OPTIONS = ADAM_OPTIONS
+
+# Positional layouts of the renderer extension's calls (the reference's
+# adapter.py:21-47, 67-92): names of the values in call order. In the direct
+# variants the packed "sh" slot is replaced by the two tensors dc, rest.
+FORWARD_ARGS = ("bg", "means", "colors", "opacity", "scales", "rotations", "scale_modifier",
+                "cov3d", "viewmatrix", "projmatrix", "tanfovx", "tanfovy", "image_height",
+                "image_width", "sh", "sh_degree", "campos", "prefiltered", "antialiasing",
+                "debug")
+BACKWARD_ARGS = ("bg", "means", "radii", "colors", "opacity", "scales", "rotations",
+                 "scale_modifier", "cov3d", "viewmatrix", "projmatrix", "tanfovx", "tanfovy",
+                 "dout_color", "dout_invdepth", "sh", "sh_degree", "campos", "geom",
+                 "num_rendered", "binning", "image", "antialiasing", "debug")
+_SETTINGS = ("bg", "scale_modifier", "viewmatrix", "projmatrix", "tanfovx", "tanfovy",
+             "image_height", "image_width", "sh_degree", "campos", "prefiltered",
+             "antialiasing", "debug")
 
 
-def _forward_arguments(settings, means, opacity, scale, rotation, sh, empty):
-    return (settings.bg, means, empty, opacity, scale, rotation,
-            settings.scale_modifier, empty, settings.viewmatrix, settings.projmatrix,
-            settings.tanfovx, settings.tanfovy, settings.image_height,
-            settings.image_width, sh, settings.sh_degree, settings.campos,
-            settings.prefiltered, settings.antialiasing, settings.debug)
+def _call_args(layout, values, split_sh):
+    """Values in the extension's positional order; `split_sh` puts (dc, rest)
+    where the packed coefficients would go."""
+    out = []
+    for name in layout:
+        if name == "sh" and split_sh:
+            out += [values["dc"], values["rest"]]
+        else:
+            out.append(values[name])
+    return tuple(out)
+
+
+def _settings_values(settings):
+    return {name: getattr(settings, name) for name in _SETTINGS}
 
 
 class ConsumerRender(torch.autograd.Function):
-    """Rasterizer call whose backward consumes the SH gradient (adapter.py:13-119)."""
+    """Renderer call whose backward hands the SH adjoint to the fused Adam
+    kernel instead of returning it (the reference's adapter.py:13-119)."""
 
     @staticmethod
     def forward(ctx, means, screen, dc, rest, opacity, scale, rotation, settings, owner):
         empty = torch.empty(0, device=means.device)
-        direct = getattr(owner, "direct_inputs", False)
-        sh = empty if direct else torch.cat((dc, rest), 1)
-        args = _forward_arguments(settings, means, opacity, scale, rotation, sh, empty)
-        if direct:
-            args = args[:14] + (dc, rest) + args[15:]
-            count, color, radii, geom, binning, image, depth = \
-                owner.extension.rasterize_gaussians_direct(*args)
-        else:
-            count, color, radii, geom, binning, image, depth = \
-                owner.extension.rasterize_gaussians(*args)
+        split = bool(getattr(owner, "direct_inputs", False))
+        packed = empty if split else torch.cat((dc, rest), 1)
+        values = dict(_settings_values(settings), means=means, colors=empty, opacity=opacity,
+                      scales=scale, rotations=rotation, cov3d=empty, sh=packed, dc=dc,
+                      rest=rest)
+        render = (owner.extension.rasterize_gaussians_direct if split
+                  else owner.extension.rasterize_gaussians)
+        count, color, radii, geom, binning, image, depth = render(
+            *_call_args(FORWARD_ARGS, values, split))
         ctx.settings, ctx.owner, ctx.count = settings, owner, count
-        ctx.save_for_backward(means, opacity, scale, rotation, radii, sh, geom,
-                              binning, image, dc, rest)
+        ctx.save_for_backward(means, opacity, scale, rotation, radii, packed, geom, binning,
+                              image, dc, rest)
         return color, radii, depth
 
     @staticmethod
     def backward(ctx, seed, _radii_seed, depth_seed):
         owner = ctx.owner
-        native_only = getattr(owner, "native_only", False)
-        if native_only and torch.is_grad_enabled():
+        unconsumed = bool(getattr(owner, "native_only", False))
+        if unconsumed and torch.is_grad_enabled():
             raise RuntimeError("Direct SH inputs support first-order backward only")
-        (means, opacity, scale, rotation, radii, sh, geom, binning, image, dc,
+        (means, opacity, scale, rotation, radii, packed, geom, binning, image, dc,
          rest) = ctx.saved_tensors
-        s = ctx.settings
         empty = torch.empty(0, device=means.device)
-        args = (s.bg, means, radii, empty, opacity, scale, rotation, s.scale_modifier,
-                empty, s.viewmatrix, s.projmatrix, s.tanfovx, s.tanfovy,
-                seed.contiguous(), depth_seed.contiguous(), sh, s.sh_degree, s.campos,
-                geom, ctx.count, binning, image, s.antialiasing, s.debug)
-        if native_only:
-            grads = owner.extension.rasterize_gaussians_backward_direct(
-                *(args[:15] + (dc, rest) + args[16:]))
-            g_screen, _, g_opacity, g_means, _, g_sh, g_scale, g_rot = grads
-            return (g_means, g_screen, g_sh[:, :1], g_sh[:, 1:], g_opacity, g_scale,
-                    g_rot, None, None)
-        m_dc, v_dc = owner.moments["dc"]
-        m_rest, v_rest = owner.moments["rest"]
-        step = owner.iteration
-        bias1, bias2 = 1 - 0.9 ** step, math.sqrt(1 - 0.999 ** step)
-        consume = (owner.extension.rasterize_gaussians_backward_consume_direct
-                   if getattr(owner, "direct_inputs", False)
+        values = dict(_settings_values(ctx.settings), means=means, radii=radii, colors=empty,
+                      opacity=opacity, scales=scale, rotations=rotation, cov3d=empty,
+                      dout_color=seed.contiguous(), dout_invdepth=depth_seed.contiguous(),
+                      sh=packed, dc=dc, rest=rest, geom=geom, num_rendered=ctx.count,
+                      binning=binning, image=image)
+        if unconsumed:
+            out = owner.extension.rasterize_gaussians_backward_direct(
+                *_call_args(BACKWARD_ARGS, values, True))
+            d_screen, _, d_opacity, d_means, _, d_sh, d_scale, d_rot = out
+            return (d_means, d_screen, d_sh[:, :1], d_sh[:, 1:], d_opacity, d_scale, d_rot,
+                    None, None)
+        split = bool(getattr(owner, "direct_inputs", False))
+        consume = (owner.extension.rasterize_gaussians_backward_consume_direct if split
                    else owner.extension.rasterize_gaussians_backward_consume)
-        extra = {}
-        position = "xyz" in owner.params
-        if position:
+        bias1, bias2 = bias_corrections(owner.iteration)
+        (m_dc, v_dc), (m_rest, v_rest) = owner.moments["dc"], owner.moments["rest"]
+        position = {}
+        if "xyz" in owner.params:
             m_xyz, v_xyz = owner.moments["xyz"]
-            extra["xyz"] = dict(first=m_xyz, second=v_xyz, rate=owner.position_rate,
-                                bias1=bias1, bias2_sqrt=bias2)
-        grads = consume(*args, owner.params["dc"], owner.params["rest"], m_dc, v_dc,
-                        m_rest, v_rest, bias1, bias2, **extra)
-        g_screen, _, g_opacity, g_means, _, _, g_scale, g_rot = grads
+            position["xyz"] = dict(first=m_xyz, second=v_xyz, rate=owner.position_rate,
+                                   bias1=bias1, bias2_sqrt=bias2)
+        out = consume(*_call_args(BACKWARD_ARGS, values, split), owner.params["dc"],
+                      owner.params["rest"], m_dc, v_dc, m_rest, v_rest, bias1, bias2,
+                      **position)
+        d_screen, _, d_opacity, d_means, _, _, d_scale, d_rot = out
         if position:
-            g_means = None  # applied by the kernel
-        return g_means, g_screen, None, None, g_opacity, g_scale, g_rot, None, None
+            d_means = None  # the kernel already applied the positions' Adam
+        return d_means, d_screen, None, None, d_opacity, d_scale, d_rot, None, None
 
 
 def render_direct_native(extension, means, screen, dc, rest, opacity, scale, rotation,
                          settings):
-    """Direct dc/rest reads with the ordinary SH backward (gradients for the
-    trainer's own optimizer)."""
+    """Render from dc/rest directly and return ordinary SH gradients for the
+    trainer's own optimizer."""
     owner = SimpleNamespace(extension=extension, direct_inputs=True, native_only=True)
-    return ConsumerRender.apply(means, screen, dc, rest, opacity, scale, rotation,
-                                settings, owner)
+    return ConsumerRender.apply(means, screen, dc, rest, opacity, scale, rotation, settings,
+                                owner)
 
 
 @dataclass(frozen=True)
 class StepPolicy:
-    """What the trainer does between backward and Adam on this step."""
+    """What the trainer does between this step's backward and its Adam step.
+    Any field away from its default makes the step ineligible."""
 
     optimizer_step: bool = True
     topology_change: bool = False
@@ -129,82 +151,113 @@ class StepPolicy:
     unscaled_gradients: bool = True
     exclusive_sh_use: bool = True
 
+    _REASONS = {
+        "optimizer_step": "optimizer step skipped",
+        "topology_change": "topology changes before optimizer step",
+        "observation_before_step": "parameters observed before optimizer step",
+        "single_backward": "gradient accumulation or multiple backward calls",
+        "unscaled_gradients": "scaled gradients require native optimizer processing",
+        "exclusive_sh_use": "SH parameters used by another loss or consumer",
+    }
+
     def reason(self):
-        if not self.optimizer_step:
-            return "optimizer step skipped"
-        if self.topology_change:
-            return "topology changes before optimizer step"
-        if self.observation_before_step:
-            return "parameters observed before optimizer step"
-        if not self.single_backward:
-            return "gradient accumulation or multiple backward calls"
-        if not self.unscaled_gradients:
-            return "scaled gradients require native optimizer processing"
-        if not self.exclusive_sh_use:
-            return "SH parameters used by another loss or consumer"
+        for f in fields(self):
+            if bool(getattr(self, f.name)) != f.default:
+                return self._REASONS[f.name]
         return None
 
 
 class BoundStep:
-    """The SH parameters, groups and Adam state of one consumed step."""
+    """The claims of one consumed step; `validate` right before the kernel,
+    `finish` after it."""
 
-    def __init__(self, optimizer, groups, states, extension, iteration):
+    def __init__(self, optimizer, claims, extension, iteration):
         self.optimizer = optimizer
-        self.groups = groups
-        self.states = states
+        self.claims = dict(claims)          # "dc", "rest"[, "xyz"] -> Claim
         self.extension = extension
-        keys = ("dc", "rest", "xyz")[:len(groups)]
-        self.params = {k: g["params"][0] for k, g in zip(keys, groups)}
-        self.moments = {k: (st["exp_avg"], st["exp_avg_sq"]) for k, st in zip(keys, states)}
-        self.position_rate = float(groups[2]["lr"]) if len(groups) > 2 else None
         self.iteration = iteration
         self.consumed = False
-        self.versions = [p._version for p in self.params.values()]
-        self.options = [tuple(g.get(k) for k in SH_OPTIONS) for g in groups]
-        self.values = [{k: st[k] for k in STATE_KEYS} for st in states]
-        self.state_versions = [{k: v._version for k, v in row.items()} for row in self.values]
+        self.direct_inputs = False
+        xyz = self.claims.get("xyz")
+        self.position_rate = float(xyz.group["lr"]) if xyz is not None else None
+
+    @property
+    def groups(self):
+        return [c.group for c in self.claims.values()]
+
+    @property
+    def states(self):
+        return [c.state for c in self.claims.values()]
+
+    @property
+    def params(self):
+        return {k: c.param for k, c in self.claims.items()}
+
+    @property
+    def moments(self):
+        return {k: c.moments for k, c in self.claims.items()}
 
     def validate(self):
         if self.consumed:
             raise RuntimeError("SH consumption permits one backward per optimizer step")
-        for group, p, version, state, values, state_versions, options in zip(
-                self.groups, self.params.values(), self.versions, self.states,
-                self.values, self.state_versions, self.options):
-            if (len(group["params"]) != 1 or group["params"][0] is not p
-                    or p._version != version or p.grad is not None or not p.requires_grad
-                    or not any(g is group for g in self.optimizer.param_groups)
-                    or self.optimizer.state.get(p) is not state
-                    or any(state.get(k) is not v for k, v in values.items())
-                    or any(values[k]._version != v for k, v in state_versions.items())
-                    or tuple(group.get(k) for k in SH_OPTIONS) != options):
-                raise RuntimeError("SH ownership changed between forward and backward")
+        if not all(c.intact(self.optimizer) for c in self.claims.values()):
+            raise RuntimeError("SH ownership changed between forward and backward")
 
-    @torch.no_grad()
     def finish(self):
-        for state in self.states:
-            state["step"].add_(1)
-        torch.autograd.graph.increment_version(
-            [*self.params.values(), *[v for pair in self.moments.values() for v in pair]])
+        settle(self.claims.values())
         self.consumed = True
 
 
 class LifecycleRender(ConsumerRender):
+    """ConsumerRender whose backward re-checks the claims before the kernel
+    and settles them after it."""
+
     @staticmethod
     def backward(ctx, seed, radii_seed, depth_seed):
         if torch.is_grad_enabled():
             raise RuntimeError("SH consumption supports first-order backward only")
         ctx.owner.validate()
-        result = ConsumerRender.backward(ctx, seed, radii_seed, depth_seed)
+        grads = ConsumerRender.backward(ctx, seed, radii_seed, depth_seed)
         ctx.owner.finish()
-        return result
+        return grads
+
+
+# Per-group screening of an SH or position group: (reason, predicate(group,
+# param, shape, what)), general to specific; the last failing row names the
+# fallback, which is how the reference's sequence of checks reports.
+def _group_rules(what, rate_ok):
+    return (
+        (f"{what} parameter ownership mismatch", lambda g, p, s: not owns_only(g, p)),
+        (f"unsupported {what} tensor layout", lambda g, p, s: not dense_fp32_cuda(p, s)),
+        (f"frozen or accumulated {what} gradients",
+         lambda g, p, s: not p.requires_grad or p.grad is not None),
+        (f"unsupported {what} Adam hyperparameters",
+         lambda g, p, s: not (rate_ok(g["lr"]) and reference_betas(g))),
+        (f"{what} consumption requires fused Adam without foreach",
+         lambda g, p, s: g.get("fused") is not True or bool(g.get("foreach"))),
+        ("unsupported Adam option",
+         lambda g, p, s: g.get("weight_decay", 0) != 0
+         or any(g.get(k, False) for k in ("amsgrad", "maximize", "differentiable",
+                                           "capturable"))),
+    )
+
+
+def _rate_is(value):
+    return lambda lr: isinstance(lr, (float, int)) and lr == value
+
+
+# (optimizer group name, claim key, coefficient rows, learning rate the
+# kernel's arithmetic is checked against)
+_SH_GROUPS = (("f_dc", "dc", 1, 0.0025), ("f_rest", "rest", 15, 0.000125))
+_SH_RULES = {key: _group_rules("SH", _rate_is(rate)) for _, key, _, rate in _SH_GROUPS}
+_POSITION_RULES = _group_rules("position", lambda lr: True)
 
 
 class DenseSHConsumer:
     def __init__(self, optimizer, *, native, extension, direct_inputs=False,
                  consume_position=False):
-        if direct_inputs and not all(
-                hasattr(extension, name) for name in
-                ("rasterize_gaussians_direct", "rasterize_gaussians_backward_consume_direct")):
+        needed = ("rasterize_gaussians_direct", "rasterize_gaussians_backward_consume_direct")
+        if direct_inputs and not all(hasattr(extension, n) for n in needed):
             raise ValueError("Build the extension with direct-input support first")
         self.native = native
         self.extension = extension
@@ -215,165 +268,105 @@ class DenseSHConsumer:
         self.last_reason = None
         self.position_reason = None
 
-    def _fallback(self, reason):
-        self.last_reason = reason
-        return None
+    # -- screening -------------------------------------------------------
 
-    @staticmethod
-    def _group_reason(group, param, shape, what):
-        """Why `group` cannot be consumed (None if it can); the rate is checked
-        by the caller."""
-        if len(group["params"]) != 1 or group["params"][0] is not param:
-            return f"{what} parameter ownership mismatch"
-        if (tuple(param.shape) != shape or not param.is_contiguous()
-                or param.dtype != torch.float32 or not param.is_cuda):
-            return f"unsupported {what} tensor layout"
-        if not param.requires_grad or param.grad is not None:
-            return f"frozen or accumulated {what} gradients"
-        if group["betas"] != (0.9, 0.999) or group["eps"] != 1e-15:
-            return f"unsupported {what} Adam hyperparameters"
-        if group.get("fused") is not True or group.get("foreach"):
-            return f"{what} consumption requires fused Adam without foreach"
-        if (any(group.get(k, False) for k in
-                ("amsgrad", "maximize", "differentiable", "capturable"))
-                or group.get("weight_decay", 0) != 0):
-            return "unsupported Adam option"
-        return None
+    def _step_reason(self, policy):
+        if torch.cuda.current_stream() != torch.cuda.default_stream():
+            raise RuntimeError("the pinned rasterizer requires the default CUDA stream")
+        if type(self.optimizer) is not torch.optim.Adam:
+            return "unsupported optimizer"
+        if not torch.is_grad_enabled():
+            return "evaluation without gradients"
+        return policy.reason()
 
-    @staticmethod
-    def _state_for(optimizer, group):
-        param = group["params"][0]
-        state = optimizer.state.get(param)
-        if not state:
-            state = {"step": torch.tensor(0.0, device=param.device if group.get("fused")
-                                          else "cpu"),
-                     "exp_avg": torch.zeros_like(param),
-                     "exp_avg_sq": torch.zeros_like(param)}
-        for key in ("exp_avg", "exp_avg_sq"):
-            value = state.get(key)
-            if (not torch.is_tensor(value) or value.shape != param.shape
-                    or value.dtype != param.dtype or value.device != param.device
-                    or not value.is_contiguous()):
-                return None, "moment layout"
-        step = state.get("step")
-        if (not torch.is_tensor(step) or step.device != param.device
-                or step.dtype != torch.float32 or step.numel() != 1):
-            return None, "step counter"
-        return state, None
+    def _screen_sh(self, dc, rest):
+        """(groups by claim key, reason)."""
+        if dc.ndim != 3 or rest.ndim != 3:
+            return None, "unsupported SH tensor layout"
+        found, reason, tensors = {}, None, {"dc": dc, "rest": rest}
+        for name, key, rows, _ in _SH_GROUPS:
+            group = sole_group(self.optimizer, name)
+            if group is None:
+                reason = "missing or duplicate SH optimizer group"
+                break
+            found[key] = group
+            reason = last_failure(_SH_RULES[key], group, tensors[key],
+                                  (dc.shape[0], rows, 3)) or reason
+        if dc.device != rest.device:
+            reason = "SH device mismatch"
+        return found, reason
 
-    def _position_group(self, means, count, device):
-        """The xyz group and its state, or (None, reason)."""
+    def _screen_position(self, means, count, device, sh_claims, sh_counter):
+        """(group, state) of a claimable xyz group, or (None, None, reason)."""
         if means is None:
             return None, None, "positions not given"
-        matches = [g for g in self.optimizer.param_groups if g.get("name") == "xyz"]
-        if len(matches) != 1:
+        group = sole_group(self.optimizer, "xyz")
+        if group is None:
             return None, None, "missing or duplicate xyz optimizer group"
-        group = matches[0]
-        reason = self._group_reason(group, means, (count, 3), "position")
-        rate = group.get("lr")
-        if reason is None and (not isinstance(rate, (float, int)) or not math.isfinite(rate)):
+        reason = last_failure(_POSITION_RULES, group, means, (count, 3))
+        if reason is None and not finite_rate(group.get("lr")):
             reason = "unsupported position learning rate"
         if reason is None and means.device != device:
             reason = "position device mismatch"
         if reason is not None:
             return None, None, reason
-        state, bad = self._state_for(self.optimizer, group)
-        if state is None:
-            return None, None, f"unsupported position {bad}"
+        state = state_or_fresh(self.optimizer, means, means.device if group.get("fused")
+                               else "cpu")
+        problem = state_problem(state, means)
+        if problem is not None:
+            return None, None, ("unsupported position moment layout" if problem == "moments"
+                                else "unsupported position step counter")
+        if read_counters([state])[0] != sh_counter:
+            return None, None, "position and SH Adam step counters differ"
+        owned = [t for c in sh_claims for t in (c.param, *c.entries.values())]
+        if overlapping(owned + [means] + [state[k] for k in STATE_KEYS]):
+            return None, None, "positions overlap the SH parameters or moments"
         return group, state, None
+
+    def _decline(self, reason):
+        self.last_reason = reason
+        return None
+
+    # -- binding ---------------------------------------------------------
 
     def bind(self, dc, rest, policy, means=None):
         if self.active is not None:
             raise RuntimeError("finish the previous optimizer step first")
-        reason = policy.reason()
-        if not torch.is_grad_enabled():
-            reason = "evaluation without gradients"
-        if torch.cuda.current_stream() != torch.cuda.default_stream():
-            raise RuntimeError("the pinned rasterizer requires the default CUDA stream")
-        if type(self.optimizer) is not torch.optim.Adam:
-            reason = "unsupported optimizer"
+        reason = self._step_reason(policy)
         if reason is not None:
-            return self._fallback(reason)
-        if dc.ndim != 3 or rest.ndim != 3:
-            return self._fallback("unsupported SH tensor layout")
-        groups = []
-        for name, param, shape, rate in (("f_dc", dc, (dc.shape[0], 1, 3), 0.0025),
-                                         ("f_rest", rest, (dc.shape[0], 15, 3), 0.000125)):
-            matches = [g for g in self.optimizer.param_groups if g.get("name") == name]
-            if len(matches) != 1:
-                reason = "missing or duplicate SH optimizer group"
-                break
-            group = matches[0]
-            groups.append(group)
-            if len(group["params"]) != 1 or group["params"][0] is not param:
-                reason = "SH parameter ownership mismatch"
-            if (tuple(param.shape) != shape or not param.is_contiguous()
-                    or param.dtype != torch.float32 or not param.is_cuda):
-                reason = "unsupported SH tensor layout"
-            if not param.requires_grad or param.grad is not None:
-                reason = "frozen or accumulated SH gradients"
-            if (not isinstance(group["lr"], (float, int)) or group["lr"] != rate
-                    or group["betas"] != (0.9, 0.999) or group["eps"] != 1e-15):
-                reason = "unsupported SH Adam hyperparameters"
-            if group.get("fused") is not True or group.get("foreach"):
-                reason = "SH consumption requires fused Adam without foreach"
-            if (any(group.get(k, False) for k in
-                    ("amsgrad", "maximize", "differentiable", "capturable"))
-                    or group.get("weight_decay", 0) != 0):
-                reason = "unsupported Adam option"
-        if dc.device != rest.device:
-            reason = "SH device mismatch"
+            return self._decline(reason)
+        groups, reason = self._screen_sh(dc, rest)
         if reason is not None:
-            return self._fallback(reason)
-        states = []
-        for group in groups:
+            return self._decline(reason)
+        states = {}
+        for key, group in groups.items():
             param = group["params"][0]
-            state = self.optimizer.state.get(param)
-            if not state:
-                state = {"step": torch.tensor(0.0, device=param.device if group.get("fused")
-                                              else "cpu"),
-                         "exp_avg": torch.zeros_like(param),
-                         "exp_avg_sq": torch.zeros_like(param)}
-            for key in ("exp_avg", "exp_avg_sq"):
-                value = state.get(key)
-                if (not torch.is_tensor(value) or value.shape != param.shape
-                        or value.dtype != param.dtype or value.device != param.device
-                        or not value.is_contiguous()):
-                    return self._fallback("unsupported SH moment layout")
-            step = state.get("step")
-            if (not torch.is_tensor(step) or step.device != param.device
-                    or step.dtype != torch.float32 or step.numel() != 1):
-                return self._fallback("unsupported SH step counter")
-            states.append(state)
-        writable = [dc, rest] + [st[k] for st in states for k in STATE_KEYS]
-        spans = sorted((v.data_ptr(), v.data_ptr() + v.numel() * v.element_size())
-                       for v in writable if v.numel())
-        if any(a[1] > b[0] for a, b in zip(spans, spans[1:])):
-            return self._fallback("overlapping SH parameters, moments or counters")
-        counters = [st["step"].item() for st in states]
-        if any(not math.isfinite(c) or c < 0 or c != int(c) or c >= 2**24 for c in counters):
-            return self._fallback("invalid SH step counter")
-        if counters[0] != counters[1]:
-            return self._fallback("different SH Adam step counters")
+            state = state_or_fresh(self.optimizer, param,
+                                   param.device if group.get("fused") else "cpu")
+            problem = state_problem(state, param)
+            if problem is not None:
+                return self._decline("unsupported SH moment layout" if problem == "moments"
+                                     else "unsupported SH step counter")
+            states[key] = state
+        written = [dc, rest] + [s[k] for s in states.values() for k in STATE_KEYS]
+        if overlapping(written):
+            return self._decline("overlapping SH parameters, moments or counters")
+        counters = read_counters(list(states.values()))
+        if not all(valid_counter(c) for c in counters):
+            return self._decline("invalid SH step counter")
+        if len(set(counters)) != 1:
+            return self._decline("different SH Adam step counters")
+        claims = {k: Claim.take(groups[k], states[k]) for k in groups}
         self.position_reason = None
         if self.consume_position:
-            group, state, why = self._position_group(means, dc.shape[0], dc.device)
-            if why is None and state["step"].item() != counters[0]:
-                why = "position and SH Adam step counters differ"
-            if why is None:
-                extra = [means] + [state[k] for k in STATE_KEYS]
-                spans = sorted((v.data_ptr(), v.data_ptr() + v.numel() * v.element_size())
-                               for v in writable + extra if v.numel())
-                if any(a[1] > b[0] for a, b in zip(spans, spans[1:])):
-                    why = "positions overlap the SH parameters or moments"
-            if why is None:
-                groups.append(group)
-                states.append(state)
+            group, state, why = self._screen_position(means, dc.shape[0], dc.device,
+                                                      claims.values(), counters[0])
             self.position_reason = why
-        for group, state in zip(groups, states):
-            self.optimizer.state[group["params"][0]] = state
-        self.active = BoundStep(self.optimizer, groups, states, self.extension,
-                                int(counters[0]) + 1)
+            if why is None:
+                claims["xyz"] = Claim.take(group, state)
+        for claim in claims.values():
+            self.optimizer.state[claim.param] = claim.state
+        self.active = BoundStep(self.optimizer, claims, self.extension, int(counters[0]) + 1)
         self.active.direct_inputs = self.direct_inputs
         self.last_reason = None
         return self.active
@@ -395,15 +388,16 @@ class DenseSHConsumer:
 
 def official_step_policy(iteration, options, *, white_background=False,
                          testing_iterations=(), saving_iterations=()):
-    """The trainer's steps that change state between backward and Adam
-    (densification, opacity reset, save/test, final iteration) fall back."""
-    topology = False
-    if iteration < options.densify_until_iter:
-        topology = (iteration > options.densify_from_iter
-                    and iteration % options.densification_interval == 0)
-        topology = topology or iteration % options.opacity_reset_interval == 0
-        topology = topology or (white_background and iteration == options.densify_from_iter)
-    return StepPolicy(
-        optimizer_step=iteration < options.iterations,
-        topology_change=topology,
-        observation_before_step=iteration in testing_iterations or iteration in saving_iterations)
+    """The policy of the stock trainer's loop at `iteration`: densification,
+    opacity reset (and the white-background reset at densify_from_iter) change
+    the Gaussian set before Adam; test and save iterations read parameters
+    before it; the last iteration runs no Adam step."""
+    in_window = iteration < options.densify_until_iter
+    densify = iteration > options.densify_from_iter and \
+        iteration % options.densification_interval == 0
+    reset = iteration % options.opacity_reset_interval == 0 or \
+        (white_background and iteration == options.densify_from_iter)
+    observed = iteration in testing_iterations or iteration in saving_iterations
+    return StepPolicy(optimizer_step=iteration < options.iterations,
+                      topology_change=in_window and (densify or reset),
+                      observation_before_step=observed)

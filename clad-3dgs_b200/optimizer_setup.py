@@ -1,12 +1,14 @@
-"""Dense fused Adam for the trainer's Gaussian optimizer (drop-in for the
+"""torch's fused dense Adam for the trainer's Gaussian optimizer (the
+trainer-facing `optimizer_setup` module; same names and errors as the
 reference's optimizer_setup.py:1-40).
 
-The consumed SH and activation updates reproduce torch's fused Adam
-arithmetic, so the trainer's optimizer must be `torch.optim.Adam(fused=True,
-foreach=False)` for the groups that fall back to it to match. `fused_adam`
-rebuilds an existing Adam with those options and carries parameters,
-moments and step counters over unchanged (step tensors move to the parameter
-device, which fused Adam requires).
+The consumed SH and activation updates reproduce the arithmetic of
+`torch.optim.Adam(fused=True, foreach=False)`, so the groups that stay with
+the optimizer must use that implementation too for a consumed step and a
+native one to agree. `fused_adam` builds that optimizer over the same
+parameter groups and moves the existing per-parameter state across as it is:
+moment tensors are handed over (not copied), and step counters, which fused
+Adam keeps on the parameter's device, are moved there.
 """
 
 from __future__ import annotations
@@ -14,38 +16,49 @@ from __future__ import annotations
 import torch
 
 
-def fused_adam(optimizer):
+def _unfusable(optimizer):
+    """The error message when `optimizer` cannot become fused Adam, else None."""
     if type(optimizer) is not torch.optim.Adam:
-        raise ValueError("--fused-adam requires the default dense Adam optimizer")
+        return "--fused-adam requires the default dense Adam optimizer"
     for group in optimizer.param_groups:
-        for parameter in group["params"]:
-            if not parameter.is_cuda or parameter.dtype != torch.float32:
-                raise ValueError("--fused-adam requires CUDA float32 Gaussian parameters")
-            step = optimizer.state.get(parameter, {}).get("step")
-            if step is not None and (not torch.is_tensor(step) or step.dtype != torch.float32):
-                raise ValueError("--fused-adam requires native float32 Adam step counters")
-    defaults = dict(optimizer.defaults, fused=True, foreach=False)
-    groups = [dict(group, fused=True, foreach=False) for group in optimizer.param_groups]
-    replacement = torch.optim.Adam(groups, **defaults)
-    saved = optimizer.state_dict()
-    for group in saved["param_groups"]:
-        group.update(fused=True, foreach=False)
-    replacement.load_state_dict(saved)
+        for param in group["params"]:
+            if not (param.is_cuda and param.dtype == torch.float32):
+                return "--fused-adam requires CUDA float32 Gaussian parameters"
+            step = optimizer.state.get(param, {}).get("step")
+            if step is not None and not (torch.is_tensor(step) and step.dtype == torch.float32):
+                return "--fused-adam requires native float32 Adam step counters"
+    return None
+
+
+def _moved_state(state, param):
+    moved = dict(state)
+    if "step" in moved:
+        moved["step"] = moved["step"].to(device=param.device, dtype=torch.float32)
+    return moved
+
+
+def fused_adam(optimizer):
+    problem = _unfusable(optimizer)
+    if problem is not None:
+        raise ValueError(problem)
+    fused = {"fused": True, "foreach": False}
+    replacement = torch.optim.Adam([{**g, **fused} for g in optimizer.param_groups],
+                                   **{**optimizer.defaults, **fused})
+    for param, state in optimizer.state.items():
+        if state:
+            replacement.state[param] = _moved_state(state, param)
     return replacement
 
 
 def enable_fused_adam(model_type):
-    """Re-wraps GaussianModel.training_setup and .restore so the optimizer is
-    fused Adam after setup and after a checkpoint restore."""
-    setup, restore = model_type.training_setup, model_type.restore
+    """Swaps the model's optimizer for fused Adam after `training_setup` and
+    after `restore` (a checkpoint restore rebuilds the optimizer)."""
 
-    def training_setup(model, *args, **kwargs):
-        setup(model, *args, **kwargs)
-        model.optimizer = fused_adam(model.optimizer)
+    def after(method):
+        def wrapped(model, *args, **kwargs):
+            method(model, *args, **kwargs)
+            model.optimizer = fused_adam(model.optimizer)
+        return wrapped
 
-    def restore_checkpoint(model, *args, **kwargs):
-        restore(model, *args, **kwargs)
-        model.optimizer = fused_adam(model.optimizer)
-
-    model_type.training_setup = training_setup
-    model_type.restore = restore_checkpoint
+    model_type.training_setup = after(model_type.training_setup)
+    model_type.restore = after(model_type.restore)
