@@ -124,6 +124,16 @@ __device__ __forceinline__ void covariance2d(const Projection2& P, const float c
   c = P.A[3] * u1[0] + P.A[4] * u1[1] + P.A[5] * u1[2];
 }
 
+// Exponent p = -1/2 d^T Q d of a Gaussian at offset d = (dx, dy) = mean -
+// pixel, Q = [[co.x, co.y], [co.y, co.z]]. Every rounding is explicit, so the
+// forward compositing and the backward walk (which must replay the forward's
+// contribution decisions exactly) get the same bits whatever the compiler
+// contracts elsewhere.
+__device__ __forceinline__ float gauss_power(float4 co, float dx, float dy) {
+  const float diag = __fmaf_rn(__fmul_rn(co.x, dx), dx, __fmul_rn(__fmul_rn(co.z, dy), dy));
+  return __fmaf_rn(-0.5f, diag, -__fmul_rn(__fmul_rn(co.y, dx), dy));
+}
+
 __device__ __forceinline__ float ndc_to_pixel(float v, int size) {
   return ((v + 1.f) * size - 1.f) * 0.5f;
 }

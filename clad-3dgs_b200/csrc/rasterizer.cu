@@ -39,6 +39,7 @@
 
 #include "clad3dgs_b200.h"
 #include "gaussian_math.cuh"
+#include "raster_adjoint.cuh"
 #include "raster_math.cuh"
 #include "sh_colour.cuh"
 
@@ -670,7 +671,7 @@ __global__ void __launch_bounds__(kTilePixels)
       ++contributor;
       const float dx = s_xy[j].x - fx, dy = s_xy[j].y - fy;
       const float4 co = s_co[j];
-      const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
+      const float power = gauss_power(co, dx, dy);
       if (power > 0.f) continue;
       const float alpha = fminf(kMaxAlpha, co.w * __expf(power));
       if (alpha < kMinAlpha) continue;
@@ -700,7 +701,8 @@ __global__ void __launch_bounds__(kTilePixels)
 }
 
 // ---------------------------------------------------------------------------
-// Pixel backward.
+// Pixel backward (the algebra, warp reductions and field slots are in
+// raster_adjoint.cuh).
 
 struct PixelGrads {
   float* dmean2d;    // [P][3]
@@ -710,37 +712,59 @@ struct PixelGrads {
   float* dinvdepth;  // [P] or null
 };
 
-// Address of adjoint field f (0-2 RGB, 3-4 mean x/y, 5-7 conic a/b/c,
-// 8 opacity, 9 inverse depth) of Gaussian id.
+// Address of adjoint field f (Field slots) of Gaussian id.
 __device__ __forceinline__ float* field_address(const PixelGrads& o, uint32_t id, int f) {
   switch (f) {
-    case 0: case 1: case 2: return o.dcolor + 3 * size_t(id) + f;
-    case 3: case 4: return o.dmean2d + 3 * size_t(id) + (f - 3);
-    case 5: return o.dconic + 4 * size_t(id);
-    case 6: return o.dconic + 4 * size_t(id) + 1;
-    case 7: return o.dconic + 4 * size_t(id) + 3;
-    case 8: return o.dopacity + id;
+    case kRed: case kGreen: case kBlue: return o.dcolor + 3 * size_t(id) + f;
+    case kMeanX: case kMeanY: return o.dmean2d + 3 * size_t(id) + (f - kMeanX);
+    case kConicA: return o.dconic + 4 * size_t(id);
+    case kConicB: return o.dconic + 4 * size_t(id) + 1;
+    case kConicC: return o.dconic + 4 * size_t(id) + 3;
+    case kOpacity: return o.dopacity + id;
     default: return o.dinvdepth + id;
   }
 }
 
-// Sums v[0..9] over the warp; afterwards lane L holds the total of field
-// (L >> 1) & 15 (lanes L and L ^ 1 hold the same value). Each butterfly step
-// halves the number of fields a lane keeps, so 16 shuffles cover 10 fields.
-__device__ __forceinline__ float transpose_reduce(float v[16], int lane) {
-#pragma unroll
-  for (int step = 0; step < 4; ++step) {
-    const int half = 8 >> step;          // fields kept after this step
-    const int mask = 16 >> step;         // lane bit that picks the half
-    const bool upper = lane & mask;
-#pragma unroll
-    for (int k = 0; k < half; ++k) {
-      const float send = upper ? v[k] : v[k + half];
-      const float keep = upper ? v[k + half] : v[k];
-      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
-    }
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+// Shared-memory batch of Gaussians of one tile, staged back to front.
+struct TileBatch {
+  uint32_t id[kBatch];
+  float2 xy[kBatch];
+  float4 co[kBatch];
+  float rgb[3 * kBatch];
+  float inv[kBatch];
+};
+
+// Loads slot `slot` of the batch starting `base` Gaussians from the back of
+// the first `todo` entries of the tile's list.
+__device__ __forceinline__ void stage_back_to_front(TileBatch& s, int slot, int base, int todo,
+                                                    uint2 range,
+                                                    const uint32_t* __restrict__ point_list,
+                                                    const float2* __restrict__ mean2d,
+                                                    const float4* __restrict__ conic_opacity,
+                                                    const float* __restrict__ rgb,
+                                                    const float* __restrict__ depth) {
+  const int k = base + slot;
+  if (k >= todo) return;
+  const uint32_t id = point_list[range.x + todo - k - 1];
+  s.id[slot] = id;
+  s.xy[slot] = mean2d[id];
+  s.co[slot] = conic_opacity[id];
+  s.rgb[3 * slot] = rgb[3 * id];
+  s.rgb[3 * slot + 1] = rgb[3 * id + 1];
+  s.rgb[3 * slot + 2] = rgb[3 * id + 2];
+  s.inv[slot] = 1.f / depth[id];
+}
+
+// Largest last-contributor count over the block's pixels: no pixel of the
+// tile has a contributor past it, so the walk starts there instead of at the
+// end of the tile's list (the Gaussians skipped contribute nothing).
+__device__ __forceinline__ int block_walk_length(uint32_t my_last, uint32_t* s_max) {
+  if (threadIdx.x == 0) *s_max = 0;
+  __syncthreads();
+  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, my_last);
+  if ((threadIdx.x & 31) == 0) atomicMax(s_max, warp_max);
+  __syncthreads();
+  return int(*s_max);
 }
 
 // Modes 0 and 1, one pixel per thread (mode 2 is render_backward_pairs_kernel).
@@ -759,225 +783,52 @@ __global__ void __launch_bounds__(kTilePixels)
   const int tile = blockIdx.y * grid_x + blockIdx.x;
   const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
   const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;
-  const bool inside = px < width && py < height;
-  const int pix = py * width + px;
   const int lane = threadIdx.x & 31;
-  const float fx = (float)px, fy = (float)py;
   const uint2 range = ranges[tile];
-  __shared__ uint32_t s_id[kBatch];
-  __shared__ uint32_t s_last_max;
-  __shared__ float2 s_xy[kBatch];
-  __shared__ float4 s_co[kBatch];
-  __shared__ float s_rgb[3 * kBatch];
-  __shared__ float s_inv[kBatch];
-  const int hw = width * height;
-  const float T_final = inside ? final_t[pix] : 0.f;
-  float T = T_final;
-  const uint32_t last = inside ? n_contrib[pix] : 0;
-  // No pixel of the tile has a contributor past the largest last-contributor
-  // index, so the back-to-front walk starts there instead of at the end of the
-  // tile's range (identical results; the skipped Gaussians contribute nothing).
-  if (threadIdx.x == 0) s_last_max = 0;
-  __syncthreads();
-  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, last);
-  if (lane == 0) atomicMax(&s_last_max, warp_max);
-  __syncthreads();
-  const int todo = int(s_last_max);
-  uint32_t contributor = todo;
-  float dpix[3] = {0.f, 0.f, 0.f}, dinv = 0.f;
-  if (inside) {
-    dpix[0] = dpixels[pix];
-    dpix[1] = dpixels[hw + pix];
-    dpix[2] = dpixels[2 * hw + pix];
-    if (dinvdepth_pixels) dinv = dinvdepth_pixels[pix];
-  }
-  const float bg_dot = bg[0] * dpix[0] + bg[1] * dpix[1] + bg[2] * dpix[2];
-  float acc[3] = {0.f, 0.f, 0.f}, acc_inv = 0.f;
-  float last_alpha = 0.f, last_rgb[3] = {0.f, 0.f, 0.f}, last_inv = 0.f;
-  const float ddx = 0.5f * width, ddy = 0.5f * height;
+  __shared__ TileBatch s;
+  __shared__ uint32_t s_max;
+  PixelWalk pixel;
+  walk_begin(pixel, px, py, width, height, final_t, n_contrib, dpixels, dinvdepth_pixels, bg);
+  const int todo = block_walk_length(pixel.last, &s_max);
+  const float fx = (float)px, fy = (float)py;
+  const float half_w = 0.5f * width, half_h = 0.5f * height;
+  const int fields = out.dinvdepth ? kFields : kFields - 1;
   for (int base = 0; base < todo; base += kBatch) {
     __syncthreads();
-    const int k = base + threadIdx.x;
-    if (k < todo) {
-      const uint32_t id = point_list[range.x + todo - k - 1];
-      s_id[threadIdx.x] = id;
-      s_xy[threadIdx.x] = mean2d[id];
-      s_co[threadIdx.x] = conic_opacity[id];
-      s_rgb[3 * threadIdx.x] = rgb[3 * id];
-      s_rgb[3 * threadIdx.x + 1] = rgb[3 * id + 1];
-      s_rgb[3 * threadIdx.x + 2] = rgb[3 * id + 2];
-      s_inv[threadIdx.x] = 1.f / depth[id];
-    }
+    stage_back_to_front(s, threadIdx.x, base, todo, range, point_list, mean2d, conic_opacity,
+                        rgb, depth);
     __syncthreads();
     const int count = min(kBatch, todo - base);
     for (int j = 0; j < count; ++j) {
-      --contributor;
-      bool contrib = inside && contributor < last;
-      const float4 co = s_co[j];
-      const float dx = s_xy[j].x - fx, dy = s_xy[j].y - fy;
-      const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
-      contrib = contrib && power <= 0.f;
-      const float G = __expf(power);
-      const float alpha = fminf(kMaxAlpha, co.w * G);
-      contrib = contrib && alpha >= kMinAlpha;
       float f[16];
-      if (!contrib) continue;
-      {
-        const float inv_keep = 1.f / (1.f - alpha);  // one reciprocal for T and the bg term
-        T = T * inv_keep;
-        const float w = alpha * T;
-        float dl_dalpha = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-          const float cc = s_rgb[3 * j + ch];
-          acc[ch] = last_alpha * last_rgb[ch] + (1.f - last_alpha) * acc[ch];
-          last_rgb[ch] = cc;
-          dl_dalpha += (cc - acc[ch]) * dpix[ch];
-          f[ch] = w * dpix[ch];
-        }
-        const float inv = s_inv[j];
-        acc_inv = last_alpha * last_inv + (1.f - last_alpha) * acc_inv;
-        last_inv = inv;
-        dl_dalpha += (inv - acc_inv) * dinv;
-        f[9] = w * dinv;
-        dl_dalpha *= T;
-        last_alpha = alpha;
-        dl_dalpha += (-T_final * inv_keep) * bg_dot;
-        const float dl_dg = co.w * dl_dalpha;
-        const float gdx = G * dx, gdy = G * dy;
-        const float dg_ddx = -gdx * co.x - gdy * co.y;
-        const float dg_ddy = -gdy * co.z - gdx * co.y;
-        f[3] = dl_dg * dg_ddx * ddx;
-        f[4] = dl_dg * dg_ddy * ddy;
-        f[5] = -0.5f * gdx * dx * dl_dg;
-        f[6] = -0.5f * gdx * dy * dl_dg;
-        f[7] = -0.5f * gdy * dy * dl_dg;
-        f[8] = G * dl_dalpha;
-      }
-      const uint32_t id = s_id[j];
-      const int nf = out.dinvdepth ? 10 : 9;
+      for (int q = 0; q < 16; ++q) f[q] = 0.f;
+      const float4 co = s.co[j];
+      const uint32_t index = uint32_t(todo - 1 - (base + j));
+      if (!walk_step(pixel, index, s.xy[j].x - fx, s.xy[j].y - fy, co, s.rgb + 3 * j,
+                     s.inv[j], f))
+        continue;
+      finish_moments(f, co, half_w, half_h);
+      const uint32_t id = s.id[j];
+      auto dest = [&](int q) { return field_address(out, id, q); };
       if constexpr (Mode == 0) {
-        atomicAdd(out.dcolor + 3 * size_t(id), f[0]);
-        atomicAdd(out.dcolor + 3 * size_t(id) + 1, f[1]);
-        atomicAdd(out.dcolor + 3 * size_t(id) + 2, f[2]);
-        atomicAdd(out.dmean2d + 3 * size_t(id), f[3]);
-        atomicAdd(out.dmean2d + 3 * size_t(id) + 1, f[4]);
-        atomicAdd(out.dconic + 4 * size_t(id), f[5]);
-        atomicAdd(out.dconic + 4 * size_t(id) + 1, f[6]);
-        atomicAdd(out.dconic + 4 * size_t(id) + 3, f[7]);
-        atomicAdd(out.dopacity + id, f[8]);
-        if (out.dinvdepth) atomicAdd(out.dinvdepth + id, f[9]);
+        for (int q = 0; q < fields; ++q) atomicAdd(dest(q), f[q]);
       } else {
-        // The reference's helper: whole warp on one Gaussian -> reduce, else
-        // per-lane atomics.
-        const bool full = __match_any_sync(__activemask(), id) == 0xffffffffu;
-        for (int q = 0; q < nf; ++q) {
-          float v = f[q];
-          if (full) {
-#pragma unroll
-            for (int off = 16; off; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
-            if (lane == 0) atomicAdd(field_address(out, id, q), v);
-          } else {
-            atomicAdd(field_address(out, id, q), v);
-          }
-        }
+        accumulate_by_key(id, f, fields, lane, dest);
       }
     }
   }
 }
 
 // Mode 2 with kPixelsPerThread pixels per thread: rows y, y + 16/k, ... of the
-// tile. A thread keeps every pixel's back-to-front state; per Gaussian it adds
-// its pixels' adjoints before the warp reduction, so each reduction covers
-// 32 k pixels.
+// tile. Per Gaussian a thread adds its pixels' moments first, so each warp
+// reduction covers 32 k pixels.
 #ifndef CLAD3DGS_PIXELS_PER_THREAD
 #define CLAD3DGS_PIXELS_PER_THREAD 4
 #endif
 constexpr int kPixelsPerThread = CLAD3DGS_PIXELS_PER_THREAD;
 constexpr int kPairThreads = kTilePixels / kPixelsPerThread;
-
-struct PixelState {
-  bool inside;
-  float fx, fy, T, T_final, dpix[3], dinv, bg_dot;
-  uint32_t last, contributor;
-  float acc[3], acc_inv, last_alpha, last_rgb[3], last_inv;
-};
-
-__device__ __forceinline__ void pixel_setup(PixelState& s, int px, int py, int width,
-                                            int height, const float* __restrict__ final_t,
-                                            const uint32_t* __restrict__ n_contrib,
-                                            const float* __restrict__ dpixels,
-                                            const float* __restrict__ dinvdepth_pixels,
-                                            const float* __restrict__ bg) {
-  s.inside = px < width && py < height;
-  const int pix = py * width + px, hw = width * height;
-  s.fx = (float)px;
-  s.fy = (float)py;
-  s.T_final = s.inside ? final_t[pix] : 0.f;
-  s.T = s.T_final;
-  s.last = s.inside ? n_contrib[pix] : 0;
-  s.dpix[0] = s.dpix[1] = s.dpix[2] = 0.f;
-  s.dinv = 0.f;
-  if (s.inside) {
-    s.dpix[0] = dpixels[pix];
-    s.dpix[1] = dpixels[hw + pix];
-    s.dpix[2] = dpixels[2 * hw + pix];
-    if (dinvdepth_pixels) s.dinv = dinvdepth_pixels[pix];
-  }
-  s.bg_dot = bg[0] * s.dpix[0] + bg[1] * s.dpix[1] + bg[2] * s.dpix[2];
-  s.acc[0] = s.acc[1] = s.acc[2] = 0.f;
-  s.acc_inv = 0.f;
-  s.last_alpha = 0.f;
-  s.last_rgb[0] = s.last_rgb[1] = s.last_rgb[2] = 0.f;
-  s.last_inv = 0.f;
-}
-
-// One (pixel, Gaussian) step of the walk: the same arithmetic as the one-pixel
-// kernel, adding the pixel's ten adjoints into f; returns whether it contributed.
-__device__ __forceinline__ bool pixel_step(PixelState& s, float2 xy, float4 co,
-                                           const float* rgb3, float inv, float ddx,
-                                           float ddy, float f[16]) {
-  --s.contributor;
-  bool contrib = s.inside && s.contributor < s.last;
-  const float dx = xy.x - s.fx, dy = xy.y - s.fy;
-  const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
-  contrib = contrib && power <= 0.f;
-  const float G = __expf(power);
-  const float alpha = fminf(kMaxAlpha, co.w * G);
-  contrib = contrib && alpha >= kMinAlpha;
-  if (contrib) {
-    const float inv_keep = 1.f / (1.f - alpha);
-    s.T = s.T * inv_keep;
-    const float w = alpha * s.T;
-    float dl_dalpha = 0.f;
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) {
-      const float cc = rgb3[ch];
-      s.acc[ch] = s.last_alpha * s.last_rgb[ch] + (1.f - s.last_alpha) * s.acc[ch];
-      s.last_rgb[ch] = cc;
-      dl_dalpha += (cc - s.acc[ch]) * s.dpix[ch];
-      f[ch] += w * s.dpix[ch];
-    }
-    s.acc_inv = s.last_alpha * s.last_inv + (1.f - s.last_alpha) * s.acc_inv;
-    s.last_inv = inv;
-    dl_dalpha += (inv - s.acc_inv) * s.dinv;
-    f[9] += w * s.dinv;
-    dl_dalpha *= s.T;
-    s.last_alpha = alpha;
-    dl_dalpha += (-s.T_final * inv_keep) * s.bg_dot;
-    const float dl_dg = co.w * dl_dalpha;
-    const float gdx = G * dx, gdy = G * dy;
-    const float dg_ddx = -gdx * co.x - gdy * co.y;
-    const float dg_ddy = -gdy * co.z - gdx * co.y;
-    f[3] += dl_dg * dg_ddx * ddx;
-    f[4] += dl_dg * dg_ddy * ddy;
-    f[5] += -0.5f * gdx * dx * dl_dg;
-    f[6] += -0.5f * gdx * dy * dl_dg;
-    f[7] += -0.5f * gdy * dy * dl_dg;
-    f[8] += G * dl_dalpha;
-  }
-  return contrib;
-}
+constexpr int kRowStep = kTileY / kPixelsPerThread;
 
 __global__ void __launch_bounds__(kPairThreads)
     render_backward_pairs_kernel(const uint2* __restrict__ ranges,
@@ -995,72 +846,106 @@ __global__ void __launch_bounds__(kPairThreads)
   const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;  // first row of this thread
   const int lane = threadIdx.x & 31;
   const uint2 range = ranges[tile];
-  __shared__ uint32_t s_id[kBatch];
-  __shared__ uint32_t s_last_max;
-  __shared__ float2 s_xy[kBatch];
-  __shared__ float4 s_co[kBatch];
-  __shared__ float s_rgb[3 * kBatch];
-  __shared__ float s_inv[kBatch];
-  PixelState st[kPixelsPerThread];
+  __shared__ TileBatch s;
+  __shared__ uint32_t s_max;
+  PixelWalk pixel[kPixelsPerThread];
   uint32_t my_last = 0;
 #pragma unroll
   for (int r = 0; r < kPixelsPerThread; ++r) {
-    pixel_setup(st[r], px, py + r * (kTileY / kPixelsPerThread), width, height, final_t,
-                n_contrib, dpixels, dinvdepth_pixels, bg);
-    my_last = max(my_last, st[r].last);
+    walk_begin(pixel[r], px, py + r * kRowStep, width, height, final_t, n_contrib, dpixels,
+               dinvdepth_pixels, bg);
+    my_last = max(my_last, pixel[r].last);
   }
-  // Start at the tile's largest last-contributor index (see the one-pixel kernel).
-  if (threadIdx.x == 0) s_last_max = 0;
-  __syncthreads();
-  const uint32_t warp_max = __reduce_max_sync(0xffffffffu, my_last);
-  if (lane == 0) atomicMax(&s_last_max, warp_max);
-  __syncthreads();
-  const int todo = int(s_last_max);
-#pragma unroll
-  for (int r = 0; r < kPixelsPerThread; ++r) st[r].contributor = todo;
-  const float ddx = 0.5f * width, ddy = 0.5f * height;
-  const int nf = out.dinvdepth ? 10 : 9;
+  const int todo = block_walk_length(my_last, &s_max);
+  const float fx = (float)px;
+  const float half_w = 0.5f * width, half_h = 0.5f * height;
+  const int fields = out.dinvdepth ? kFields : kFields - 1;
   for (int base = 0; base < todo; base += kBatch) {
     __syncthreads();
 #pragma unroll
-    for (int h = 0; h < kPixelsPerThread; ++h) {
-      const int slot = threadIdx.x + h * kPairThreads;
-      const int k = base + slot;
-      if (k < todo) {
-        const uint32_t id = point_list[range.x + todo - k - 1];
-        s_id[slot] = id;
-        s_xy[slot] = mean2d[id];
-        s_co[slot] = conic_opacity[id];
-        s_rgb[3 * slot] = rgb[3 * id];
-        s_rgb[3 * slot + 1] = rgb[3 * id + 1];
-        s_rgb[3 * slot + 2] = rgb[3 * id + 2];
-        s_inv[slot] = 1.f / depth[id];
-      }
-    }
+    for (int h = 0; h < kPixelsPerThread; ++h)
+      stage_back_to_front(s, threadIdx.x + h * kPairThreads, base, todo, range, point_list,
+                          mean2d, conic_opacity, rgb, depth);
     __syncthreads();
     const int count = min(kBatch, todo - base);
     for (int j = 0; j < count; ++j) {
       float f[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) f[q] = 0.f;
-      const float2 xy = s_xy[j];
-      const float4 co = s_co[j];
-      const float* rgb3 = s_rgb + 3 * j;
-      const float inv = s_inv[j];
+      const float2 xy = s.xy[j];
+      const float4 co = s.co[j];
+      const uint32_t index = uint32_t(todo - 1 - (base + j));
+      const float dx = xy.x - fx;
       bool any = false;
 #pragma unroll
       for (int r = 0; r < kPixelsPerThread; ++r)
-        any = pixel_step(st[r], xy, co, rgb3, inv, ddx, ddy, f) || any;
+        any = walk_step(pixel[r], index, dx, xy.y - (float)(py + r * kRowStep), co,
+                        s.rgb + 3 * j, s.inv[j], f) || any;
       if (!__any_sync(0xffffffffu, any)) continue;
-      const float total = transpose_reduce(f, lane);
-      const int q = (lane >> 1) & 15;
-      if ((lane & 1) == 0 && q < nf) atomicAdd(field_address(out, s_id[j], q), total);
+      finish_moments(f, co, half_w, half_h);
+      const uint32_t id = s.id[j];
+      accumulate_converged(f, fields, lane, [&](int q) { return field_address(out, id, q); });
     }
   }
 }
 
+// Test probe of the accumulation helpers above on caller-given lane streams:
+// thread i (linear index over the grid, blocks of whole warps) holds key[i],
+// active[i] and values[i][0..fields). Mode 0: per-lane atomics; mode 1:
+// accumulate_by_key (the pixel backward's mode 1); mode 2:
+// accumulate_converged with every lane of the warp taking part and lanes that
+// are inactive or past n adding zeros (keys must be the same for all lanes of
+// a warp; a lane that disagrees records -1 in grouped[i] and its warp adds
+// nothing). grouped[i] records whether lane i's values went through a warp
+// reduction. Keys outside [0, rows) record -2 and add nothing.
+__global__ void warp_probe_kernel(int mode, int n, int fields, const int* __restrict__ keys,
+                                  const unsigned char* __restrict__ active,
+                                  const float* __restrict__ values, float* __restrict__ out,
+                                  int rows, int* __restrict__ grouped) {
+  const int in_block = (threadIdx.z * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;
+  const int i = blockIdx.x * blockDim.x * blockDim.y * blockDim.z + in_block;
+  const int lane = in_block & 31;
+  if (mode == 2) {
+    const bool in_range = i < n;
+    const unsigned lanes = __ballot_sync(0xffffffffu, in_range);
+    if (lanes == 0u) return;  // the whole warp is past n
+    const int mine = in_range ? keys[i] : 0;
+    const int key = __shfl_sync(0xffffffffu, mine, __ffs(lanes) - 1);
+    const bool agree = __all_sync(0xffffffffu, !in_range || mine == key);
+    const bool valid = key >= 0 && key < rows;
+    if (!agree || !valid) {
+      if (in_range) grouped[i] = agree ? -2 : -1;
+      return;  // warp-uniform
+    }
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      v[q] = (in_range && active[i] && q < fields) ? values[size_t(i) * fields + q] : 0.f;
+    if (in_range) grouped[i] = 1;
+    accumulate_converged(v, fields, lane,
+                         [&](int q) { return out + size_t(key) * fields + q; });
+    return;
+  }
+  if (i >= n || !active[i]) return;
+  const int key = keys[i];
+  if (key < 0 || key >= rows) {
+    grouped[i] = -2;
+    return;
+  }
+  float v[16];
+  for (int q = 0; q < fields; ++q) v[q] = values[size_t(i) * fields + q];
+  auto dest = [&](int q) { return out + size_t(key) * fields + q; };
+  if (mode == 1) {
+    grouped[i] = whole_warp_on(uint32_t(key));
+    accumulate_by_key(uint32_t(key), v, fields, lane, dest);
+  } else {
+    grouped[i] = 0;
+    for (int q = 0; q < fields; ++q) atomicAdd(dest(q), v[q]);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// Geometry backward: one thread per Gaussian.
+// Geometry backward: one thread per Gaussian (algebra in raster_adjoint.cuh).
 
 struct GeomGrads {
   const float* dmean2d;    // [P][3]
@@ -1097,147 +982,130 @@ __global__ void preprocess_backward_kernel(
   const Vec3 t = affine3(cam.view, p);
   const float* cov = g.cov3d + 6 * i;
   const Projection2 J = screen_jacobian(t, cam.fx, cam.fy, cam.tan_x, cam.tan_y, cam.view);
+  const float* A0 = J.A;      // rows of A = J W
+  const float* A1 = J.A + 3;
+  // Screen covariance S2 (low-pass included) and the conic Q = S2^-1 of the forward.
   float a0, b, c0;
   covariance2d(J, cov, a0, b, c0);
-  const float a = a0 + kLowPass, c = c0 + kLowPass;
-  const float det0 = a0 * c0 - b * b;
-  const float det = a * c - b * b;
-  // Opacity: the renderer used opacity * s with s = sqrt(max(2.5e-5, det0/det)).
-  float dl_da = 0.f, dl_db = 0.f, dl_dc = 0.f;
-  const float dop_scaled = o.dopacity[i];
+  const Sym2 S2{a0 + kLowPass, b, c0 + kLowPass};
+  const float det = S2.xx * S2.yy - b * b;
+  const Sym2 Q{S2.yy / det, -b / det, S2.xx / det};
+  // dL/dS2 = -Q Gq Q.
+  const float* dq = o.dconic + 4 * i;
+  const Sym2 QGQ = sandwich2(Q, Sym2{dq[0], dq[1], dq[3]});
+  Sym2 Gs{-QGQ.xx, -QGQ.xy, -QGQ.yy};
+  // Antialiasing scaled the opacity by s = sqrt(max(2.5e-5, r)),
+  // r = det(S2 - 0.3 I) / det(S2).
   if (antialiasing) {
+    const float dop_scaled = o.dopacity[i];
+    const float det0 = a0 * c0 - b * b;
     const float r = det0 / det;
     const float s = sqrtf(fmaxf(0.000025f, r));
     o.dopacity[i] = dop_scaled * s;
     if (r > 0.000025f) {
-      const float dl_ds = dop_scaled * opacities[i];
-      const float dl_dr = dl_ds * 0.5f / s;
-      const float id2 = 1.f / (det * det);
-      // r = det0 / det; d det0 = (c0, -2b, a0), d det = (c, -2b, a) wrt (a0, b, c0)
-      dl_da += dl_dr * (c0 * det - det0 * c) * id2;
-      dl_db += dl_dr * (-2.f * b * det + 2.f * b * det0) * id2;
-      dl_dc += dl_dr * (a0 * det - det0 * a) * id2;
+      const float dr = dop_scaled * opacities[i] * 0.5f / s;
+      const float k0 = dr / det, k1 = dr * det0 / (det * det);
+      Gs.xx += k0 * c0 - k1 * S2.yy;
+      Gs.xy -= (k0 - k1) * b;
+      Gs.yy += k0 * a0 - k1 * S2.xx;
     }
   }
-  // Conic = inverse of [[a, b], [b, c]]; dconic.y holds half the adjoint of the
-  // off-diagonal value (each symmetric entry receives it).
-  const float* dq = o.dconic + 4 * i;
-  const float gx = dq[0], gy2 = dq[1], gz = dq[3];
-  const float id2 = 1.f / (det * det + 0.0000001f);
-  if (id2 != 0.f) {
-    dl_da += id2 * (-c * c * gx + 2.f * b * c * gy2 + (det - a * c) * gz);
-    dl_dc += id2 * (-a * a * gz + 2.f * a * b * gy2 + (det - a * c) * gx);
-    dl_db += id2 * 2.f * (b * c * gx - (det + 2.f * b * b) * gy2 + a * b * gz);
-  }
-  // Screen covariance A Sigma A^T -> Sigma (six unique entries).
-  const float* A0 = J.A;
-  const float* A1 = J.A + 3;
-  float dcov[6];
-  {
-    int k = 0;
-    for (int r = 0; r < 3; ++r)
-      for (int s = r; s < 3; ++s, ++k) {
-        const float mul = r == s ? 1.f : 2.f;
-        const float sym_b = r == s ? A0[r] * A1[r] : A0[r] * A1[s] + A0[s] * A1[r];
-        dcov[k] = mul * (A0[r] * A0[s] * dl_da + A1[r] * A1[s] * dl_dc) + sym_b * dl_db;
-      }
-  }
+  // Gs A (2 x 3) serves both adjoints of the congruence S2 = A S3 A^T.
+  float GA0[3], GA1[3];
 #pragma unroll
-  for (int k = 0; k < 6; ++k) o.dcov3d[6 * i + k] = dcov[k];
-  // Through the projection Jacobian to the camera-space mean.
-  const float S[9] = {cov[0], cov[1], cov[2], cov[1], cov[3], cov[4], cov[2], cov[4], cov[5]};
-  float sa0[3], sa1[3];
-#pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    sa0[k] = S[3 * k] * A0[0] + S[3 * k + 1] * A0[1] + S[3 * k + 2] * A0[2];
-    sa1[k] = S[3 * k] * A1[0] + S[3 * k + 1] * A1[1] + S[3 * k + 2] * A1[2];
+  for (int c = 0; c < 3; ++c) {
+    GA0[c] = Gs.xx * A0[c] + Gs.xy * A1[c];
+    GA1[c] = Gs.xy * A0[c] + Gs.yy * A1[c];
   }
+  // dL/dS3 = A^T Gs A, symmetric; stored as the upper triangle with the
+  // off-diagonals counted for both positions.
+  float G3[9];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) G3[3 * r + c] = A0[r] * GA0[c] + A1[r] * GA1[c];
+  o.dcov3d[6 * i + 0] = G3[0];
+  o.dcov3d[6 * i + 1] = 2.f * G3[1];
+  o.dcov3d[6 * i + 2] = 2.f * G3[2];
+  o.dcov3d[6 * i + 3] = G3[4];
+  o.dcov3d[6 * i + 4] = 2.f * G3[5];
+  o.dcov3d[6 * i + 5] = G3[8];
+  // dL/dA = 2 Gs A S3.
+  float S3[9];
+  full3(cov, S3);
   float dA0[3], dA1[3];
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    dA0[k] = 2.f * dl_da * sa0[k] + dl_db * sa1[k];
-    dA1[k] = dl_db * sa0[k] + 2.f * dl_dc * sa1[k];
+  for (int c = 0; c < 3; ++c) {
+    dA0[c] = 2.f * (GA0[0] * S3[c] + GA0[1] * S3[3 + c] + GA0[2] * S3[6 + c]);
+    dA1[c] = 2.f * (GA1[0] * S3[c] + GA1[1] * S3[3 + c] + GA1[2] * S3[6 + c]);
   }
-  // A = J W: dJ = dA W^T; J00 = fx/z, J02 = -fx tx/z^2, J11 = fy/z, J12 = -fy ty/z^2.
-  float dJ00 = 0.f, dJ02 = 0.f, dJ11 = 0.f, dJ12 = 0.f;
+  // A = J W with W[k][c] = view[4c + k]: dL/dJ = dL/dA W^T. J's varying
+  // entries: J00 = fx/z, J02 = -fx tx/z^2, J11 = fy/z, J12 = -fy ty/z^2.
+  float gJ00 = 0.f, gJ02 = 0.f, gJ11 = 0.f, gJ12 = 0.f;
 #pragma unroll
-  for (int col = 0; col < 3; ++col) {
-    dJ00 += dA0[col] * cam.view[4 * col + 0];
-    dJ02 += dA0[col] * cam.view[4 * col + 2];
-    dJ11 += dA1[col] * cam.view[4 * col + 1];
-    dJ12 += dA1[col] * cam.view[4 * col + 2];
+  for (int c = 0; c < 3; ++c) {
+    gJ00 += dA0[c] * cam.view[4 * c + 0];
+    gJ02 += dA0[c] * cam.view[4 * c + 2];
+    gJ11 += dA1[c] * cam.view[4 * c + 1];
+    gJ12 += dA1[c] * cam.view[4 * c + 2];
   }
   const float iz = 1.f / J.tz, iz2 = iz * iz, iz3 = iz2 * iz;
-  const float dtx = (J.clamp_x ? 0.f : 1.f) * -cam.fx * iz2 * dJ02;
-  const float dty = (J.clamp_y ? 0.f : 1.f) * -cam.fy * iz2 * dJ12;
-  float dtz = -cam.fx * iz2 * dJ00 - cam.fy * iz2 * dJ11 + 2.f * cam.fx * J.tx * iz3 * dJ02 +
-              2.f * cam.fy * J.ty * iz3 * dJ12;
-  if (o.dinvdepth) dtz += -o.dinvdepth[i] * iz2;
-  // Camera-space -> world: t = W p + b, so dp = W^T dt.
+  const float dJ02_dtx = -cam.fx * iz2, dJ12_dty = -cam.fy * iz2;
+  const float dJ00_dz = -cam.fx * iz2, dJ11_dz = -cam.fy * iz2;
+  const float dJ02_dz = 2.f * cam.fx * J.tx * iz3, dJ12_dz = 2.f * cam.fy * J.ty * iz3;
+  float dt[3];
+  dt[0] = J.clamp_x ? 0.f : gJ02 * dJ02_dtx;
+  dt[1] = J.clamp_y ? 0.f : gJ12 * dJ12_dty;
+  dt[2] = gJ00 * dJ00_dz + gJ11 * dJ11_dz + gJ02 * dJ02_dz + gJ12 * dJ12_dz;
+  if (o.dinvdepth) dt[2] -= o.dinvdepth[i] * iz2;  // d(1/z)/dz = -1/z^2
+  // t = W p + b: dL/dp = W^T dL/dt.
   float dm[3];
 #pragma unroll
   for (int k = 0; k < 3; ++k)
-    dm[k] = cam.view[4 * k + 0] * dtx + cam.view[4 * k + 1] * dty + cam.view[4 * k + 2] * dtz;
-  // Screen mean (NDC adjoint) -> world mean through the projective divide.
+    dm[k] = cam.view[4 * k + 0] * dt[0] + cam.view[4 * k + 1] * dt[1] +
+            cam.view[4 * k + 2] * dt[2];
+  // Screen mean in NDC, h.xy / (h.w + 1e-7) with h = proj [p, 1]:
+  // d ndc / dp_k = (proj_row(k) - ndc * proj_w(k)) / (h.w + 1e-7).
   {
-    const float hw = affine_w(cam.proj, p);
+    const float iw = 1.f / (affine_w(cam.proj, p) + 0.0000001f);
     const Vec3 h = affine3(cam.proj, p);
-    const float iw = 1.f / (hw + 0.0000001f);
-    const float gxn = o.dmean2d[3 * i], gyn = o.dmean2d[3 * i + 1];
-    const float mx = h.x * iw * iw, my = h.y * iw * iw;
+    const float nx = h.x * iw, ny = h.y * iw;
+    const float gx = o.dmean2d[3 * i], gy = o.dmean2d[3 * i + 1];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      const float pk3 = cam.proj[4 * k + 3];
-      dm[k] += (cam.proj[4 * k + 0] * iw - pk3 * mx) * gxn +
-               (cam.proj[4 * k + 1] * iw - pk3 * my) * gyn;
+      const float pw = cam.proj[4 * k + 3];
+      dm[k] += iw * ((cam.proj[4 * k + 0] - nx * pw) * gx + (cam.proj[4 * k + 1] - ny * pw) * gy);
     }
   }
   // (The SH colour's share of dmeans, the view direction's adjoint, is added
   // by sh_backward_kernel afterwards.)
 #pragma unroll
   for (int k = 0; k < 3; ++k) o.dmeans[3 * i + k] += dm[k];
-  // Sigma = M M^T, M = R diag(s): dM = 2 G M with G the symmetric adjoint.
-  if (!cov3d_precomp) {
-    const float G[9] = {dcov[0], 0.5f * dcov[1], 0.5f * dcov[2], 0.5f * dcov[1], dcov[3],
-                        0.5f * dcov[4], 0.5f * dcov[2], 0.5f * dcov[4], dcov[5]};
-    const float s[3] = {scale_modifier * scales[3 * i], scale_modifier * scales[3 * i + 1],
-                        scale_modifier * scales[3 * i + 2]};
-    const float q[4] = {rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
-                        rotations[4 * i + 3]};
-    float R[9];
-    rotation(q, R);
-    float M[9], dM[9];
+  if (cov3d_precomp) return;
+  // S3 = M M^T with M = R diag(s): dL/dM = 2 G3 M; M_rc = R_rc s_c.
+  const float s[3] = {scale_modifier * scales[3 * i], scale_modifier * scales[3 * i + 1],
+                      scale_modifier * scales[3 * i + 2]};
+  const float q[4] = {rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
+                      rotations[4 * i + 3]};
+  float R[9];
+  rotation(q, R);
+  float dR[9];
 #pragma unroll
-    for (int r = 0; r < 3; ++r)
+  for (int c = 0; c < 3; ++c) {
+    float ds = 0.f;
 #pragma unroll
-      for (int col = 0; col < 3; ++col) M[3 * r + col] = R[3 * r + col] * s[col];
-#pragma unroll
-    for (int r = 0; r < 3; ++r)
-#pragma unroll
-      for (int col = 0; col < 3; ++col)
-        dM[3 * r + col] =
-            2.f * (G[3 * r] * M[col] + G[3 * r + 1] * M[3 + col] + G[3 * r + 2] * M[6 + col]);
-    // M_rc = R_rc s_c
-#pragma unroll
-    for (int col = 0; col < 3; ++col)
-      o.dscales[3 * i + col] =
-          scale_modifier * (dM[col] * R[col] + dM[3 + col] * R[3 + col] + dM[6 + col] * R[6 + col]);
-    float dR[9];
-#pragma unroll
-    for (int r = 0; r < 3; ++r)
-#pragma unroll
-      for (int col = 0; col < 3; ++col) dR[3 * r + col] = dM[3 * r + col] * s[col];
-    const float w = q[0], x = q[1], y = q[2], z = q[3];
-    // dR/dq for R(w, x, y, z) of the rotation() above.
-    o.drotations[4 * i + 0] = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] -
-                                     y * dR[6] + x * dR[7]);
-    o.drotations[4 * i + 1] = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] -
-                                     w * dR[5] + z * dR[6] + w * dR[7] - 2.f * x * dR[8]);
-    o.drotations[4 * i + 2] = 2.f * (-2.f * y * dR[0] + x * dR[1] + w * dR[2] + x * dR[3] +
-                                     z * dR[5] - w * dR[6] + z * dR[7] - 2.f * y * dR[8]);
-    o.drotations[4 * i + 3] = 2.f * (-2.f * z * dR[0] - w * dR[1] + x * dR[2] + w * dR[3] -
-                                     2.f * z * dR[4] + y * dR[5] + x * dR[6] + y * dR[7]);
+    for (int r = 0; r < 3; ++r) {
+      const float dM = 2.f * (G3[3 * r] * R[c] * s[c] + G3[3 * r + 1] * R[3 + c] * s[c] +
+                              G3[3 * r + 2] * R[6 + c] * s[c]);
+      ds += dM * R[3 * r + c];
+      dR[3 * r + c] = dM * s[c];
+    }
+    o.dscales[3 * i + c] = scale_modifier * ds;
   }
+  float dq4[4];
+  rotation_vjp(q, dR, dq4);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) o.drotations[4 * i + k] = dq4[k];
 }
 
 // SH colour of every drawn Gaussian (radius > 0): colour + 0.5, clamped at 0,
@@ -1496,6 +1364,28 @@ extern "C" int clad3dgs_raster_render_backward(
         img.ranges, point_list, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   return status_of(cudaPeekAtLastError(), "pixel backward");
+}
+
+extern "C" int clad3dgs_warp_accumulate_probe(int mode, int n, int fields, const int* keys,
+                                              const unsigned char* active,
+                                              const float* values, float* out, int rows,
+                                              int* grouped, int block_x, int block_y,
+                                              int block_z, cudaStream_t stream) {
+  if (mode < 0 || mode > 2)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "accumulation mode must be 0, 1 or 2");
+  if (fields < 1 || fields > 16)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "between 1 and 16 fields per lane");
+  const long block = long(block_x) * block_y * block_z;
+  if (block_x < 1 || block_y < 1 || block_z < 1 || block % 32 != 0 || block > 1024)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "blocks must hold whole warps (at most 1024 threads)");
+  if (n < 0 || rows < 0) return fail(CLAD3DGS_INVALID_ARGUMENT, "negative size");
+  if (n == 0) return CLAD3DGS_OK;
+  if (!keys || !active || !values || !out || !grouped)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "warp probe: null pointer");
+  const unsigned grid = unsigned((long(n) + block - 1) / block);
+  warp_probe_kernel<<<grid, dim3(block_x, block_y, block_z), 0, stream>>>(
+      mode, n, fields, keys, active, values, out, rows, grouped);
+  return status_of(cudaPeekAtLastError(), "warp probe");
 }
 
 // Full backward. Outputs (zeroed by the caller): dmean2d [P][3], dcolor [P][3],

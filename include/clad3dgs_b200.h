@@ -260,6 +260,24 @@ int clad3dgs_raster_render_backward(
     const float* dpixels, const float* dinvdepth_pixels, float* dmean2d, float* dconic,
     float* dopacity, float* dcolor, float* dinvdepth, int mode, cudaStream_t stream);
 
+/* Test probe of the pixel backward's warp accumulation (its helpers run on
+ * caller-given lane streams, for parity with the reference's own helper,
+ * WarpAccumulation.cuh:9-29, on the same streams). Thread i of the launch
+ * (linear index over blocks of block_x * block_y * block_z threads, a multiple
+ * of 32, like the reference's self-check SHGradientConsumer.cu:302-324) holds
+ * keys[i], active[i] and values[i][0..fields), 1 <= fields <= 16, and adds its
+ * values into out[keys[i]][0..fields) (rows = number of rows of out): mode 0
+ * per-lane atomics, mode 1 the reference's rule (accumulation mode 1), mode 2
+ * the converged-warp transposing reduction (accumulation mode 2; keys must
+ * agree within each warp, inactive lanes add zeros). grouped[i] receives 1 when
+ * lane i's values went through a warp reduction, 0 when not, -1 when mode 2
+ * found keys that differ within the warp (that warp adds nothing) and -2 for a
+ * key outside [0, rows). No counterpart in the reference's exported API. */
+int clad3dgs_warp_accumulate_probe(int mode, int n, int fields, const int* keys,
+                                   const unsigned char* active, const float* values,
+                                   float* out, int rows, int* grouped, int block_x,
+                                   int block_y, int block_z, cudaStream_t stream);
+
 /* Full backward (the renderer's rasterize_gaussians_backward, adapter.py:67-97)
  * or, with consume_sh, the consumed variant (prepare_native.py:32-93,
  * direct_inputs.py:151-171): the SH adjoint is applied by the fused SH + Adam

@@ -272,6 +272,73 @@ def raster_backward(scene, dpix, dinv):
     return out
 
 
+def pixel_tiles(mean2d, conic_opacity, rgb, depth, radii, width, height, bg, tiles, dpix):
+    """Pixel stage of projected 2D Gaussians on the listed tiles (double
+    precision; see oracle_pixel_tiles in raster_oracle.c). Inputs are the
+    float32 arrays the CUDA path reads. Returns a dict with colour [3,H,W]
+    and final_t [H,W] (only the listed tiles' pixels are written), the
+    adjoints dmean2d [P,2], dconic [P,3], dopacity [P], dcolor [P,3] from those
+    pixels, the matching sizes mag_* and the `ambiguous` flags [P]."""
+    P = int(mean2d.shape[0])
+    f32 = lambda a: np.ascontiguousarray(a, np.float32)
+    mean2d, conic_opacity, rgb, depth = map(f32, (mean2d, conic_opacity, rgb, depth))
+    radii = np.ascontiguousarray(radii, np.int32)
+    tiles = np.ascontiguousarray(tiles, np.int32)
+    bg, dpix = _d(bg), _d(dpix)
+    out = dict(color=np.zeros((3, height, width)), final_t=np.zeros((height, width)),
+               dmean2d=np.zeros((P, 2)), dconic=np.zeros((P, 3)), dopacity=np.zeros(P),
+               dcolor=np.zeros((P, 3)), mag_mean2d=np.zeros((P, 2)),
+               mag_conic=np.zeros((P, 3)), mag_opacity=np.zeros(P),
+               mag_color=np.zeros((P, 3)), ambiguous=np.zeros(P, np.uint8))
+    f = lib().oracle_pixel_tiles
+    f.restype = ctypes.c_int
+    status = f(ctypes.c_int(P), _dp(mean2d), _dp(conic_opacity), _dp(rgb), _dp(depth),
+               _dp(radii), ctypes.c_int(width), ctypes.c_int(height), _dp(bg),
+               ctypes.c_int(len(tiles)), _dp(tiles), _dp(dpix),
+               *[_dp(out[k]) for k in ("color", "final_t", "dmean2d", "dconic", "dopacity",
+                                      "dcolor", "mag_mean2d", "mag_conic", "mag_opacity",
+                                      "mag_color", "ambiguous")])
+    if status != 0:
+        raise MemoryError("oracle_pixel_tiles: out of memory")
+    return out
+
+
+def raster_backward_sized(scene, dpix, dinv):
+    """Pixel-stage adjoints with the sizes of their sums and the per-Gaussian
+    geometry map (see oracle_raster_backward_sized). Returns x_* and size_*
+    for mean2d [P,3], conic [P,4], opacity [P], color [P,3], invdepth [P], and
+    jac [P,65,10]: rows (dL/dopacity, dL/dmeans 3, dL/dcov3D 6, dL/dsh 48,
+    dL/dscales 3, dL/drotations 4), columns (dmean2D x, y, dconic a, b, c,
+    blended opacity, colour r, g, b, inverse depth)."""
+    s, args = _scene_args(scene)
+    P = s["P"]
+    shapes = dict(mean2d=(P, 3), conic=(P, 4), opacity=(P,), color=(P, 3), invdepth=(P,))
+    out = {f"{p}_{k}": np.zeros(v) for p in ("x", "size") for k, v in shapes.items()}
+    out["jac"] = np.zeros((P, 65, 10))
+    dpix, dinv = _d(dpix), _d(dinv)
+    lib().oracle_raster_backward_sized(
+        *args, _dp(dpix), _dp(dinv), *[_dp(out[f"x_{k}"]) for k in shapes],
+        *[_dp(out[f"size_{k}"]) for k in shapes], _dp(out["jac"]))
+    return out
+
+
+GEOMETRY_ROWS = dict(dopacity=slice(0, 1), dmeans=slice(1, 4), dcov3d=slice(4, 10),
+                     dsh=slice(10, 58), dscales=slice(58, 61), drots=slice(61, 65))
+
+
+def geometry_inputs(sized):
+    """The pixel-stage vector x [P,10] in the column order of `jac`."""
+    return np.concatenate([sized["x_mean2d"][:, :2], sized["x_conic"][:, [0, 1, 3]],
+                           sized["x_opacity"][:, None], sized["x_color"],
+                           sized["x_invdepth"][:, None]], 1)
+
+
+def geometry_input_sizes(sized):
+    return np.concatenate([sized["size_mean2d"][:, :2], sized["size_conic"][:, [0, 1, 3]],
+                           sized["size_opacity"][:, None], sized["size_color"],
+                           sized["size_invdepth"][:, None]], 1)
+
+
 def raster_loss(scene, dpix, dinv):
     s, args = _scene_args(scene)
     dpix, dinv = _d(dpix), _d(dinv)

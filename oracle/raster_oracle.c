@@ -195,20 +195,84 @@ static int by_depth(const void* a, const void* b) {
   return i < j ? -1 : (i > j);
 }
 
+/* Adjoints of one pixel's compositing, in double, from the quantities the
+ * forward stored: m contributors (front to back) with their alphas a[k], the
+ * transmittance in front of each, Tin[k], and per-Gaussian scalars
+ * g[k] = dL/dC . colour_k + dL/dinvdepth * invdepth_k. With the final
+ * transmittance Tf and bgdot = dL/dC . bg, the colour is
+ * C = sum_k c_k a_k Tin_k + Tf bg, Tin_{k+1} = Tin_k (1 - a_k), so
+ *   dL/da_k = g_k Tin_k - (S_k + Tf bgdot) / (1 - a_k),
+ *   S_k = sum_{i>k} g_i a_i Tin_i   (an explicit suffix sum here).
+ * `mag` (when given) receives |g_k Tin_k| + (sum_{i>k} |g_i a_i Tin_i| +
+ * |Tf bgdot|) / (1 - a_k): the size of every term summed into dL/da_k (its
+ * conditioning); `suffix` is scratch of m + m entries. */
+static void pixel_alpha_adjoints(int m, const double* a, const double* Tin, const double* g,
+                                 double Tf, double bgdot, double* dalpha, double* mag,
+                                 double* suffix) {
+  double run = 0, size = 0;
+  double* sizes = suffix + m;
+  for (int k = m - 1; k >= 0; --k) {
+    suffix[k] = run;
+    sizes[k] = size;
+    run += g[k] * a[k] * Tin[k];
+    size += fabs(g[k] * a[k] * Tin[k]);
+  }
+  for (int k = 0; k < m; ++k) {
+    double behind = suffix[k] + Tf * bgdot;
+    dalpha[k] = g[k] * Tin[k] - behind / (1 - a[k]);
+    if (mag) mag[k] = fabs(g[k] * Tin[k]) + (sizes[k] + fabs(Tf * bgdot)) / (1 - a[k]);
+  }
+}
+
+/* The per-pixel share of one contributor's screen adjoints given dL/dalpha:
+ * with u = dL/dp = o G dL/dalpha (p the Gaussian's exponent, the 0.99 cap
+ * not differentiated), dL/dQ = -1/2 u d d^T (full matrix entries a, b, c),
+ * dL/dmean = -u Q d (pixels; times W/2, H/2 for NDC), dL/do = G dL/dalpha. */
+static void pixel_screen_adjoints(double dx, double dy, const double conic[3], double o,
+                                  double G, double dal, double W, double H, double out[6]) {
+  double u = o * G * dal;
+  out[0] = -u * (conic[0] * dx + conic[1] * dy) * 0.5 * W;
+  out[1] = -u * (conic[1] * dx + conic[2] * dy) * 0.5 * H;
+  out[2] = -0.5 * u * dx * dx;
+  out[3] = -0.5 * u * dx * dy;
+  out[4] = -0.5 * u * dy * dy;
+  out[5] = G * dal;
+}
+
+/* Sizes of the terms of pixel_screen_adjoints: the same products with
+ * |dL/dalpha| replaced by the size `dal_size` of what it sums and every
+ * product taken by absolute value. */
+static void pixel_term_sizes(double dx, double dy, const double conic[3], double o, double G,
+                             double dal_size, double W, double H, double out[6]) {
+  double u = o * G * dal_size;
+  out[0] = u * (fabs(conic[0] * dx) + fabs(conic[1] * dy)) * 0.5 * W;
+  out[1] = u * (fabs(conic[1] * dx) + fabs(conic[2] * dy)) * 0.5 * H;
+  out[2] = 0.5 * u * dx * dx;
+  out[3] = 0.5 * u * fabs(dx * dy);
+  out[4] = 0.5 * u * dy * dy;
+  out[5] = G * dal_size;
+}
+
 /* Forward + (when dpix != NULL) backward of the whole image.
  * Gradient outputs (may be NULL in forward-only use) are accumulated. */
 static void render(const scene_t* s, double* color, double* invdepth, int* radii,
                    const double* dpix, const double* dinv, double* dmean2d, double* dconic,
-                   double* dop_scaled, double* dcolor, double* dinvdepth) {
+                   double* dop_scaled, double* dcolor, double* dinvdepth, double* const* mags) {
   proj_t* g = calloc((size_t)s->P, sizeof(proj_t));
   for (int i = 0; i < s->P; ++i) {
     project(s, i, &g[i]);
     if (radii) radii[i] = g[i].visible ? g[i].radius : 0;
   }
   int gx = (s->W + TILE - 1) / TILE, gy = (s->H + TILE - 1) / TILE;
-  int* list = malloc(sizeof(int) * (size_t)(s->P > 0 ? s->P : 1));
-  double* alpha_buf = malloc(sizeof(double) * (size_t)(s->P > 0 ? s->P : 1));
-  int* used = malloc(sizeof(int) * (size_t)(s->P > 0 ? s->P : 1));
+  size_t cap = (size_t)(s->P > 0 ? s->P : 1);
+  int* list = malloc(sizeof(int) * cap);
+  int* used = malloc(sizeof(int) * cap);
+  double* alpha = malloc(sizeof(double) * cap);
+  double* Tin = malloc(sizeof(double) * cap);
+  double* gk = malloc(sizeof(double) * cap);
+  double* dal = malloc(sizeof(double) * cap);
+  double* suffix = malloc(2 * sizeof(double) * cap);
+  double* magk = malloc(sizeof(double) * cap);
   for (int ty = 0; ty < gy; ++ty)
     for (int tx = 0; tx < gx; ++tx) {
       int n = 0;
@@ -218,7 +282,7 @@ static void render(const scene_t* s, double* color, double* invdepth, int* radii
       qsort(list, (size_t)n, sizeof(int), by_depth);
       for (int py = ty * TILE; py < (ty + 1) * TILE && py < s->H; ++py)
         for (int px = tx * TILE; px < (tx + 1) * TILE && px < s->W; ++px) {
-          int pix = py * s->W + px, m = 0;
+          int pix = py * s->W + px, m = 0, hw = s->H * s->W;
           double T = 1, C[3] = {0, 0, 0}, D = 0;
           for (int k = 0; k < n; ++k) {
             const proj_t* q = &g[list[k]];
@@ -226,66 +290,70 @@ static void render(const scene_t* s, double* color, double* invdepth, int* radii
             double power = -0.5 * (q->conic[0] * dx * dx + q->conic[2] * dy * dy) -
                            q->conic[1] * dx * dy;
             if (power > 0) continue;
-            double alpha = fmin(0.99, q->opacity * exp(power));
-            if (alpha < 1.0 / 255.0) continue;
-            double tt = T * (1 - alpha);
+            double al = fmin(0.99, q->opacity * exp(power));
+            if (al < 1.0 / 255.0) continue;
+            double tt = T * (1 - al);
             if (tt < 0.0001) break;
-            for (int ch = 0; ch < 3; ++ch) C[ch] += q->rgb[ch] * alpha * T;
-            D += (1.0 / q->depth) * alpha * T;
-            T = tt;
+            for (int ch = 0; ch < 3; ++ch) C[ch] += q->rgb[ch] * al * T;
+            D += (1.0 / q->depth) * al * T;
             used[m] = list[k];
-            alpha_buf[m] = alpha;
+            alpha[m] = al;
+            Tin[m] = T;
             ++m;
+            T = tt;
           }
-          int hw = s->H * s->W;
           for (int ch = 0; ch < 3; ++ch) color[ch * hw + pix] = C[ch] + T * s->bg[ch];
           if (invdepth) invdepth[pix] = D;
           if (!dpix) continue;
-          /* Backward: walk the contributors back to front. */
           double dp[3] = {dpix[pix], dpix[hw + pix], dpix[2 * hw + pix]};
           double di = dinv ? dinv[pix] : 0;
-          double Tf = T, Tc = T, acc[3] = {0, 0, 0}, acc_i = 0, last_a = 0, last_c[3] = {0, 0, 0},
-                 last_i = 0;
           double bgdot = s->bg[0] * dp[0] + s->bg[1] * dp[1] + s->bg[2] * dp[2];
-          for (int k = m - 1; k >= 0; --k) {
+          for (int k = 0; k < m; ++k) {
+            const proj_t* q = &g[used[k]];
+            gk[k] = q->rgb[0] * dp[0] + q->rgb[1] * dp[1] + q->rgb[2] * dp[2] +
+                    di / q->depth;
+          }
+          pixel_alpha_adjoints(m, alpha, Tin, gk, T, bgdot, dal, mags ? magk : NULL, suffix);
+          for (int k = 0; k < m; ++k) {
             int id = used[k];
             const proj_t* q = &g[id];
-            double alpha = alpha_buf[k];
-            double dx = q->px - px, dy = q->py - py;
-            double power = -0.5 * (q->conic[0] * dx * dx + q->conic[2] * dy * dy) -
-                           q->conic[1] * dx * dy;
-            double G = exp(power);
-            Tc = Tc / (1 - alpha);
-            double w = alpha * Tc, dl_dalpha = 0;
-            for (int ch = 0; ch < 3; ++ch) {
-              acc[ch] = last_a * last_c[ch] + (1 - last_a) * acc[ch];
-              last_c[ch] = q->rgb[ch];
-              dl_dalpha += (q->rgb[ch] - acc[ch]) * dp[ch];
-              dcolor[3 * id + ch] += w * dp[ch];
-            }
-            double inv = 1.0 / q->depth;
-            acc_i = last_a * last_i + (1 - last_a) * acc_i;
-            last_i = inv;
-            dl_dalpha += (inv - acc_i) * di;
+            double w = alpha[k] * Tin[k];
+            for (int ch = 0; ch < 3; ++ch) dcolor[3 * id + ch] += w * dp[ch];
             if (dinvdepth) dinvdepth[id] += w * di;
-            dl_dalpha *= Tc;
-            last_a = alpha;
-            dl_dalpha += (-Tf / (1 - alpha)) * bgdot;
-            /* alpha = opacity * G below the 0.99 cap */
-            double dl_dg = q->opacity * dl_dalpha;
-            double gdx = G * dx, gdy = G * dy;
-            dmean2d[3 * id] += dl_dg * (-gdx * q->conic[0] - gdy * q->conic[1]) * 0.5 * s->W;
-            dmean2d[3 * id + 1] += dl_dg * (-gdy * q->conic[2] - gdx * q->conic[1]) * 0.5 * s->H;
-            dconic[4 * id] += -0.5 * gdx * dx * dl_dg;
-            dconic[4 * id + 1] += -0.5 * gdx * dy * dl_dg;
-            dconic[4 * id + 3] += -0.5 * gdy * dy * dl_dg;
-            dop_scaled[id] += G * dl_dalpha;
+            double dx = q->px - px, dy = q->py - py;
+            double G = exp(-0.5 * (q->conic[0] * dx * dx + q->conic[2] * dy * dy) -
+                           q->conic[1] * dx * dy);
+            double sa[6];
+            pixel_screen_adjoints(dx, dy, q->conic, q->opacity, G, dal[k], s->W, s->H, sa);
+            dmean2d[3 * id] += sa[0];
+            dmean2d[3 * id + 1] += sa[1];
+            dconic[4 * id] += sa[2];
+            dconic[4 * id + 1] += sa[3];
+            dconic[4 * id + 3] += sa[4];
+            dop_scaled[id] += sa[5];
+            if (mags) {
+              double sm[6];
+              pixel_term_sizes(dx, dy, q->conic, q->opacity, G, magk[k], s->W, s->H, sm);
+              mags[0][3 * id] += sm[0];
+              mags[0][3 * id + 1] += sm[1];
+              mags[1][4 * id] += sm[2];
+              mags[1][4 * id + 1] += sm[3];
+              mags[1][4 * id + 3] += sm[4];
+              mags[2][id] += sm[5];
+              for (int ch = 0; ch < 3; ++ch) mags[3][3 * id + ch] += fabs(w * dp[ch]);
+              mags[4][id] += fabs(w * di);
+            }
           }
         }
     }
   free(list);
-  free(alpha_buf);
   free(used);
+  free(alpha);
+  free(Tin);
+  free(gk);
+  free(dal);
+  free(suffix);
+  free(magk);
   free(g);
 }
 
@@ -307,38 +375,33 @@ void oracle_raster_forward(int P, int degree, const double* bg, const double* me
                            double* invdepth, int* radii) {
   scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
                          tany, H, W, sh, campos, antialias);
-  render(&s, color, invdepth, radii, NULL, NULL, NULL, NULL, NULL, NULL, NULL);
+  render(&s, color, invdepth, radii, NULL, NULL, NULL, NULL, NULL, NULL, NULL, NULL);
 }
 
 /* Full backward. Outputs (zero-initialised by the caller, P-major like the
  * renderer's): dmean2d [P][3], dconic [P][4], dopacity [P], dcolor [P][3],
  * dinvdepth [P], dmeans [P][3], dcov3d [P][6], dsh [P][48], dscales [P][3],
  * drots [P][4]. */
-void oracle_raster_backward(int P, int degree, const double* bg, const double* means,
-                            const double* opacities, const double* scales, double mod,
-                            const double* rots, const double* view, const double* proj,
-                            double tanx, double tany, int H, int W, const double* sh,
-                            const double* campos, int antialias, const double* dpix,
-                            const double* dinv, double* dmean2d, double* dconic,
-                            double* dopacity, double* dcolor, double* dinvdepth,
-                            double* dmeans, double* dcov3d, double* dsh, double* dscales,
-                            double* drots) {
-  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
-                         tany, H, W, sh, campos, antialias);
-  double* color = malloc(sizeof(double) * 3 * (size_t)H * W);
-  double* dop_scaled = calloc((size_t)(P > 0 ? P : 1), sizeof(double));
-  render(&s, color, NULL, NULL, dpix, dinv, dmean2d, dconic, dop_scaled, dcolor, dinvdepth);
-  free(color);
-  for (int i = 0; i < P; ++i) {
-    proj_t q;
-    project(&s, i, &q);
-    if (!q.visible) continue;
+/* Geometry backward of Gaussian i (visible) as a function of its pixel-stage
+ * adjoints x[10] = (dL/dmean2D x, y (NDC), dL/dconic a, b, c (full-matrix
+ * entries), dL/d(blended opacity), dL/dcolour r, g, b, dL/d(inverse depth)).
+ * Writes y[65] = (dL/dopacity, dL/dmeans [3], dL/dcov3D [6], dL/dsh [48],
+ * dL/dscales [3], dL/drotations [4]); y is linear in x. */
+static void geometry_one(const scene_t* s, int i, const double* x, double* y) {
+  const double *means = s->means, *opacities = s->opacities, *scales = s->scales,
+               *rots = s->rots, *view = s->view, *proj = s->proj, *sh = s->sh;
+  const double mod = s->mod, tanx = s->tanx, tany = s->tany;
+  const int W = s->W, H = s->H, degree = s->degree, antialias = s->antialias;
+  memset(y, 0, sizeof(double) * 65);
+  proj_t q;
+  project(s, i, &q);
+  if (!q.visible) return;
     v3 p = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
     double a0 = q.a0, b = q.b, c0 = q.c0, a = a0 + 0.3, c = c0 + 0.3;
     double det0 = a0 * c0 - b * b, det = a * c - b * b;
     double dl_da = 0, dl_db = 0, dl_dc = 0;
-    double dop = dop_scaled[i];
-    dopacity[i] = dop * q.aa;
+    double dop = x[5];
+    y[0] = dop * q.aa;
     if (antialias) {
       double r = det0 / det;
       if (r > 0.000025) {
@@ -349,7 +412,7 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
       }
     }
     /* conic = inverse([[a, b], [b, c]]); dconic[1] is half the off-diagonal adjoint */
-    double gx = dconic[4 * i], gy = 2 * dconic[4 * i + 1], gz = dconic[4 * i + 3];
+    double gx = x[2], gy = 2 * x[3], gz = x[4];
     double d2 = det * det;
     dl_da += (-c * c * gx + b * c * gy + (det - a * c) * gz) / d2;
     dl_dc += ((det - a * c) * gx + a * b * gy - a * a * gz) / d2;
@@ -363,7 +426,7 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
       for (int cc = r; cc < 3; ++cc, ++k) {
         double f = r == cc ? 1 : 2;
         double sb = r == cc ? A0[r] * A1[r] : A0[r] * A1[cc] + A0[cc] * A1[r];
-        dcov3d[6 * i + k] += f * (A0[r] * A0[cc] * dl_da + A1[r] * A1[cc] * dl_dc) + sb * dl_db;
+        y[4 + k] += f * (A0[r] * A0[cc] * dl_da + A1[r] * A1[cc] * dl_dc) + sb * dl_db;
       }
     /* through A = J W to the camera-space mean */
     double dA0[3], dA1[3];
@@ -383,7 +446,7 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
     double dty = (q.clampy ? 0 : 1) * -fy / (z * z) * dJ12;
     double dtz = -fx / (z * z) * dJ00 - fy / (z * z) * dJ11 + 2 * fx * q.tx / (z * z * z) * dJ02 +
                  2 * fy * q.ty / (z * z * z) * dJ12;
-    dtz += -dinvdepth[i] / (z * z);
+    dtz += -x[9] / (z * z);
     double dm[3];
     for (int kk = 0; kk < 3; ++kk)
       dm[kk] = view[4 * kk] * dtx + view[4 * kk + 1] * dty + view[4 * kk + 2] * dtz;
@@ -392,8 +455,8 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
       double hw = affine_w(proj, p) + 0.0000001;
       v3 h = affine(proj, p);
       for (int kk = 0; kk < 3; ++kk) {
-        dm[kk] += (proj[4 * kk] / hw - proj[4 * kk + 3] * h.x / (hw * hw)) * dmean2d[3 * i] +
-                  (proj[4 * kk + 1] / hw - proj[4 * kk + 3] * h.y / (hw * hw)) * dmean2d[3 * i + 1];
+        dm[kk] += (proj[4 * kk] / hw - proj[4 * kk + 3] * h.x / (hw * hw)) * x[0] +
+                  (proj[4 * kk + 1] / hw - proj[4 * kk + 3] * h.y / (hw * hw)) * x[1];
       }
     }
     /* SH colour */
@@ -402,11 +465,11 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
       sh_basis(q.dir[0], q.dir[1], q.dir[2], bb, gg);
       int nt = (degree + 1) * (degree + 1);
       double gc[3], dd[3] = {0, 0, 0};
-      for (int ch = 0; ch < 3; ++ch) gc[ch] = q.clamped[ch] ? 0 : dcolor[3 * i + ch];
+      for (int ch = 0; ch < 3; ++ch) gc[ch] = q.clamped[ch] ? 0 : x[6 + ch];
       for (int j = 0; j < nt; ++j) {
         double dot = 0;
         for (int ch = 0; ch < 3; ++ch) {
-          dsh[48 * i + 3 * j + ch] += bb[j] * gc[ch];
+          y[10 + 3 * j + ch] += bb[j] * gc[ch];
           dot += sh[48 * i + 3 * j + ch] * gc[ch];
         }
         for (int kk = 0; kk < 3; ++kk) dd[kk] += gg[j][kk] * dot;
@@ -414,12 +477,12 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
       double ds = q.dir[0] * dd[0] + q.dir[1] * dd[1] + q.dir[2] * dd[2];
       for (int kk = 0; kk < 3; ++kk) dm[kk] += (dd[kk] - q.dir[kk] * ds) / q.dist;
     }
-    for (int kk = 0; kk < 3; ++kk) dmeans[3 * i + kk] += dm[kk];
+    for (int kk = 0; kk < 3; ++kk) y[1 + kk] += dm[kk];
     /* Sigma = R diag(s^2) R^T -> scale and rotation */
     {
-      double G[9] = {dcov3d[6 * i], 0.5 * dcov3d[6 * i + 1], 0.5 * dcov3d[6 * i + 2],
-                     0.5 * dcov3d[6 * i + 1], dcov3d[6 * i + 3], 0.5 * dcov3d[6 * i + 4],
-                     0.5 * dcov3d[6 * i + 2], 0.5 * dcov3d[6 * i + 4], dcov3d[6 * i + 5]};
+      double G[9] = {y[4], 0.5 * y[5], 0.5 * y[6],
+                     0.5 * y[5], y[7], 0.5 * y[8],
+                     0.5 * y[6], 0.5 * y[8], y[9]};
       double sc[3] = {mod * scales[3 * i], mod * scales[3 * i + 1], mod * scales[3 * i + 2]};
       double R[9], M[9], dM[9], dR[9];
       rot(rots + 4 * i, R);
@@ -432,7 +495,7 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
           dM[3 * r + cc] = 2 * acc;
         }
       for (int cc = 0; cc < 3; ++cc)
-        dscales[3 * i + cc] += mod * (dM[cc] * R[cc] + dM[3 + cc] * R[3 + cc] + dM[6 + cc] * R[6 + cc]);
+        y[58 + cc] += mod * (dM[cc] * R[cc] + dM[3 + cc] * R[3 + cc] + dM[6 + cc] * R[6 + cc]);
       for (int r = 0; r < 3; ++r)
         for (int cc = 0; cc < 3; ++cc) dR[3 * r + cc] = dM[3 * r + cc] * sc[cc];
       /* dR/dq: numerically exact central difference of the polynomial map
@@ -447,11 +510,77 @@ void oracle_raster_backward(int P, int degree, const double* bg, const double* m
         rot(qp, Rp);
         rot(qm, Rm);
         for (int l = 0; l < 9; ++l) acc += dR[l] * (Rp[l] - Rm[l]) / (2 * h);
-        drots[4 * i + kq] += acc;
+        y[61 + kq] += acc;
       }
     }
   }
+
+void oracle_raster_backward(int P, int degree, const double* bg, const double* means,
+                            const double* opacities, const double* scales, double mod,
+                            const double* rots, const double* view, const double* proj,
+                            double tanx, double tany, int H, int W, const double* sh,
+                            const double* campos, int antialias, const double* dpix,
+                            const double* dinv, double* dmean2d, double* dconic,
+                            double* dopacity, double* dcolor, double* dinvdepth,
+                            double* dmeans, double* dcov3d, double* dsh, double* dscales,
+                            double* drots) {
+  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                         tany, H, W, sh, campos, antialias);
+  double* color = malloc(sizeof(double) * 3 * (size_t)H * W);
+  double* dop_scaled = calloc((size_t)(P > 0 ? P : 1), sizeof(double));
+  render(&s, color, NULL, NULL, dpix, dinv, dmean2d, dconic, dop_scaled, dcolor, dinvdepth,
+         NULL);
+  free(color);
+  for (int i = 0; i < P; ++i) {
+    double x[10] = {dmean2d[3 * i], dmean2d[3 * i + 1], dconic[4 * i], dconic[4 * i + 1],
+                    dconic[4 * i + 3], dop_scaled[i], dcolor[3 * i], dcolor[3 * i + 1],
+                    dcolor[3 * i + 2], dinvdepth[i]};
+    double y[65];
+    proj_t q;
+    project(&s, i, &q);
+    if (!q.visible) continue;
+    geometry_one(&s, i, x, y);
+    dopacity[i] = y[0];
+    for (int k = 0; k < 3; ++k) dmeans[3 * i + k] += y[1 + k];
+    for (int k = 0; k < 6; ++k) dcov3d[6 * i + k] += y[4 + k];
+    for (int k = 0; k < 48; ++k) dsh[48 * i + k] += y[10 + k];
+    for (int k = 0; k < 3; ++k) dscales[3 * i + k] += y[58 + k];
+    for (int k = 0; k < 4; ++k) drots[4 * i + k] += y[61 + k];
+  }
   free(dop_scaled);
+}
+
+/* The pixel stage of the backward with the sizes of its sums, and the
+ * geometry stage as a per-Gaussian linear map, for tolerances that follow the
+ * conditioning of each adjoint. Outputs (zeroed by the caller): the pixel
+ * stage's adjoints x_mean2d [P][3] (NDC), x_conic [P][4], x_opacity [P] (of
+ * the blended opacity), x_color [P][3], x_invdepth [P]; the same shapes
+ * `size_*` holding the sums of absolute values of the terms added into each;
+ * and jac [P][65][10], the geometry map of geometry_one (zero rows for
+ * invisible Gaussians). */
+void oracle_raster_backward_sized(int P, int degree, const double* bg, const double* means,
+                                  const double* opacities, const double* scales, double mod,
+                                  const double* rots, const double* view, const double* proj,
+                                  double tanx, double tany, int H, int W, const double* sh,
+                                  const double* campos, int antialias, const double* dpix,
+                                  const double* dinv, double* x_mean2d, double* x_conic,
+                                  double* x_opacity, double* x_color, double* x_invdepth,
+                                  double* size_mean2d, double* size_conic, double* size_opacity,
+                                  double* size_color, double* size_invdepth, double* jac) {
+  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                         tany, H, W, sh, campos, antialias);
+  double* color = malloc(sizeof(double) * 3 * (size_t)H * W);
+  double* const mags[5] = {size_mean2d, size_conic, size_opacity, size_color, size_invdepth};
+  render(&s, color, NULL, NULL, dpix, dinv, x_mean2d, x_conic, x_opacity, x_color, x_invdepth,
+         mags);
+  free(color);
+  for (int i = 0; i < P; ++i)
+    for (int k = 0; k < 10; ++k) {
+      double e[10] = {0}, y[65];
+      e[k] = 1;
+      geometry_one(&s, i, e, y);
+      for (int r = 0; r < 65; ++r) jac[((size_t)i * 65 + r) * 10 + k] = y[r];
+    }
 }
 
 /* The scalar loss sum(dpix * colour) + sum(dinv * inverse depth), for
@@ -473,4 +602,140 @@ double oracle_raster_loss(int P, int degree, const double* bg, const double* mea
   free(color);
   free(inv);
   return L;
+}
+
+/* ------------------------------------------------------------------------
+ * Pixel stage of already projected 2D Gaussians on selected tiles (the
+ * 1920x1080 pixel-backward configuration, checked on a sample of tiles).
+ *
+ * Inputs are the float32 values the CUDA path reads: mean2d [P][2] pixels,
+ * conic_opacity [P][4] (a, b, c, opacity), rgb [P][3], depth [P], radii [P].
+ * Each tile's list is built here from the 3-sigma rectangles (every Gaussian
+ * whose rectangle covers the tile), ordered by (float depth, index); the
+ * CUDA path keeps only tiles its alpha footprint reaches, and the extra
+ * entries here contribute nothing. For the pixels of the `ntiles` tiles
+ * listed in `tiles` (tile index ty * grid_x + tx) it writes colour [3][H][W]
+ * and final transmittance [H][W], and accumulates the adjoints of every
+ * Gaussian from those pixels only: dmean2d [P][2] (NDC, as the renderer
+ * reports), dconic [P][3] (a, b, c), dopacity [P] (of the opacity the blend
+ * used), dcolor [P][3]. mag_* (same shapes) accumulate the absolute values
+ * of the per-pixel terms with both parts of dL/dalpha taken by size: the
+ * size of what the float sums add up (their conditioning).
+ *
+ * Contribution decisions are taken in double; the CUDA path takes them in
+ * float with a fast exponential, so where a decision sits within rounding of
+ * its threshold the two may differ. Such Gaussians are flagged in
+ * `ambiguous` [P]: an alpha within 1e-5 (relative) of 1/255 or an exponent
+ * within 1e-6 of 0 flags that Gaussian; a transmittance stop within 1e-4
+ * (relative) of 1e-4 flags every Gaussian of that pixel's list up to the stop.
+ * Returns 0, or -1 when memory runs out. */
+static const float* g_tile_depth;
+static int by_float_depth(const void* a, const void* b) {
+  int i = *(const int*)a, j = *(const int*)b;
+  float di = g_tile_depth[i], dj = g_tile_depth[j];
+  if (di != dj) return di < dj ? -1 : 1;
+  return i < j ? -1 : (i > j);
+}
+
+int oracle_pixel_tiles(int P, const float* mean2d, const float* conic_opacity, const float* rgb,
+                       const float* depth, const int* radii, int W, int H, const double* bg,
+                       int ntiles, const int* tiles, const double* dpix, double* color,
+                       double* final_t, double* dmean2d, double* dconic, double* dopacity,
+                       double* dcolor, double* mag_mean2d, double* mag_conic,
+                       double* mag_opacity, double* mag_color, unsigned char* ambiguous) {
+  int gx = (W + TILE - 1) / TILE, gy = (H + TILE - 1) / TILE, hw = W * H;
+  size_t cap = (size_t)(P > 0 ? P : 1);
+  int* list = malloc(sizeof(int) * cap);
+  int* used = malloc(sizeof(int) * cap);
+  double* alpha = malloc(sizeof(double) * cap);
+  double* Tin = malloc(sizeof(double) * cap);
+  double* gk = malloc(sizeof(double) * cap);
+  double* dal = malloc(sizeof(double) * cap);
+  double* mag = malloc(sizeof(double) * cap);
+  double* suffix = malloc(2 * sizeof(double) * cap);
+  if (!list || !used || !alpha || !Tin || !gk || !dal || !mag || !suffix) {
+    free(list); free(used); free(alpha); free(Tin); free(gk); free(dal); free(mag);
+    free(suffix);
+    return -1;
+  }
+  g_tile_depth = depth;
+  for (int t = 0; t < ntiles; ++t) {
+    int tx = tiles[t] % gx, ty = tiles[t] / gx, n = 0;
+    if (ty >= gy) continue;
+    for (int i = 0; i < P; ++i) {
+      int r = radii[i];
+      if (r <= 0) continue;
+      double mx = mean2d[2 * i], my = mean2d[2 * i + 1];
+      int x0 = (int)fmin(gx, fmax(0, (int)((mx - r) / TILE)));
+      int y0 = (int)fmin(gy, fmax(0, (int)((my - r) / TILE)));
+      int x1 = (int)fmin(gx, fmax(0, (int)((mx + r + TILE - 1) / TILE)));
+      int y1 = (int)fmin(gy, fmax(0, (int)((my + r + TILE - 1) / TILE)));
+      if (tx >= x0 && tx < x1 && ty >= y0 && ty < y1) list[n++] = i;
+    }
+    qsort(list, (size_t)n, sizeof(int), by_float_depth);
+    for (int py = ty * TILE; py < (ty + 1) * TILE && py < H; ++py)
+      for (int px = tx * TILE; px < (tx + 1) * TILE && px < W; ++px) {
+        int pix = py * W + px, m = 0;
+        double T = 1, C[3] = {0, 0, 0};
+        for (int k = 0; k < n; ++k) {
+          int id = list[k];
+          const float* co = conic_opacity + 4 * id;
+          double dx = (double)mean2d[2 * id] - px, dy = (double)mean2d[2 * id + 1] - py;
+          double power = -0.5 * ((double)co[0] * dx * dx + (double)co[2] * dy * dy) -
+                         (double)co[1] * dx * dy;
+          if (fabs(power) <= 1e-6) ambiguous[id] = 1;
+          if (power > 0) continue;
+          double al = fmin(0.99, (double)co[3] * exp(power));
+          if (fabs(al * 255.0 - 1.0) <= 1e-5) ambiguous[id] = 1;
+          if (al < 1.0 / 255.0) continue;
+          double tt = T * (1 - al);
+          if (fabs(tt / 0.0001 - 1.0) <= 1e-4) {
+            for (int j = 0; j <= k; ++j) ambiguous[list[j]] = 1;
+          }
+          if (tt < 0.0001) break;
+          for (int ch = 0; ch < 3; ++ch) C[ch] += rgb[3 * id + ch] * al * T;
+          used[m] = id;
+          alpha[m] = al;
+          Tin[m] = T;
+          ++m;
+          T = tt;
+        }
+        for (int ch = 0; ch < 3; ++ch) color[ch * hw + pix] = C[ch] + T * bg[ch];
+        final_t[pix] = T;
+        double dp[3] = {dpix[pix], dpix[hw + pix], dpix[2 * hw + pix]};
+        double bgdot = bg[0] * dp[0] + bg[1] * dp[1] + bg[2] * dp[2];
+        for (int k = 0; k < m; ++k) {
+          const float* c = rgb + 3 * used[k];
+          gk[k] = c[0] * dp[0] + c[1] * dp[1] + c[2] * dp[2];
+        }
+        pixel_alpha_adjoints(m, alpha, Tin, gk, T, bgdot, dal, mag, suffix);
+        for (int k = 0; k < m; ++k) {
+          int id = used[k];
+          const float* co = conic_opacity + 4 * id;
+          double q[3] = {co[0], co[1], co[2]};
+          double w = alpha[k] * Tin[k];
+          for (int ch = 0; ch < 3; ++ch) {
+            dcolor[3 * id + ch] += w * dp[ch];
+            mag_color[3 * id + ch] += fabs(w * dp[ch]);
+          }
+          double dx = (double)mean2d[2 * id] - px, dy = (double)mean2d[2 * id + 1] - py;
+          double G = exp(-0.5 * (q[0] * dx * dx + q[2] * dy * dy) - q[1] * dx * dy);
+          double sa[6], sm[6];
+          pixel_screen_adjoints(dx, dy, q, co[3], G, dal[k], W, H, sa);
+          pixel_term_sizes(dx, dy, q, co[3], G, mag[k], W, H, sm);
+          dmean2d[2 * id] += sa[0];
+          dmean2d[2 * id + 1] += sa[1];
+          mag_mean2d[2 * id] += sm[0];
+          mag_mean2d[2 * id + 1] += sm[1];
+          for (int e = 0; e < 3; ++e) {
+            dconic[3 * id + e] += sa[2 + e];
+            mag_conic[3 * id + e] += sm[2 + e];
+          }
+          dopacity[id] += sa[5];
+          mag_opacity[id] += sm[5];
+        }
+      }
+  }
+  free(list); free(used); free(alpha); free(Tin); free(gk); free(dal); free(mag); free(suffix);
+  return 0;
 }

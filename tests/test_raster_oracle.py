@@ -55,3 +55,24 @@ def test_raster_oracle_empty_scene_is_background():
     for ch in range(3):
         assert np.allclose(color[ch], scene["bg"][ch])
     assert np.allclose(inv, 0)
+
+
+def test_geometry_map_reproduces_the_backward():
+    """The per-Gaussian geometry map (used to carry the pixel stage's
+    tolerance to the geometry adjoints) applied to the pixel-stage adjoints
+    gives the oracle's full backward."""
+    scene = oracle.raster_scene(120, 40, 56, seed=9, antialiasing=True)
+    rng = np.random.default_rng(4)
+    dpix = rng.standard_normal((3, 40, 56)) * 0.1
+    dinv = rng.standard_normal((40, 56)) * 0.01
+    full = oracle.raster_backward(scene, dpix, dinv)
+    sized = oracle.raster_backward_sized(scene, dpix, dinv)
+    np.testing.assert_allclose(sized["x_mean2d"], full["dmean2d"], rtol=1e-12, atol=1e-15)
+    np.testing.assert_allclose(sized["x_color"], full["dcolor"], rtol=1e-12, atol=1e-15)
+    y = np.einsum("prk,pk->pr", sized["jac"], oracle.geometry_inputs(sized))
+    for name, rows in oracle.GEOMETRY_ROWS.items():
+        ref = full[name].reshape(len(y), -1)
+        np.testing.assert_allclose(y[:, rows], ref, rtol=1e-9, atol=1e-12 * np.abs(ref).max())
+    sizes = oracle.geometry_input_sizes(sized)
+    x = oracle.geometry_inputs(sized)
+    assert (sizes >= np.abs(x) * (1 - 1e-12)).all()
