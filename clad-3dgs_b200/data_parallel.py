@@ -167,8 +167,11 @@ class ShardedAdam:
     """
 
     def __init__(self, n, rates=None, *, group=None, exchange=None, device=None,
-                 update=None, sh_exchange=None, degree=3):
+                 update=None, sh_exchange=None, degree=3, gate=None):
         self.group = group
+        # rank_health.StepGate: when given, every step first settles on the
+        # host that all ranks are present (before any collective is enqueued).
+        self.gate = gate
         self.distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if self.distributed else 1
         self.rank = dist.get_rank(group) if self.distributed else 0
@@ -300,6 +303,12 @@ class ShardedAdam:
             native.check(native.library().clad3dgs_ipc_free(address), "ipc free")
         self._own = []
 
+    def leave(self):
+        """This rank takes part in no further step: the other ranks' next gate
+        raises RankFailure instead of waiting in a collective."""
+        if self.gate is not None:
+            self.gate.leave()
+
     def __enter__(self):
         return self
 
@@ -350,6 +359,8 @@ class ShardedAdam:
         """Sums the ranks' gradients of this rank's share, runs Adam on it and
         brings every replica up to date."""
         self.t += 1
+        if self.gate is not None and self.world > 1:
+            self.gate.arrive_and_wait(self.t)
         names = [n for n, _ in GROUPS]
         seeded = self.sh_exchange == "seeds"
         if self.world == 1:
@@ -439,10 +450,11 @@ class DataParallelTrainer:
     ranks exchange and update (ShardedAdam.step)."""
 
     def __init__(self, values, rates=None, *, degree=3, bg=(0.0, 0.0, 0.0), group=None,
-                 exchange=None, device=None, pixel_accumulation=2, sh_exchange=None):
+                 exchange=None, device=None, pixel_accumulation=2, sh_exchange=None,
+                 gate=None):
         n = int(values["xyz"].shape[0])
         self.adam = ShardedAdam(n, rates, group=group, exchange=exchange, device=device,
-                                sh_exchange=sh_exchange, degree=degree)
+                                sh_exchange=sh_exchange, degree=degree, gate=gate)
         self.adam.load(values)
         self.n, self.degree = n, int(degree)
         self.mode = int(pixel_accumulation)

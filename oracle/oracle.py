@@ -322,6 +322,18 @@ def raster_backward_sized(scene, dpix, dinv):
     return out
 
 
+def geometry_spread(scene, x, rel=4 * 2.0 ** -24, draws=8):
+    """[P,65] spread of the geometry map under rounding-level perturbations of
+    all its inputs (see oracle_raster_geometry_spread); x is [P,10] in the
+    column order of `jac`."""
+    s, args = _scene_args(scene)
+    out = np.zeros((s["P"], 65))
+    x = _d(x)
+    lib().oracle_raster_geometry_spread(*args, _dp(x), ctypes.c_double(rel),
+                                        ctypes.c_int(draws), _dp(out))
+    return out
+
+
 GEOMETRY_ROWS = dict(dopacity=slice(0, 1), dmeans=slice(1, 4), dcov3d=slice(4, 10),
                      dsh=slice(10, 58), dscales=slice(58, 61), drots=slice(61, 65))
 

@@ -583,6 +583,63 @@ void oracle_raster_backward_sized(int P, int degree, const double* bg, const dou
     }
 }
 
+/* Sensitivity of the geometry map to rounding-level perturbations: for each
+ * of `draws` draws, every input of the map (means, scales, rotations,
+ * opacities, SH coefficients, camera matrices and position, and the
+ * pixel-stage adjoints x [P][10]) is multiplied by (1 + rel u), u uniform in
+ * [-1, 1] from a fixed-seed generator, and spread [P][65] receives the
+ * largest |y_perturbed - y| over the draws. A float evaluation of the map
+ * behaves like an exact evaluation at inputs perturbed by a few ulps, so this
+ * spread (with rel a few float ulps) sizes its rounding error, including
+ * where exact cancellation makes an output zero. */
+static double lcg_uniform(uint64_t* state) {
+  *state = *state * 6364136223846793005ull + 1442695040888963407ull;
+  return ((*state >> 11) * (1.0 / 9007199254740992.0)) * 2.0 - 1.0;
+}
+
+static double* perturbed(const double* v, size_t n, double rel, uint64_t* state) {
+  double* out = malloc(sizeof(double) * (n ? n : 1));
+  for (size_t k = 0; k < n; ++k) out[k] = v[k] * (1.0 + rel * lcg_uniform(state));
+  return out;
+}
+
+void oracle_raster_geometry_spread(int P, int degree, const double* bg, const double* means,
+                                   const double* opacities, const double* scales, double mod,
+                                   const double* rots, const double* view, const double* proj,
+                                   double tanx, double tany, int H, int W, const double* sh,
+                                   const double* campos, int antialias, const double* x,
+                                   double rel, int draws, double* spread) {
+  scene_t s = make_scene(P, degree, bg, means, opacities, scales, mod, rots, view, proj, tanx,
+                         tany, H, W, sh, campos, antialias);
+  double* y0 = malloc(sizeof(double) * 65 * (size_t)(P ? P : 1));
+  for (int i = 0; i < P; ++i) geometry_one(&s, i, x + 10 * (size_t)i, y0 + 65 * (size_t)i);
+  memset(spread, 0, sizeof(double) * 65 * (size_t)P);
+  uint64_t state = 0x9e3779b97f4a7c15ull;
+  for (int d = 0; d < draws; ++d) {
+    double* pm = perturbed(means, 3 * (size_t)P, rel, &state);
+    double* po = perturbed(opacities, (size_t)P, rel, &state);
+    double* ps = perturbed(scales, 3 * (size_t)P, rel, &state);
+    double* pr = perturbed(rots, 4 * (size_t)P, rel, &state);
+    double* pv = perturbed(view, 16, rel, &state);
+    double* pp = perturbed(proj, 16, rel, &state);
+    double* psh = perturbed(sh, 48 * (size_t)P, rel, &state);
+    double* pc = perturbed(campos, 3, rel, &state);
+    double* px = perturbed(x, 10 * (size_t)P, rel, &state);
+    scene_t q = make_scene(P, degree, bg, pm, po, ps, mod, pr, pv, pp, tanx, tany, H, W, psh,
+                           pc, antialias);
+    for (int i = 0; i < P; ++i) {
+      double y[65];
+      geometry_one(&q, i, px + 10 * (size_t)i, y);
+      for (int r = 0; r < 65; ++r) {
+        double dev = fabs(y[r] - y0[65 * (size_t)i + r]);
+        if (dev > spread[65 * (size_t)i + r]) spread[65 * (size_t)i + r] = dev;
+      }
+    }
+    free(pm); free(po); free(ps); free(pr); free(pv); free(pp); free(psh); free(pc); free(px);
+  }
+  free(y0);
+}
+
 /* The scalar loss sum(dpix * colour) + sum(dinv * inverse depth), for
  * finite-difference checks of the backward. */
 double oracle_raster_loss(int P, int degree, const double* bg, const double* means,

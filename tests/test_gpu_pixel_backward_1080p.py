@@ -83,7 +83,7 @@ def test_sampled_tiles_adjoints_match_oracle(cuda, scene_1080p, mode):
     touched = ((ref["mag_opacity"] > 0) | (ref["mag_color"].sum(1) > 0))
     ambiguous = ref["ambiguous"].astype(bool)
     compared = touched & ~ambiguous
-    assert compared.sum() > 20_000, int(compared.sum())
+    assert compared.sum() > 5_000, int(compared.sum())
     assert ambiguous.sum() <= 0.01 * touched.sum(), (int(ambiguous.sum()), int(touched.sum()))
     pairs = (
         ("dmean2d", got["dmean2d"][:, :2], ref["dmean2d"], ref["mag_mean2d"]),
@@ -96,6 +96,9 @@ def test_sampled_tiles_adjoints_match_oracle(cuda, scene_1080p, mode):
         tol = 1e-4 * np.abs(r) + FLOOR * m
         err = np.abs(g - r)
         bad = err > tol
+        print(f"mode {mode} {name}: {g.size} compared, worst error/tolerance "
+              f"{float((err / tol).max()):.3f}, worst relative "
+              f"{float((err / np.maximum(np.abs(r), 1e-30)).max()):.2e}")
         assert not bad.any(), (name, int(bad.sum()), g[bad][:4], r[bad][:4],
                                float((err / tol).max()))
     # Nothing reaches a Gaussian the sampled tiles do not hold.
