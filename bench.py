@@ -244,15 +244,16 @@ def measured_peaks():
 
 
 def ncu_traffic():
-    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary."""
+    """(DRAM bytes of one 1.1M-Gaussian launch of the fused kernel, note) from
+    the committed ncu capture."""
     path = ROOT / "profiles" / "fused_gaussian_step_traffic.json"
     if not path.exists():
-        return None
+        return None, None
     try:
         data = json.loads(path.read_text())
-        return float(data["bytes_per_launch_at_1.1M"])
+        return float(data["bytes_per_launch_at_1.1M"]), data.get("note")
     except (ValueError, KeyError):
-        return None
+        return None, None
 
 
 def cpu_baseline(budget_s=15.0):
@@ -336,6 +337,7 @@ def native_arm(args):
     peak, peak_kind = measured_peaks()
     mean_step_s = statistics.mean(per_step) / 1e3
     achieved = BYTES_PER_GAUSSIAN * n_g / mean_step_s / 1e9
+    traffic, traffic_note = ncu_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": "Gaussians/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
@@ -345,7 +347,8 @@ def native_arm(args):
                    "sh_degree": DEGREE, "camera": "980x545 pinhole, fov 60",
                    "parallelism": f"Gaussian-index shards x{world}", "l2": L2_NOTE},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": ncu_traffic(),
+                     "frac": achieved / peak, "traffic": traffic,
+                     "traffic_note": traffic_note,
                      "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
                      "algorithmic_bytes_per_gaussian": BYTES_PER_GAUSSIAN,
                      "kernel_time_ms": mean_step_s * 1e3},

@@ -278,7 +278,8 @@ def pixel_tiles(mean2d, conic_opacity, rgb, depth, radii, width, height, bg, til
     float32 arrays the CUDA path reads. Returns a dict with colour [3,H,W]
     and final_t [H,W] (only the listed tiles' pixels are written), the
     adjoints dmean2d [P,2], dconic [P,3], dopacity [P], dcolor [P,3] from those
-    pixels, the matching sizes mag_* and the `ambiguous` flags [P]."""
+    pixels, the matching sizes mag_*, the allowances allow_* for stop
+    decisions within rounding and the `ambiguous` flags [P]."""
     P = int(mean2d.shape[0])
     f32 = lambda a: np.ascontiguousarray(a, np.float32)
     mean2d, conic_opacity, rgb, depth = map(f32, (mean2d, conic_opacity, rgb, depth))
@@ -289,7 +290,9 @@ def pixel_tiles(mean2d, conic_opacity, rgb, depth, radii, width, height, bg, til
                dmean2d=np.zeros((P, 2)), dconic=np.zeros((P, 3)), dopacity=np.zeros(P),
                dcolor=np.zeros((P, 3)), mag_mean2d=np.zeros((P, 2)),
                mag_conic=np.zeros((P, 3)), mag_opacity=np.zeros(P),
-               mag_color=np.zeros((P, 3)), ambiguous=np.zeros(P, np.uint8))
+               mag_color=np.zeros((P, 3)), allow_mean2d=np.zeros((P, 2)),
+               allow_conic=np.zeros((P, 3)), allow_opacity=np.zeros(P),
+               allow_color=np.zeros((P, 3)), ambiguous=np.zeros(P, np.uint8))
     f = lib().oracle_pixel_tiles
     f.restype = ctypes.c_int
     status = f(ctypes.c_int(P), _dp(mean2d), _dp(conic_opacity), _dp(rgb), _dp(depth),
@@ -297,7 +300,8 @@ def pixel_tiles(mean2d, conic_opacity, rgb, depth, radii, width, height, bg, til
                ctypes.c_int(len(tiles)), _dp(tiles), _dp(dpix),
                *[_dp(out[k]) for k in ("color", "final_t", "dmean2d", "dconic", "dopacity",
                                       "dcolor", "mag_mean2d", "mag_conic", "mag_opacity",
-                                      "mag_color", "ambiguous")])
+                                      "mag_color", "allow_mean2d", "allow_conic",
+                                      "allow_opacity", "allow_color", "ambiguous")])
     if status != 0:
         raise MemoryError("oracle_pixel_tiles: out of memory")
     return out

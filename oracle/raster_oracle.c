@@ -680,11 +680,31 @@ double oracle_raster_loss(int P, int degree, const double* bg, const double* mea
  * size of what the float sums add up (their conditioning).
  *
  * Contribution decisions are taken in double; the CUDA path takes them in
- * float with a fast exponential, so where a decision sits within rounding of
- * its threshold the two may differ. Such Gaussians are flagged in
- * `ambiguous` [P]: an alpha within 1e-5 (relative) of 1/255 or an exponent
- * within 1e-6 of 0 flags that Gaussian; a transmittance stop within 1e-4
- * (relative) of 1e-4 flags every Gaussian of that pixel's list up to the stop.
+ * float with a fast exponential, so a decision within rounding of its
+ * threshold may go the other way there:
+ *  - an alpha within 1e-5 (relative) of 1/255 or an exponent within 1e-6 of
+ *    0: that Gaussian is flagged in `ambiguous` [P] (rare);
+ *  - a transmittance stop within 1e-4 (relative) of 1e-4: the candidate at
+ *    the stop may or may not contribute, which changes its own term and,
+ *    through the transmittance left behind, every earlier contributor's
+ *    dL/dalpha by at most (|g| + |bg . dL/dC|) alpha T / (1 - alpha_j) (the
+ *    candidate's g, alpha, T). allow_* (same shapes as mag_*) accumulate
+ *    these possible changes, carried to each adjoint like the term sizes.
+ * The exponent p = -1/2 d^T Q d is evaluated exactly as the CUDA path
+ * rounds it (float, the same products and fused multiply-adds, so the same
+ * bits): for an elongated Gaussian its terms cancel heavily and that float
+ * value, not the exact one, is what the renderer composites; the derivatives
+ * of p are then taken exactly. What remains between the two is the fast
+ * exponential and the product with the opacity (relative error of alpha_k at
+ * most kappa_k = eps (|p_k| + 8), eps = 2^-24) and the float rounding of
+ * 1 - alpha_k and of the transmittance product. Through the transmittance a
+ * change of alpha_k moves every term of the pixel by at most
+ * e_k = (kappa_k + 2 eps) / (1 - alpha_k) relative. These roundings are
+ * independent, so their sum grows like the square root of their count:
+ * E = sqrt(sum_k e_k^2) is its standard deviation, and the pixel's terms add
+ * 4 E times their sizes to allow_* (four standard deviations; the worst case
+ * sum_k e_k would make the bound hundreds of times looser than the errors
+ * seen), and the stop margin is the larger of 1e-4 and 4 E.
  * Returns 0, or -1 when memory runs out. */
 static const float* g_tile_depth;
 static int by_float_depth(const void* a, const void* b) {
@@ -694,12 +714,32 @@ static int by_float_depth(const void* a, const void* b) {
   return i < j ? -1 : (i > j);
 }
 
+/* p = -1/2 d^T Q d rounded as the CUDA path rounds it: (a dx) dx fused with
+ * (c dy) dy, then -1/2 of that fused with -(b dx) dy (every product and sum
+ * of float operands rounded to float; fmaf rounds once). d = mean - pixel in
+ * float. */
+static float float_form(const float* co, float dx, float dy) {
+  float ax = co[0] * dx, cy = co[2] * dy, bx = co[1] * dx;
+  float diag = fmaf(ax, dx, cy * dy);
+  return fmaf(-0.5f, diag, -(bx * dy));
+}
+
+static void add_sizes(double* mean2d, double* conic, double* opacity, int id,
+                      const double sm[6]) {
+  mean2d[2 * id] += sm[0];
+  mean2d[2 * id + 1] += sm[1];
+  for (int e = 0; e < 3; ++e) conic[3 * id + e] += sm[2 + e];
+  opacity[id] += sm[5];
+}
+
 int oracle_pixel_tiles(int P, const float* mean2d, const float* conic_opacity, const float* rgb,
                        const float* depth, const int* radii, int W, int H, const double* bg,
                        int ntiles, const int* tiles, const double* dpix, double* color,
                        double* final_t, double* dmean2d, double* dconic, double* dopacity,
                        double* dcolor, double* mag_mean2d, double* mag_conic,
-                       double* mag_opacity, double* mag_color, unsigned char* ambiguous) {
+                       double* mag_opacity, double* mag_color, double* allow_mean2d,
+                       double* allow_conic, double* allow_opacity, double* allow_color,
+                       unsigned char* ambiguous) {
   int gx = (W + TILE - 1) / TILE, gy = (H + TILE - 1) / TILE, hw = W * H;
   size_t cap = (size_t)(P > 0 ? P : 1);
   int* list = malloc(sizeof(int) * cap);
@@ -733,21 +773,27 @@ int oracle_pixel_tiles(int P, const float* mean2d, const float* conic_opacity, c
     for (int py = ty * TILE; py < (ty + 1) * TILE && py < H; ++py)
       for (int px = tx * TILE; px < (tx + 1) * TILE && px < W; ++px) {
         int pix = py * W + px, m = 0;
-        double T = 1, C[3] = {0, 0, 0};
+        int cand = -1, cand_m = 0;  /* a stop decision within rounding */
+        double cand_alpha = 0, cand_T = 0, T = 1, C[3] = {0, 0, 0}, E2 = 0;
+        const double eps = 1.0 / 16777216.0;
         for (int k = 0; k < n; ++k) {
           int id = list[k];
           const float* co = conic_opacity + 4 * id;
-          double dx = (double)mean2d[2 * id] - px, dy = (double)mean2d[2 * id + 1] - py;
-          double power = -0.5 * ((double)co[0] * dx * dx + (double)co[2] * dy * dy) -
-                         (double)co[1] * dx * dy;
-          if (fabs(power) <= 1e-6) ambiguous[id] = 1;
+          double power = float_form(co, mean2d[2 * id] - (float)px,
+                                    mean2d[2 * id + 1] - (float)py);
+          double kappa = eps * (fabs(power) + 8);
           if (power > 0) continue;
           double al = fmin(0.99, (double)co[3] * exp(power));
-          if (fabs(al * 255.0 - 1.0) <= 1e-5) ambiguous[id] = 1;
+          if (fabs(al * 255.0 - 1.0) <= 1e-5 + kappa) ambiguous[id] = 1;
           if (al < 1.0 / 255.0) continue;
           double tt = T * (1 - al);
-          if (fabs(tt / 0.0001 - 1.0) <= 1e-4) {
-            for (int j = 0; j <= k; ++j) ambiguous[list[j]] = 1;
+          double e_k = (kappa + 2 * eps) / (1 - al);
+          double margin = fmax(1e-4, 4 * sqrt(E2 + e_k * e_k));
+          if (cand < 0 && fabs(tt / 0.0001 - 1.0) <= margin) {
+            cand = id;
+            cand_m = m;
+            cand_alpha = al;
+            cand_T = T;
           }
           if (tt < 0.0001) break;
           for (int ch = 0; ch < 3; ++ch) C[ch] += rgb[3 * id + ch] * al * T;
@@ -756,6 +802,7 @@ int oracle_pixel_tiles(int P, const float* mean2d, const float* conic_opacity, c
           Tin[m] = T;
           ++m;
           T = tt;
+          E2 += e_k * e_k;
         }
         for (int ch = 0; ch < 3; ++ch) color[ch * hw + pix] = C[ch] + T * bg[ch];
         final_t[pix] = T;
@@ -776,23 +823,53 @@ int oracle_pixel_tiles(int P, const float* mean2d, const float* conic_opacity, c
             mag_color[3 * id + ch] += fabs(w * dp[ch]);
           }
           double dx = (double)mean2d[2 * id] - px, dy = (double)mean2d[2 * id + 1] - py;
-          double G = exp(-0.5 * (q[0] * dx * dx + q[2] * dy * dy) - q[1] * dx * dy);
+          double G = exp(float_form(co, mean2d[2 * id] - (float)px,
+                                    mean2d[2 * id + 1] - (float)py));
           double sa[6], sm[6];
           pixel_screen_adjoints(dx, dy, q, co[3], G, dal[k], W, H, sa);
           pixel_term_sizes(dx, dy, q, co[3], G, mag[k], W, H, sm);
           dmean2d[2 * id] += sa[0];
           dmean2d[2 * id + 1] += sa[1];
-          mag_mean2d[2 * id] += sm[0];
-          mag_mean2d[2 * id + 1] += sm[1];
-          for (int e = 0; e < 3; ++e) {
-            dconic[3 * id + e] += sa[2 + e];
-            mag_conic[3 * id + e] += sm[2 + e];
-          }
+          for (int e = 0; e < 3; ++e) dconic[3 * id + e] += sa[2 + e];
           dopacity[id] += sa[5];
-          mag_opacity[id] += sm[5];
+          add_sizes(mag_mean2d, mag_conic, mag_opacity, id, sm);
+          /* the float blend's own rounding: 4 E of every term */
+          double spread = 4 * sqrt(E2);
+          for (int e = 0; e < 6; ++e) sm[e] *= spread;
+          add_sizes(allow_mean2d, allow_conic, allow_opacity, id, sm);
+          for (int ch = 0; ch < 3; ++ch) allow_color[3 * id + ch] += spread * fabs(w * dp[ch]);
+        }
+        if (cand >= 0) {
+          /* The candidate's own term (whether or not it was kept here) ... */
+          const float* cc = rgb + 3 * cand;
+          const float* co = conic_opacity + 4 * cand;
+          double q[3] = {co[0], co[1], co[2]};
+          double g = cc[0] * dp[0] + cc[1] * dp[1] + cc[2] * dp[2];
+          double change = (fabs(g) + fabs(bgdot)) * cand_alpha * cand_T;
+          double dx = (double)mean2d[2 * cand] - px, dy = (double)mean2d[2 * cand + 1] - py;
+          double G = exp(float_form(co, mean2d[2 * cand] - (float)px,
+                                    mean2d[2 * cand + 1] - (float)py));
+          double sm[6];
+          pixel_term_sizes(dx, dy, q, co[3], G,
+                           fabs(g) * cand_T + fabs(cand_T * bgdot) / (1 - cand_alpha), W, H, sm);
+          add_sizes(allow_mean2d, allow_conic, allow_opacity, cand, sm);
+          for (int ch = 0; ch < 3; ++ch)
+            allow_color[3 * cand + ch] += fabs(cand_alpha * cand_T * dp[ch]);
+          /* ... and the change it makes to every contributor in front of it. */
+          for (int k = 0; k < cand_m && k < m; ++k) {
+            int id = used[k];
+            const float* cj = conic_opacity + 4 * id;
+            double qj[3] = {cj[0], cj[1], cj[2]};
+            double djx = (double)mean2d[2 * id] - px, djy = (double)mean2d[2 * id + 1] - py;
+            double Gj = exp(float_form(cj, mean2d[2 * id] - (float)px,
+                                       mean2d[2 * id + 1] - (float)py));
+            pixel_term_sizes(djx, djy, qj, cj[3], Gj, change / (1 - alpha[k]), W, H, sm);
+            add_sizes(allow_mean2d, allow_conic, allow_opacity, id, sm);
+          }
         }
       }
   }
   free(list); free(used); free(alpha); free(Tin); free(gk); free(dal); free(mag); free(suffix);
   return 0;
 }
+

@@ -10,10 +10,12 @@ tiles' pixels, which the oracle computes with its own tile lists (3-sigma
 rectangles, depth order) and stored transmittances. Compared elementwise
 with |got - ref| <= 1e-4 |ref| + 3e-5 x (sum of |terms| of that element),
 the floor being the float error of a sum relative to the size of its terms
-(see test_gpu_rasterizer.py). Gaussians touched by a contribution decision
-within rounding of its threshold (alpha near 1/255, exponent near 0, a
-transmittance stop near 1e-4) can legitimately differ between float and
-double and are left out; their count is bounded. Every Gaussian outside the
+(see test_gpu_rasterizer.py). A contribution decision within rounding of its
+threshold can go either way in float: where a transmittance stop lies
+within 1e-4 of 1e-4, the oracle adds to each affected Gaussian's tolerance
+the most that decision can change (its allow_* arrays); Gaussians with an
+alpha within rounding of 1/255 or an exponent within rounding of 0 are left
+out, and their count is bounded (0.5% of those compared). Every Gaussian outside the
 sampled tiles must come out exactly zero. All three accumulation modes are
 checked, and the sampled pixels' colours match within 1e-5.
 """
@@ -84,16 +86,17 @@ def test_sampled_tiles_adjoints_match_oracle(cuda, scene_1080p, mode):
     ambiguous = ref["ambiguous"].astype(bool)
     compared = touched & ~ambiguous
     assert compared.sum() > 5_000, int(compared.sum())
-    assert ambiguous.sum() <= 0.01 * touched.sum(), (int(ambiguous.sum()), int(touched.sum()))
+    assert ambiguous.sum() <= 0.005 * touched.sum(), (int(ambiguous.sum()), int(touched.sum()))
     pairs = (
-        ("dmean2d", got["dmean2d"][:, :2], ref["dmean2d"], ref["mag_mean2d"]),
-        ("dconic", got["dconic"][:, [0, 1, 3]], ref["dconic"], ref["mag_conic"]),
-        ("dopacity", got["dopacity"], ref["dopacity"], ref["mag_opacity"]),
-        ("dcolor", got["dcolor"], ref["dcolor"], ref["mag_color"]),
+        ("dmean2d", got["dmean2d"][:, :2], "dmean2d", "mean2d"),
+        ("dconic", got["dconic"][:, [0, 1, 3]], "dconic", "conic"),
+        ("dopacity", got["dopacity"], "dopacity", "opacity"),
+        ("dcolor", got["dcolor"], "dcolor", "color"),
     )
-    for name, g, r, m in pairs:
-        g, r, m = g[compared], r[compared], m[compared]
-        tol = 1e-4 * np.abs(r) + FLOOR * m
+    for name, g, key, part in pairs:
+        g, r = g[compared], ref[key][compared]
+        m, a = ref["mag_" + part][compared], ref["allow_" + part][compared]
+        tol = 1e-4 * np.abs(r) + FLOOR * m + a
         err = np.abs(g - r)
         bad = err > tol
         print(f"mode {mode} {name}: {g.size} compared, worst error/tolerance "
