@@ -91,63 +91,84 @@ def dist_env():
 # Clock sampling during the measurement.
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and throttle reasons of one GPU, sampled every 2 ms from
+    a background thread through NVML (read-only queries) across warm-up and the
+    timed loop; `timed()` marks the timed window, and the summary covers the
+    samples inside it when there are at least three, else every sample under
+    load. Falls back to nothing (reason "NVML unavailable") without NVML."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = (Path(os.environ.get("TMPDIR", "/tmp"))
-                     / f"clocks_{os.getpid()}_{id(self):x}.csv")
+    # NVML clocks-event-reason bits.
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int, period_s: float = 0.002):
+        self.index, self.period = index, period_s
+        self.rows, self.window = [], [None, None]
+        self.handle = self.thread = None
+        self.stop = False
+
+    def _open(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.index)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except pynvml.NVMLError:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        return pynvml, handle
+
+    def _run(self, nvml, handle):
+        while not self.stop:
+            try:
+                self.rows.append((time.monotonic(),
+                                  nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM),
+                                  nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0,
+                                  nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+            except nvml.NVMLError:
+                pass
+            time.sleep(self.period)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.out = self.path.open("w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
-                stdout=self.out, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            nvml, self.handle = self._open()
+        except Exception:  # no NVML on this machine
+            self.handle = None
+            return self
+        self.thread = threading.Thread(target=self._run, args=(nvml, self.handle), daemon=True)
+        self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.out.close()
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def timed(self, begin: bool):
+        """Marks the start (True) or end (False) of the timed region."""
+        self.window[0 if begin else 1] = time.monotonic()
 
     def summary(self):
-        if self.proc is None or not self.path.exists():
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
-                                 power=float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
-                                 hw=parts[5], hwt=parts[6], swt=parts[7], cap=parts[8]))
-            except ValueError:
-                continue
-        self.path.unlink(missing_ok=True)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [r for r in rows if r["power"] > 200] or rows
-        reasons = set()
-        for r in loaded:
-            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
-                              ("swt", "sw_thermal_slowdown"), ("cap", "sw_power_cap")):
-                if r[key].lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
-                "sm_max_mhz": max(r["smax"] for r in rows),
-                "reasons": sorted(reasons), "samples": len(loaded)}
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML unavailable"]}
+        lo, hi = self.window
+        inside = [r for r in self.rows if lo is not None and hi is not None and lo <= r[0] <= hi]
+        window = "timed region"
+        if len(inside) < 3:
+            inside = [r for r in self.rows if r[2] > 200] or list(self.rows)
+            window = "warm-up and timed region"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        reasons = sorted({name for r in inside for bit, name in self.REASONS.items()
+                          if r[3] & bit})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(inside), "window": window,
+                "power_w_median": statistics.median(r[2] for r in inside), "source": "NVML"}
 
 
 # ---------------------------------------------------------------------------
@@ -235,6 +256,13 @@ def run_step(consume, s, t):
                           act_rates=a["rates"], act_bias1=[b1] * 3, act_bias2=[b2] * 3)
 
 
+def fused_config(gaussians_per_gpu, world):
+    """The `config` of the fused-step line (the same in both arms)."""
+    return {"workload": WORKLOAD, "gaussians_per_gpu": gaussians_per_gpu, "sh_degree": DEGREE,
+            "camera": "980x545 pinhole, fov 60",
+            "parallelism": f"Gaussian-index shards x{world}", "l2": L2_NOTE}
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -299,12 +327,14 @@ def native_arm(args):
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
         events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        clocks.timed(True)
         events[0].record(stream)
         for k in range(args.steps):
             t += 1
             run_step(consume, state, t)
             events[k + 1].record(stream)
         torch.cuda.synchronize()
+        clocks.timed(False)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -343,9 +373,7 @@ def native_arm(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+f64",
         "data": "synthetic (seeded; distributions of the fused-step configuration)",
-        "config": {"workload": WORKLOAD, "gaussians_per_gpu": n_g,
-                   "sh_degree": DEGREE, "camera": "980x545 pinhole, fov 60",
-                   "parallelism": f"Gaussian-index shards x{world}", "l2": L2_NOTE},
+        "config": fused_config(n_g, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "traffic_note": traffic_note,
@@ -403,12 +431,53 @@ def e2e_measurement(args, device, consume):
     end.record()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    h2d = H2D_BYTES_PER_GAUSSIAN * N_GAUSSIANS + 12
+    d2h = D2H_BYTES_PER_GAUSSIAN * N_GAUSSIANS
+    ceiling = pcie_ceiling(device)
+    # Both directions run concurrently, so the step cannot be shorter than the
+    # slower direction at the measured concurrent copy rates.
+    floor_ms = max(h2d / ceiling["both_h2d_gbs"], d2h / ceiling["both_d2h_gbs"]) / 1e6
     return {"value": N_GAUSSIANS * steps / (ms / 1e3), "unit": "Gaussians/s",
-            "h2d_bytes_per_step": H2D_BYTES_PER_GAUSSIAN * N_GAUSSIANS + 12,
-            "d2h_bytes_per_step": D2H_BYTES_PER_GAUSSIAN * N_GAUSSIANS,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "ms_per_step": ms / steps,
+            "pcie": dict(ceiling, copy_floor_ms=floor_ms, frac_of_copy_floor=floor_ms / (ms / steps)),
             "path": f"clad3dgs_gaussian_step_host (C ABI), pinned host buffers, {chunk:,}-"
                     "Gaussian chunks on 3 streams"}
+
+
+def pcie_ceiling(device, nbytes=512 << 20, reps=5):
+    """Pinned host<->device copy rates (GB/s): each direction alone and both at
+    once on two streams (cudaMemcpyAsync through torch), best of `reps`."""
+    import torch
+
+    host_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    host_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev_in = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev_out = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def timed(fn):
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        return best
+
+    def both():
+        with torch.cuda.stream(s1):
+            dev_in.copy_(host_in, non_blocking=True)
+        with torch.cuda.stream(s2):
+            host_out.copy_(dev_out, non_blocking=True)
+
+    t_h2d = timed(lambda: dev_in.copy_(host_in, non_blocking=True))
+    t_d2h = timed(lambda: host_out.copy_(dev_out, non_blocking=True))
+    t_both = timed(both)
+    return {"h2d_gbs": nbytes / t_h2d / 1e9, "d2h_gbs": nbytes / t_d2h / 1e9,
+            "both_h2d_gbs": nbytes / t_both / 1e9, "both_d2h_gbs": nbytes / t_both / 1e9,
+            "bytes_per_copy": nbytes}
 
 
 def reference_arm(args):
@@ -426,15 +495,15 @@ def reference_arm(args):
     n = int(min(N_GAUSSIANS, max(1024, budget / per_g)))
     res = torch_cpu_path.time_cpu_path(n, steps=args.steps, warmup=args.warmup)
     sample = (f"{n} Gaussians per step (of {N_GAUSSIANS}), {args.steps} timed steps after "
-              f"{args.warmup} warm-up; torch CPU eval_sh + autograd + torch.optim.Adam")
+              f"{args.warmup} warm-up, on the host cores of rank 0; torch CPU eval_sh + "
+              "autograd + torch.optim.Adam")
     line = {
         "impl": "reference", "metric": METRIC, "value": res["gaussians_per_s"],
         "unit": "Gaussians/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["total_s"] * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; distributions of the fused-step configuration)",
-        "config": {"workload": WORKLOAD, "gaussians_per_gpu": N_GAUSSIANS, "sh_degree": DEGREE,
-                   "parallelism": "host cores of rank 0"},
+        "config": fused_config(N_GAUSSIANS, world),
         "cpu_baseline": {"value": res["gaussians_per_s"], "unit": "Gaussians/s",
                          "cores": res["threads"], "kind": "port", "sample": sample},
         "e2e": {"value": res["gaussians_per_s"], "unit": "Gaussians/s",
@@ -646,10 +715,13 @@ def measure_train_step(args, steps, warmup, with_e2e):
                 first_loss = float(loss.item())
         bracket()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        clocks.timed(True)
         ev[0].record(stream)
         for _ in range(steps):
             loss, instances = step_once()
         ev[1].record(stream)
+        torch.cuda.synchronize()
+        clocks.timed(False)
         bracket()
     step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps, "step_ms")
     last_loss = float(loss.item())

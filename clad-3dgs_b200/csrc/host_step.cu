@@ -211,8 +211,13 @@ std::mutex g_static_lock;
 void* g_static_address[64] = {};  // device address of g_static_staging, per device
 
 // Largest multiple of 64 Gaussians whose staging set and camera fit the array.
+// The results go back from the same slots the inputs came in, so a chunk needs
+// the staged bytes once: start from the array size over the bytes per
+// Gaussian and step down past the slot padding.
 int64_t static_chunk_limit() {
-  int64_t chunk = (CLAD3DGS_STATIC_STAGING_BYTES / 1451) / 64 * 64;
+  size_t per_gaussian = 0;
+  for (int s = 0; s < S_COUNT; ++s) per_gaussian += kSlotWidth[s] * slot_elem(s);
+  int64_t chunk = int64_t(CLAD3DGS_STATIC_STAGING_BYTES / per_gaussian) / 64 * 64;
   while (chunk > 0 && set_bytes(chunk) + kAlign > CLAD3DGS_STATIC_STAGING_BYTES)
     chunk -= 64;
   return chunk;
@@ -249,18 +254,29 @@ extern "C" int clad3dgs_gaussian_step_host_static(
   if (e != cudaSuccess) return clad3dgs::fail(CLAD3DGS_CUDA_ERROR, cudaGetErrorString(e));
   char* ws = nullptr;
   {
-    // Set-up, once per device with that device current: the array's name is
-    // only a host-side handle; its device address comes from the runtime.
+    // The array's name is only a host-side handle; its device address comes
+    // from the runtime, with this device current. It is looked up again on
+    // every call made outside a stream capture (so a call after a device reset
+    // gets the new context's address); a call inside a capture uses the
+    // address of the last call outside one, so the first call on a device
+    // must come before any capture.
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &capture);
+    if (e != cudaSuccess) return clad3dgs::fail(CLAD3DGS_CUDA_ERROR, cudaGetErrorString(e));
     std::lock_guard<std::mutex> guard(g_static_lock);
     void*& address = g_static_address[dev & 63];
-    if (address == nullptr) {
-      e = cudaGetSymbolAddress(&address, g_static_staging);
-      if (e != cudaSuccess) {
-        address = nullptr;
+    if (capture == cudaStreamCaptureStatusNone) {
+      void* current = nullptr;
+      e = cudaGetSymbolAddress(&current, g_static_staging);
+      if (e != cudaSuccess)
         return clad3dgs::fail(CLAD3DGS_CUDA_ERROR,
                               std::string("static staging address: ") +
                                   cudaGetErrorString(e));
-      }
+      address = current;
+    } else if (address == nullptr) {
+      return clad3dgs::fail(CLAD3DGS_INVALID_ARGUMENT,
+                            "static host step: the first call on a device must come "
+                            "before any stream capture");
     }
     ws = static_cast<char*>(address);
   }

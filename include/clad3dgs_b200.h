@@ -351,8 +351,12 @@ int clad3dgs_raster_forward_2d(int P, const float* mean2d, const float* conic_op
  * CLAD3DGS_INVALID_ARGUMENT (the message gives the limit), as is a chunk that is
  * not a multiple of 64. Copies and kernels run on `stream` only (no streams or
  * events are created); the call returns when the results are in host memory.
- * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture. Every call
+ * Each call made outside a stream capture looks up the array's device address
+ * (with that device current), so calls after a device reset work; a call inside
+ * a capture reuses the address of the last call outside one, so make the first
+ * call on a device before any stream capture. The largest chunk is about 65K
+ * Gaussians (767 staged bytes per Gaussian: results go back from the slots
+ * their inputs came in). Every call
  * on a device shares the one array, so calls that overlap on the GPU (from two
  * host threads or two streams) race; nothing in it needs clearing, since each
  * call copies in every staged byte it reads. */

@@ -90,3 +90,67 @@ def test_host_buffer_pipeline_bit_exact(cuda, n, chunk):
     for k in ("params", "first", "second"):
         for j in range(3):
             assert _bits_equal(ha[k][j].numpy(), want_act[k][j]), (k, j)
+
+
+def _saved_of(params):
+    """Saved activations of the current raw parameters (|q|, exp(scale),
+    sigmoid(opacity)), as the activation forward produces them."""
+    rot, scl, opa = params
+    norm = np.sqrt((rot.astype(np.float64) ** 2).sum(1, keepdims=True)).astype(np.float32)
+    sig = (1 / (1 + np.exp(-opa.astype(np.float64)))).astype(np.float32)
+    return [norm, np.exp(scl).astype(np.float32), sig]
+
+
+def test_thirty_consecutive_steps_at_full_size(cuda):
+    """The fused-step configuration: 1,100,000 Gaussians, SH degree 3 +
+    activations, 30 consecutive steps from a fresh Adam state (bias
+    corrections of steps 1..30, moments carried over), new upstream adjoints
+    each step and the saved activations of the current parameters. After every
+    step every parameter, moment and dm must equal the oracle's bit for bit."""
+    import consume
+
+    n, steps = 1_100_000, 30
+    sh = cases.sh_problem(n, seed=42, moments=False)
+    act = cases.activation_problem(n, seed=43, moments=False)
+    d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(cuda) for k, v in sh.items()}
+    da = {k: [torch.from_numpy(np.ascontiguousarray(x)).to(cuda) for x in act[k]]
+          for k in ("params", "seeds", "saved", "first", "second")}
+    ref = {k: sh[k].copy() for k in cases.SH_KEYS}
+    ref_act = {k: [x.copy() for x in act[k]] for k in ("params", "first", "second")}
+    rng = np.random.default_rng(44)
+    for t in range(1, steps + 1):
+        seed = (rng.standard_normal((n, 3)) * 1e-3).astype(np.float32)
+        dm = (rng.standard_normal((n, 3)) * 1e-4).astype(np.float32)
+        act_seeds = [(rng.standard_normal(p.shape) * 1e-4).astype(np.float32)
+                     for p in ref_act["params"]]
+        saved = _saved_of(ref_act["params"])
+        d["seed"].copy_(torch.from_numpy(seed))
+        d["dm"].copy_(torch.from_numpy(dm))
+        for j in range(3):
+            da["seeds"][j].copy_(torch.from_numpy(act_seeds[j]))
+            da["saved"][j].copy_(torch.from_numpy(saved[j]))
+        b1, b2 = cases.bias(t)
+        consume.gaussian_step(d["means"], d["radii"], d["clamped"], d["camera"], d["seed"],
+                              d["dm"], d["dc"], d["rest"], d["dc_first"], d["dc_second"],
+                              d["rest_first"], d["rest_second"], bias1=b1, bias2_sqrt=b2,
+                              degree=3, act_parameters=da["params"], act_seeds=da["seeds"],
+                              act_saved=da["saved"], act_first=da["first"],
+                              act_second=da["second"], act_rates=act["rates"],
+                              act_bias1=[b1] * 3, act_bias2=[b2] * 3)
+        ref["dm"] = dm.copy()
+        oracle.sh_consume("split_torch_adam", 3, sh["means"], sh["radii"], sh["clamped"],
+                          sh["camera"], seed, ref["dm"], dc=ref["dc"], rest=ref["rest"],
+                          dc_first=ref["dc_first"], dc_second=ref["dc_second"],
+                          rest_first=ref["rest_first"], rest_second=ref["rest_second"],
+                          bias1=b1, bias2_sqrt=b2)
+        oracle.activation_consume(ref_act["params"], act_seeds,
+                                  [saved[0].reshape(-1).copy(), saved[1],
+                                   saved[2].reshape(-1).copy()],
+                                  ref_act["first"], ref_act["second"], act["rates"],
+                                  [b1] * 3, [b2] * 3)
+        torch.cuda.synchronize()
+        for k in cases.SH_KEYS:
+            assert _bits_equal(d[k].cpu().numpy(), ref[k]), (t, k)
+        for k in ("params", "first", "second"):
+            for j in range(3):
+                assert _bits_equal(da[k][j].cpu().numpy(), ref_act[k][j]), (t, k, j)

@@ -96,3 +96,52 @@ def test_static_step_rejects_chunks_beyond_the_fixed_array(cuda):
         assert status == native.INVALID_ARGUMENT
         assert b"staging" in lib.clad3dgs_last_error()
     assert _identical(_snapshot(*state[:2]), before)
+
+
+def _static_limit(lib, native, state):
+    """The largest chunk the fixed array takes, as the rejection message states."""
+    import re
+
+    head, cfg, arrays, rates, b1, b2 = _arguments(*state, 1)
+    status = lib.clad3dgs_gaussian_step_host_static(1000, 3, *head, cfg, *arrays, rates,
+                                                    b1, b2, 1 << 22, 0)
+    assert status == native.INVALID_ARGUMENT
+    return int(re.search(rb"up to (\d+)", lib.clad3dgs_last_error()).group(1))
+
+
+def test_static_step_at_its_chunk_limit(cuda):
+    """A chunk exactly at the limit runs and matches the workspace step bit for
+    bit; one step of 64 above it is refused before anything is written. The
+    limit uses the array's 48 MiB: about 65K Gaussians at 767 staged bytes each."""
+    import consume
+    import _native as native
+
+    lib = native.library()
+    probe = _host_state(1000, seed=6)
+    limit = _static_limit(lib, native, probe)
+    per_gaussian = 767
+    assert limit % 64 == 0
+    staging = 48 << 20  # CLAD3DGS_STATIC_STAGING_BYTES
+    assert limit * per_gaussian <= staging
+    assert (limit + 128) * per_gaussian > staging - 64 * 256
+    n = limit + 1000  # two chunks: one full, one partial
+    static_state = _host_state(n, seed=31)
+    workspace_state = _host_state(n, seed=31)
+    head, cfg, arrays, rates, b1, b2 = _arguments(*static_state, 1)
+    status = lib.clad3dgs_gaussian_step_host_static(n, 3, *head, cfg, *arrays, rates,
+                                                    b1, b2, limit + 64, 0)
+    assert status == native.INVALID_ARGUMENT
+    assert _identical(_snapshot(*static_state[:2]), _snapshot(*workspace_state[:2]))
+    stream = torch.cuda.current_stream().cuda_stream
+    status = lib.clad3dgs_gaussian_step_host_static(n, 3, *head, cfg, *arrays, rates,
+                                                    b1, b2, limit, stream)
+    assert status == native.OK, lib.clad3dgs_last_error()
+    ws_chunk = 8192
+    workspace = torch.empty(consume.host_step_workspace(ws_chunk), dtype=torch.uint8,
+                            device=cuda)
+    head, cfg, arrays, rates, b1, b2 = _arguments(*workspace_state, 1)
+    status = lib.clad3dgs_gaussian_step_host(n, 3, *head, cfg, *arrays, rates, b1, b2,
+                                             workspace.data_ptr(), workspace.numel(),
+                                             ws_chunk, stream)
+    assert status == native.OK, lib.clad3dgs_last_error()
+    assert _identical(_snapshot(*static_state[:2]), _snapshot(*workspace_state[:2]))
