@@ -578,6 +578,27 @@ def pixel_backward_arm(args):
     ms = results[modes[0]]
     names = {2: "converged_warp_reduction", 1: "full_warp_only (reference helper)",
              0: "per_lane_atomics"}
+    # Atomics of one pass (a counting pass replays the walk's contribution
+    # test; it is not timed). Nine adjoint fields without an inverse-depth
+    # adjoint: colour 3, screen mean 2, conic 3, opacity 1.
+    fields = 9
+    counts = rasterizer.count_accumulation_2d(state)
+    per_mode = {0: counts["pairs"] * fields, 1: counts["mode1_per_field"] * fields,
+                2: counts["mode2_reductions"] * fields}
+    atomics = {
+        "contributing_pairs": counts["pairs"],
+        "reference_sites_times_pairs": 8 * counts["pairs"],
+        "per_lane_atomics_mode0": per_mode[0],
+        "full_warp_only_atomics_mode1": per_mode[1],
+        "converged_reduction_instructions_mode2": counts["mode2_reductions"],
+        "converged_reduction_atomics_mode2": per_mode[2],
+        "atomics_per_pass": per_mode[modes[0]],
+        "atomics_per_s": per_mode[modes[0]] / (ms / 1e3),
+        "atomic_instructions_per_s": (counts["mode2_reductions"] if modes[0] == 2
+                                      else per_mode[modes[0]]) / (ms / 1e3),
+        "note": "lane-level atomic operations per pass; mode 2 issues one multi-lane "
+                "atomic instruction per (warp, Gaussian) covering all nine fields",
+    }
     line = {
         "metric": "rasterizer pixel backward, Gaussians/s (1920x1080, one pass over every "
                   "2D Gaussian)",
@@ -589,6 +610,7 @@ def pixel_backward_arm(args):
                                "T stop 1e-4, dL/dpixel N(0,1e-3)",
                    "tile_instances": num, "accumulation_mode": modes[0],
                    "ms_per_mode": {names[m]: results[m] for m in modes}},
+        "atomics": atomics,
         "roofline": {"bound": "hbm", "limiter": "instruction issue and latency (the ncu "
                                                 "summary of this kernel: DRAM < 1% of peak)",
                      "achieved": algorithmic / (ms / 1e3) / 1e9,

@@ -81,6 +81,7 @@ _SIGNATURES = {
                                 + [c_int, _P, _P, _P, _P, _P, POINTER(c_int), _P]),
     "clad3dgs_raster_render_backward": (c_int, [c_int, c_int, c_int] + [_P] * 3 + [c_int]
                                         + [_P] * 8 + [c_int, _P]),
+    "clad3dgs_raster_count_accumulation": (c_int, [c_int] * 3 + [_P] * 2 + [c_int] + [_P] * 3),
     "clad3dgs_warp_accumulate_probe": (c_int, [c_int] * 3 + [_P] * 4 + [c_int, _P]
                                        + [c_int] * 3 + [_P]),
     "clad3dgs_raster_backward": (c_int, [c_int, c_int] + [_P] * 6 + [c_float] + [_P] * 4

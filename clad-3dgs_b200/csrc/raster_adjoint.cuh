@@ -83,17 +83,16 @@ __device__ __forceinline__ void walk_begin(PixelWalk& s, int px, int py, int wid
 }
 
 // Gaussian number `index` of the tile list (back to front), at offset
-// d = mean - pixel from this pixel. Adds the pixel's share to f (moment form)
-// and returns whether it contributed.
-__device__ __forceinline__ bool walk_step(PixelWalk& s, uint32_t index, float dx, float dy,
-                                          float4 co, const float* rgb3, float invdepth,
-                                          float f[16]) {
-  if (index >= s.last) return false;
-  const float p = gauss_power(co, dx, dy);
-  if (p > 0.f) return false;
+// d = mean - pixel from this pixel, p its exponent there (gauss_power). Adds
+// the pixel's share to f (moment form) and returns whether it contributed.
+// The exponential is taken whether or not the pixel is live, so a walk over
+// several pixels branches once per pixel.
+__device__ __forceinline__ bool walk_step(PixelWalk& s, uint32_t index, float p, float dx,
+                                          float dy, float4 co, const float* rgb3,
+                                          float invdepth, float f[16]) {
   const float G = __expf(p);
   const float alpha = fminf(kMaxAlpha, co.w * G);
-  if (alpha < kMinAlpha) return false;
+  if (!(index < s.last && p <= 0.f && alpha >= kMinAlpha)) return false;
   const float keep_inv = 1.f / (1.f - alpha);
   s.T *= keep_inv;                       // T_k from T_{k+1}
   const float w = alpha * s.T;           // the Gaussian's blend weight here

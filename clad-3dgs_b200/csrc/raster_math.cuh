@@ -125,13 +125,29 @@ __device__ __forceinline__ void covariance2d(const Projection2& P, const float c
 }
 
 // Exponent p = -1/2 d^T Q d of a Gaussian at offset d = (dx, dy) = mean -
-// pixel, Q = [[co.x, co.y], [co.y, co.z]]. Every rounding is explicit, so the
-// forward compositing and the backward walk (which must replay the forward's
-// contribution decisions exactly) get the same bits whatever the compiler
-// contracts elsewhere.
+// pixel, Q = [[co.x, co.y], [co.y, co.z]], as a quadratic in dy whose
+// coefficients depend only on the pixel column:
+//     p = c2 dy^2 + c1 dy + c0,  c2 = -co.z / 2, c1 = -co.y dx, c0 = -co.x dx^2 / 2,
+// evaluated by Horner's rule. A thread that shades several rows of one column
+// forms (c0, c1, c2) once per Gaussian and spends two fused multiply-adds per
+// pixel. Every rounding is explicit, so the forward compositing and the
+// backward walk (which must replay the forward's contribution decisions
+// exactly) get the same bits whatever the compiler contracts elsewhere.
+struct ColumnForm {
+  float c0, c1, c2;
+};
+
+__device__ __forceinline__ ColumnForm column_form(float4 co, float dx) {
+  return {__fmul_rn(-0.5f, __fmul_rn(__fmul_rn(co.x, dx), dx)), -__fmul_rn(co.y, dx),
+          -0.5f * co.z};
+}
+
+__device__ __forceinline__ float row_power(const ColumnForm& f, float dy) {
+  return __fmaf_rn(__fmaf_rn(f.c2, dy, f.c1), dy, f.c0);
+}
+
 __device__ __forceinline__ float gauss_power(float4 co, float dx, float dy) {
-  const float diag = __fmaf_rn(__fmul_rn(co.x, dx), dx, __fmul_rn(__fmul_rn(co.z, dy), dy));
-  return __fmaf_rn(-0.5f, diag, -__fmul_rn(__fmul_rn(co.y, dx), dy));
+  return row_power(column_form(co, dx), dy);
 }
 
 __device__ __forceinline__ float ndc_to_pixel(float v, int size) {

@@ -805,7 +805,8 @@ __global__ void __launch_bounds__(kTilePixels)
       for (int q = 0; q < 16; ++q) f[q] = 0.f;
       const float4 co = s.co[j];
       const uint32_t index = uint32_t(todo - 1 - (base + j));
-      if (!walk_step(pixel, index, s.xy[j].x - fx, s.xy[j].y - fy, co, s.rgb + 3 * j,
+      const float dx = s.xy[j].x - fx, dy = s.xy[j].y - fy;
+      if (!walk_step(pixel, index, gauss_power(co, dx, dy), dx, dy, co, s.rgb + 3 * j,
                      s.inv[j], f))
         continue;
       finish_moments(f, co, half_w, half_h);
@@ -830,7 +831,13 @@ constexpr int kPixelsPerThread = CLAD3DGS_PIXELS_PER_THREAD;
 constexpr int kPairThreads = kTilePixels / kPixelsPerThread;
 constexpr int kRowStep = kTileY / kPixelsPerThread;
 
-__global__ void __launch_bounds__(kPairThreads)
+// Twelve resident 64-thread blocks per SM (at most 85 registers a thread): the
+// measured best at 1080p/3M (1.30 ms against 1.43 ms unconstrained at 93
+// registers and 1.37 ms at 64).
+#ifndef CLAD3DGS_PAIR_MIN_BLOCKS
+#define CLAD3DGS_PAIR_MIN_BLOCKS 12
+#endif
+__global__ void __launch_bounds__(kPairThreads, CLAD3DGS_PAIR_MIN_BLOCKS)
     render_backward_pairs_kernel(const uint2* __restrict__ ranges,
                                  const uint32_t* __restrict__ point_list, int width,
                                  int height, int grid_x, const float* __restrict__ bg,
@@ -876,17 +883,90 @@ __global__ void __launch_bounds__(kPairThreads)
       const float4 co = s.co[j];
       const uint32_t index = uint32_t(todo - 1 - (base + j));
       const float dx = xy.x - fx;
+      const ColumnForm column = column_form(co, dx);
       bool any = false;
 #pragma unroll
-      for (int r = 0; r < kPixelsPerThread; ++r)
-        any = walk_step(pixel[r], index, dx, xy.y - (float)(py + r * kRowStep), co,
-                        s.rgb + 3 * j, s.inv[j], f) || any;
+      for (int r = 0; r < kPixelsPerThread; ++r) {
+        const float dy = xy.y - (float)(py + r * kRowStep);
+        any = walk_step(pixel[r], index, row_power(column, dy), dx, dy, co, s.rgb + 3 * j,
+                        s.inv[j], f) || any;
+      }
       if (!__any_sync(0xffffffffu, any)) continue;
       finish_moments(f, co, half_w, half_h);
       const uint32_t id = s.id[j];
       accumulate_converged(f, fields, lane, [&](int q) { return field_address(out, id, q); });
     }
   }
+}
+
+// Counting pass of the pixel backward (not part of it): replays the walk's
+// contribution test, one pixel per thread in the 256-thread layout of modes 0
+// and 1, and tallies per tile
+//   counts[0] contributing (pixel, Gaussian) pairs (mode 0 issues one atomic
+//             per pair and field);
+//   counts[1] mode 1's atomics per field: per (warp, Gaussian) 1 when all 32
+//             lanes contribute, else the contributing lanes;
+//   counts[2] mode 2's warp reductions (one 9- or 10-lane atomic instruction
+//             each): per (warp of the four-pixels-per-thread layout, Gaussian)
+//             with any contributing lane. That warp holds pixel rows
+//             {0,1,4,5,8,9,12,13} (warp 0) or {2,3,6,7,10,11,14,15} (warp 1)
+//             of the tile, i.e. the one-pixel warps w with w % 2 equal to it.
+__global__ void __launch_bounds__(kTilePixels)
+    count_accumulation_kernel(const uint2* __restrict__ ranges,
+                              const uint32_t* __restrict__ point_list, int width, int height,
+                              int grid_x, const float2* __restrict__ mean2d,
+                              const float4* __restrict__ conic_opacity,
+                              const uint32_t* __restrict__ n_contrib,
+                              unsigned long long* __restrict__ counts) {
+  static_assert(kTilePixels == 256 && kPixelsPerThread == 4, "counting layout");
+  const int tile = blockIdx.y * grid_x + blockIdx.x;
+  const int px = blockIdx.x * kTileX + threadIdx.x % kTileX;
+  const int py = blockIdx.y * kTileY + threadIdx.x / kTileX;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool inside = px < width && py < height;
+  const uint32_t last = inside ? n_contrib[py * width + px] : 0;
+  const uint2 range = ranges[tile];
+  __shared__ uint32_t s_max;
+  __shared__ float2 s_xy[kBatch];
+  __shared__ float4 s_co[kBatch];
+  __shared__ unsigned char s_any[kBatch][8];  // per Gaussian of the batch and warp
+  const int todo = block_walk_length(last, &s_max);
+  const float fx = (float)px, fy = (float)py;
+  unsigned long long pairs = 0, whole_or_lanes = 0, reductions = 0;
+  for (int base = 0; base < todo; base += kBatch) {
+    __syncthreads();
+    const int k = base + threadIdx.x;
+    if (k < todo) {
+      const uint32_t id = point_list[range.x + todo - k - 1];
+      s_xy[threadIdx.x] = mean2d[id];
+      s_co[threadIdx.x] = conic_opacity[id];
+    }
+    __syncthreads();
+    const int count = min(kBatch, todo - base);
+    for (int j = 0; j < count; ++j) {
+      const uint32_t index = uint32_t(todo - 1 - (base + j));
+      const float4 co = s_co[j];
+      const float p = gauss_power(co, s_xy[j].x - fx, s_xy[j].y - fy);
+      const float alpha = fminf(kMaxAlpha, co.w * __expf(p));
+      const bool live = index < last && p <= 0.f && alpha >= kMinAlpha;
+      const unsigned lanes = __ballot_sync(0xffffffffu, live);
+      if (lane == 0) {
+        pairs += __popc(lanes);
+        whole_or_lanes += lanes == 0xffffffffu ? 1u : __popc(lanes);
+        s_any[j][warp] = lanes != 0u;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < count) {
+      const unsigned char* a = s_any[threadIdx.x];
+      reductions += (a[0] | a[2] | a[4] | a[6]) + (a[1] | a[3] | a[5] | a[7]);
+    }
+  }
+  if (lane == 0 && (pairs || whole_or_lanes)) {
+    atomicAdd(counts, pairs);
+    atomicAdd(counts + 1, whole_or_lanes);
+  }
+  if (reductions) atomicAdd(counts + 2, reductions);
 }
 
 // Test probe of the accumulation helpers above on caller-given lane streams:
@@ -1364,6 +1444,28 @@ extern "C" int clad3dgs_raster_render_backward(
         img.ranges, point_list, width, height, gx, bg, g.mean2d, g.conic_opacity, g.rgb,
         g.depth, img.final_t, img.n_contrib, dpixels, dinvdepth_pixels, o);
   return status_of(cudaPeekAtLastError(), "pixel backward");
+}
+
+extern "C" int clad3dgs_raster_count_accumulation(int P, int width, int height,
+                                                  const void* geom_buffer,
+                                                  const void* binning_buffer,
+                                                  int num_rendered, const void* image_buffer,
+                                                  unsigned long long* counts,
+                                                  cudaStream_t stream) {
+  if (!counts) return fail(CLAD3DGS_INVALID_ARGUMENT, "count pass: null counts");
+  cudaError_t e = cudaMemsetAsync(counts, 0, 3 * sizeof(unsigned long long), stream);
+  if (e != cudaSuccess) return status_of(e, "count pass");
+  if (P <= 0 || num_rendered <= 0) return CLAD3DGS_OK;
+  if (!geom_buffer || !binning_buffer || !image_buffer)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "count pass: null buffer");
+  const int gx = (width + kTileX - 1) / kTileX, gy = (height + kTileY - 1) / kTileY;
+  GeomState g = geom_from(static_cast<char*>(const_cast<void*>(geom_buffer)), P);
+  ImageState img = image_from(static_cast<char*>(const_cast<void*>(image_buffer)),
+                              width * height, gx * gy);
+  count_accumulation_kernel<<<dim3(gx, gy), kTilePixels, 0, stream>>>(
+      img.ranges, point_list_from(binning_buffer), width, height, gx, g.mean2d,
+      g.conic_opacity, img.n_contrib, counts);
+  return status_of(cudaPeekAtLastError(), "count pass");
 }
 
 extern "C" int clad3dgs_warp_accumulate_probe(int mode, int n, int fields, const int* keys,

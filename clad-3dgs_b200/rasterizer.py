@@ -402,6 +402,19 @@ def forward_2d(mean2d, conic_opacity, rgb, depth, radii, width, height, bg):
     return num.value, color, invdepth, state
 
 
+def count_accumulation_2d(state):
+    """Atomic counts of the pixel backward on a forward_2d state (a counting
+    pass, not the backward): dict(pairs, mode1_per_field, mode2_reductions);
+    see clad3dgs_raster_count_accumulation."""
+    counts = torch.zeros(3, dtype=torch.int64, device=state["geom"].device)
+    native.check(native.library().clad3dgs_raster_count_accumulation(
+        state["P"], state["width"], state["height"], state["geom"].data_ptr(),
+        state["binning"].data_ptr(), state["num_rendered"], state["image"].data_ptr(),
+        counts.data_ptr(), native.stream_handle()), "count_accumulation_2d")
+    pairs, mode1, mode2 = (int(x) for x in counts.cpu().tolist())
+    return dict(pairs=pairs, mode1_per_field=mode1, mode2_reductions=mode2)
+
+
 def render_backward_2d(state, dpixels, grads, mode=None, dinvdepth_pixels=None):
     """Pixel backward into grads = dict(dmean2d [P,3], dconic [P,4],
     dopacity [P], dcolor [P,3], dinvdepth [P] or None), accumulated."""

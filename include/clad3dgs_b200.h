@@ -260,6 +260,19 @@ int clad3dgs_raster_render_backward(
     const float* dpixels, const float* dinvdepth_pixels, float* dmean2d, float* dconic,
     float* dopacity, float* dcolor, float* dinvdepth, int mode, cudaStream_t stream);
 
+/* Counting pass of the pixel backward (for the measurement's atomic counts;
+ * not part of the backward): after a forward, writes counts[3] (u64, device):
+ * [0] contributing (pixel, Gaussian) pairs; [1] atomics per adjoint field of
+ * accumulation mode 1 (per warp and Gaussian: 1 when all 32 lanes contribute,
+ * else the contributing lanes); [2] warp reductions of mode 2 (each one
+ * multi-lane atomic instruction covering every field). Mode 0 issues counts[0]
+ * atomics per field. The reference's patched renderer holds 8 atomic sites
+ * per contributing pair (prepare_native.py:25). */
+int clad3dgs_raster_count_accumulation(int P, int width, int height,
+                                       const void* geom_buffer, const void* binning_buffer,
+                                       int num_rendered, const void* image_buffer,
+                                       unsigned long long* counts, cudaStream_t stream);
+
 /* Test probe of the pixel backward's warp accumulation (its helpers run on
  * caller-given lane streams, for parity with the reference's own helper,
  * WarpAccumulation.cuh:9-29, on the same streams). Thread i of the launch

@@ -714,14 +714,14 @@ static int by_float_depth(const void* a, const void* b) {
   return i < j ? -1 : (i > j);
 }
 
-/* p = -1/2 d^T Q d rounded as the CUDA path rounds it: (a dx) dx fused with
- * (c dy) dy, then -1/2 of that fused with -(b dx) dy (every product and sum
- * of float operands rounded to float; fmaf rounds once). d = mean - pixel in
- * float. */
+/* p = -1/2 d^T Q d rounded as the CUDA path rounds it: the quadratic in dy
+ * c2 dy^2 + c1 dy + c0 with c2 = -c/2, c1 = -(b dx), c0 = -((a dx) dx)/2, by
+ * Horner's rule with fused multiply-adds (every product of float operands
+ * rounded to float; fmaf rounds once). d = mean - pixel in float. */
 static float float_form(const float* co, float dx, float dy) {
-  float ax = co[0] * dx, cy = co[2] * dy, bx = co[1] * dx;
-  float diag = fmaf(ax, dx, cy * dy);
-  return fmaf(-0.5f, diag, -(bx * dy));
+  float ax = co[0] * dx;
+  float c0 = -0.5f * (ax * dx), c1 = -(co[1] * dx), c2 = -0.5f * co[2];
+  return fmaf(fmaf(c2, dy, c1), dy, c0);
 }
 
 static void add_sizes(double* mean2d, double* conic, double* opacity, int id,
