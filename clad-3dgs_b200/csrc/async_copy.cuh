@@ -11,7 +11,7 @@ namespace clad3dgs {
 
 // Fault codes OR-ed into the per-module fault word when a wait gives up.
 enum FaultCode : unsigned {
-  kFaultProducerWait = 1u,   // producer timed out waiting for a free stage
+  kFaultProducerWait = 1u,   // producer timed out waiting for a tile to be computed
   kFaultConsumerWait = 2u,   // consumers timed out waiting for a full stage
 };
 

@@ -12,9 +12,11 @@
 //    (cp.async.bulk, the TMA engine) per array into shared memory and written
 //    back the same way. There are no per-lane 12-byte accesses.
 //  * The main kernel is persistent: up to three CTAs per SM, each with a ring of
-//    stages in shared memory, one producer thread issuing bulk loads ahead and
-//    sixteen consumer warps doing the arithmetic. Stage reuse is gated by
-//    mbarriers, write-back by bulk-store groups, so HBM reads, compute and HBM
+//    stages in shared memory, one producer warp issuing the bulk loads ahead
+//    and the bulk stores behind, and sixteen consumer warps doing the
+//    arithmetic. The consumers signal each computed tile on an mbarrier and
+//    never wait on a store; the producer stores that tile, waits until the
+//    stores have read the stage and refills it. HBM reads, compute and HBM
 //    writes overlap, and one CTA's barrier waits overlap another's arithmetic.
 //  * Per tile: the view direction of each Gaussian is computed once (phase A0),
 //    warp j then owns SH term j for the 32 Gaussians of the tile (phase A1, lane
@@ -574,20 +576,21 @@ __device__ __forceinline__ void lane_array(int lane, bool& present, bool& writte
 static_assert(NUM_ARR <= 32, "one producer lane per staged array");
 
 // ---------------------------------------------------------------------------
-// Persistent pipeline: warp 0 produces, the other warps consume.
+// Persistent pipeline: warp 0 produces (loads ahead, stores behind), the
+// other warps consume.
 template <class C>
 __global__ void __launch_bounds__(kPersistThreads, C::ctas)
     stream_kernel(const StepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full_bar[C::stages];
-  __shared__ __align__(8) uint64_t empty_bar[C::stages];
+  __shared__ __align__(8) uint64_t done_bar[C::stages];
   __shared__ Scratch scratch;
   constexpr int S = C::stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&done_bar[s], 1);
     }
     scratch.abort = 0;
     fence_barrier_init();
@@ -597,23 +600,41 @@ __global__ void __launch_bounds__(kPersistThreads, C::ctas)
   const long long stride = gridDim.x;
 
   if (warp == 0) {
-    // Lane a issues the bulk load of staged array a (one warp instruction per
-    // tile instead of one per array); lane 0 owns the barriers.
+    // Lane a loads and stores staged array a (one warp instruction per tile
+    // for all arrays); lane 0 owns the barriers. Tile k goes to stage k % S.
+    // Before the stage is reused for tile k + S, the producer waits until the
+    // consumers have computed tile k, issues tile k's bulk stores and waits
+    // until they have read the stage; the consumers never wait on a store.
     bool present, written;
     uint32_t off, bytes;
     lane_array<C>(lane, present, written, off, bytes);
     const char* base = present ? static_cast<const char*>(p.ptr[lane]) : nullptr;
+    char* out = (present && written) ? static_cast<char*>(const_cast<void*>(p.ptr[lane]))
+                                     : nullptr;
+    auto drain = [&](int kd) -> bool {
+      const int s = kd % S;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(&done_bar[s], (kd / S) & 1) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      if (out) {
+        const long long t = first + (long long)kd * stride;
+        bulk_store(out + t * (long long)bytes, smem + size_t(s) * C::stage_bytes + off, bytes);
+        bulk_commit();
+      }
+      return true;
+    };
     int k = 0;
     for (long long t = first; t < p.tile_end; t += stride, ++k) {
       const int s = k % S;
-      int ok = 1;
       if (k >= S) {
-        if (lane == 0) ok = mbar_wait_bounded(&empty_bar[s], ((k / S) - 1) & 1) ? 1 : 0;
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-      }
-      if (!ok) {
-        if (lane == 0) atomicOr(&g_fault_word, kFaultProducerWait);
-        return;
+        if (!drain(k - S)) {
+          if (lane == 0) atomicOr(&g_fault_word, kFaultProducerWait);
+          bulk_wait_read<0>();
+          return;
+        }
+        bulk_wait_read<0>();  // the stores of tile k - S have read stage s
+        __syncwarp();
       }
       if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], C::load_bytes());
       __syncwarp();
@@ -621,20 +642,19 @@ __global__ void __launch_bounds__(kPersistThreads, C::ctas)
         bulk_load(smem + size_t(s) * C::stage_bytes + off, base + t * (long long)bytes,
                   bytes, &full_bar[s]);
     }
+    for (int kd = k > S ? k - S : 0; kd < k; ++kd) {
+      if (!drain(kd)) {
+        if (lane == 0) atomicOr(&g_fault_word, kFaultProducerWait);
+        break;
+      }
+    }
+    bulk_wait_read<0>();
     return;
   }
 
   const int ct = threadIdx.x - 32;
   float cam[3];
   load_camera<C>(p, cam);
-  bool store_present = false, store_written = false;
-  uint32_t store_off = 0, store_bytes = 0;
-  char* out_base = nullptr;
-  if (ct < 32) {
-    lane_array<C>(ct, store_present, store_written, store_off, store_bytes);
-    if (store_present && store_written)
-      out_base = static_cast<char*>(const_cast<void*>(p.ptr[ct]));
-  }
   // Warp 1 waits for each stage and fills that tile's view data one tile ahead
   // (the first before the loop, the next during phase B); the barrier that
   // follows its wait orders every other consumer after its acquire, so only
@@ -674,22 +694,8 @@ __global__ void __launch_bounds__(kPersistThreads, C::ctas)
     }
     fence_async_shared();
     named_barrier(1, kConsumers);
-    if (ct < 32) {
-      // Lane a stores written array a and tracks its own bulk groups; the
-      // previous tile's stage is released once every lane's older stores have
-      // finished reading shared memory.
-      if (store_present && store_written) {
-        bulk_store(out_base + t * (long long)store_bytes, st.base + store_off, store_bytes);
-        bulk_commit();
-      }
-      if (k > 0) {
-        bulk_wait_read<1>();
-        __syncwarp();
-        if (ct == 0) mbar_arrive(&empty_bar[(k - 1) % S]);
-      }
-    }
+    if (ct == 0) mbar_arrive(&done_bar[s]);  // tile k computed: the producer stores it
   }
-  if (ct < 32) bulk_wait_read<0>();
 }
 
 // ---------------------------------------------------------------------------
