@@ -1,8 +1,8 @@
 // Bulk (TMA 1D) copies, mbarriers and named barriers for sm_100a, plus the
 // bounded waits every pipeline barrier goes through.
 //
-// No load here uses .multicast::cluster: all sources are this GPU's memory and
-// each CTA fetches its own tiles.
+// Every load here is a plain single-CTA bulk copy from this GPU's own memory:
+// each CTA fetches its own tiles, and no copy is shared across a cluster.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>

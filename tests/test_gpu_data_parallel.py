@@ -353,7 +353,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir):
+def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir, size="small"):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -366,8 +366,15 @@ def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir):
                             timeout=timedelta(seconds=120), device_id=device)
     trainer = None
     try:
-        n, W, H = 2003, 96, 64
-        values = _small_scene(n, device)
+        if size == "small":
+            n, W, H = 2003, 96, 64
+            values = _small_scene(n, device)
+        else:
+            # The 8-view training configuration: 6,000,000 Gaussians, 1920x1080 views.
+            from bench import train_values
+
+            n, W, H = 6_000_000, 1920, 1080
+            values = train_values(n, device, seed=3)
         trainer = DataParallelTrainer(values, RATES, exchange=exchange, device=device,
                                       sh_exchange=sh_exchange)
         a = trainer.adam
@@ -436,5 +443,21 @@ def test_two_gpu_exchange_matches_emulation(cuda, exchange, sh_exchange, tmp_pat
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(_dp_worker, args=(2, _free_port(), exchange, sh_exchange, str(tmp_path)),
+             nprocs=2)
+    assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
+
+
+@pytest.mark.parametrize("exchange,sh_exchange", [("peer", "seeds"), ("collective", "grads")])
+def test_two_gpu_exchange_matches_emulation_at_full_size(cuda, exchange, sh_exchange,
+                                                         tmp_path):
+    """The 8-view data-parallel configuration on two GPUs: 6,000,000 Gaussians,
+    one 1920x1080 orbit view per GPU, three steps; after each exchange every
+    rank's share, moments and replica are bit-identical to the same update
+    kernel run over local copies of both ranks' gradients (or seeds)."""
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_dp_worker, args=(2, _free_port(), exchange, sh_exchange, str(tmp_path), "full"),
              nprocs=2)
     assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
