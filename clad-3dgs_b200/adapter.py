@@ -33,7 +33,7 @@ import torch
 
 from optimizer_claims import (ADAM_OPTIONS, STATE_KEYS, Claim, bias_corrections,
                               dense_fp32_cuda, finite_rate, last_failure, overlapping,
-                              owns_only, plain_fused_adam, read_counters, reference_betas,
+                              owns_only, read_counters, reference_betas,
                               settle, sole_group, state_or_fresh, state_problem, valid_counter)
 
 SH_OPTIONS = ADAM_OPTIONS
