@@ -72,9 +72,10 @@ def parse():
                     help="train-step: rank r renders orbit camera (r + offset) mod 8")
     ap.add_argument("--exchange", choices=["peer", "collective"], default=None,
                     help="train-step: gradient exchange (default: peer memory on >1 GPU)")
-    ap.add_argument("--sh-exchange", choices=["seeds", "grads"], default=None,
+    ap.add_argument("--sh-exchange", choices=["seeds", "colours", "grads"], default=None,
                     help="train-step: what a view publishes for the SH coefficients "
-                         "(default: colour seeds unless the exchange is collective)")
+                         "(default: colour seeds unless the exchange is collective; "
+                         "colours: the owners also render each rank's next colours)")
     ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
                     help="pixel-backward: 2D Gaussians (smaller cases are for profiling only)")
     ap.add_argument("--pixel-modes", default="2,1,0",
@@ -643,9 +644,10 @@ TRAIN_GAUSSIANS, TRAIN_W, TRAIN_H = 6_000_000, 1920, 1080
 # row gather, row emission, row layout, tile counts, tile totals, tile ranges,
 # instance placement, render forward, L1 loss, render backward, preprocess
 # backward, then with SH gradients: SH backward, shard update; with colour
-# seeds: seeds, SH + position update, shard update of the other groups (CUB's
-# scans, sorts and reductions and NCCL's barriers are library launches).
-TRAIN_LAUNCHES_PER_STEP = {"grads": 17, "seeds": 18}
+# seeds: seeds, SH + position update, shard update of the other groups; the
+# colour form has no SH colour pass (CUB's scans, sorts and reductions and
+# NCCL's barriers are library launches).
+TRAIN_LAUNCHES_PER_STEP = {"grads": 17, "seeds": 18, "colours": 17}
 
 
 def train_step_arm(args):
@@ -695,16 +697,30 @@ def measure_train_step(args, steps, warmup, with_e2e):
         gen = torch.Generator(device=device).manual_seed(100 + v)
         targets.append(torch.rand(3, TRAIN_H, TRAIN_W, generator=gen, device=device))
     counter = [0]
+    coloured = trainer.adam.sh_exchange == "colours"
 
-    def view():
+    def draw():
         order = random.Random(1000 + counter[0]).sample(range(8), 8)
         v = (order[rank % 8] + args.view_offset) % 8
         counter[0] += 1
         return v
 
+    # The colour form declares each step's next view: the views are drawn one
+    # step ahead, in the same sequence.
+    ahead = [draw() if coloured else None]
+
+    def view():
+        if not coloured:
+            return draw(), None
+        v, ahead[0] = ahead[0], draw()
+        return v, ahead[0]
+
     def step_once(target=None):
-        v = view()
-        return trainer.step(cams[v], targets[v] if target is None else target(v))
+        v, nxt = view()
+        tgt = targets[v] if target is None else target(v)
+        if coloured:
+            return trainer.step(cams[v], tgt, next_camera=cams[nxt])
+        return trainer.step(cams[v], tgt)
 
     stream = torch.cuda.current_stream()
 
@@ -753,12 +769,15 @@ def measure_train_step(args, steps, warmup, with_e2e):
     for _ in range(exchange_steps):
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record(stream)
-        v = view()
+        v, nxt = view()
         trainer.backward(cams[v], targets[v])
         b1.record(stream)
         bracket()
         backward_total += b0.elapsed_time(b1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if coloured:
+            trainer.adam.next_camera.copy_(cams[nxt].campos)
+            trainer._declared = cams[nxt]
         e0.record(stream)
         trainer.adam.step()
         e1.record(stream)
@@ -822,24 +841,26 @@ def measure_train_step(args, steps, warmup, with_e2e):
     trainer.close()
     if rank != 0:
         return None
-    # Exchange roofline: bytes that must cross NVLink per GPU and direction
-    # (this share's parameters out to the other ranks, 236 B per Gaussian and
-    # peer; in: their gradients, 236 B, or in seed form their colour seeds and
-    # geometry gradients, 60 B), against the measured 770 GB/s peer copy; with
-    # one GPU the update is HBM-bound (inputs, params, moments read; params,
-    # moments written).
+    # Exchange roofline: bytes that must cross NVLink per GPU and direction,
+    # per Gaussian of this share and peer: out, this share's parameters (236 B;
+    # colour form: 44 B without the SH, and 12 B of colours); in, the peers'
+    # gradients (236 B; seed and colour forms: 16 B colour seeds and 44 B of
+    # geometry gradients). The busier direction against the measured 770 GB/s
+    # peer copy. With one GPU the update is HBM-bound (inputs, params, moments
+    # read; params, moments written; colour form: colours and clamp bits).
     floats = 59
-    seeded = adam.sh_exchange == "seeds"
+    seeded = adam.sh_exchange != "grads"
     inputs = (16 + 11 * 4) if seeded else floats * 4  # per Gaussian and view
+    outputs = (11 * 4 + 12) if adam.sh_exchange == "colours" else floats * 4
     if world > 1:
-        link = (world - 1) * share * floats * 4
+        link = (world - 1) * share * max(inputs, outputs)
         exchange_roof = {"bound": "nvlink", "achieved": link / (exchange_ms / 1e3) / 1e9,
                          "peak": 770.0, "unit": "GB/s",
                          "frac": link / (exchange_ms / 1e3) / 1e9 / 770.0,
                          "bytes_per_direction": link,
                          "peak_kind": "measured peer copy per direction"}
     else:
-        hbm = share * (inputs + floats * 4 * 6)
+        hbm = share * (inputs + floats * 4 * 6 + (20 if adam.sh_exchange == "colours" else 0))
         peak, peak_kind = measured_peaks()
         exchange_roof = {"bound": "hbm", "achieved": hbm / (exchange_ms / 1e3) / 1e9,
                          "peak": peak, "unit": "GB/s",

@@ -40,7 +40,8 @@ class ShardUpdateArgs(ctypes.Structure):
                 ("saved_norm", c_void_p), ("rates", c_double * (SHARD_GROUPS + 1)),
                 ("bias1", c_float), ("bias2_sqrt", c_float),
                 ("seeds", c_void_p * MAX_RANKS), ("cameras", c_void_p * MAX_RANKS),
-                ("degree", c_int)]
+                ("degree", c_int), ("colours", c_void_p * MAX_RANKS),
+                ("next_cameras", c_void_p * MAX_RANKS), ("clamp_bits", c_void_p)]
 
 
 _P = c_void_p
@@ -106,6 +107,7 @@ _SIGNATURES = {
     "clad3dgs_activate": (c_int, [c_int64] + [_P] * 7 + [_P]),
     "clad3dgs_l1_loss": (c_int, [c_int64, _P, _P, _P, _P, _P]),
     "clad3dgs_shard_update": (c_int, [POINTER(ShardUpdateArgs), _P]),
+    "clad3dgs_shard_colours": (c_int, [POINTER(ShardUpdateArgs), _P]),
     "clad3dgs_ipc_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(ctypes.c_ubyte)]),
     "clad3dgs_ipc_free": (c_int, [_P]),
     "clad3dgs_ipc_open": (c_int, [POINTER(ctypes.c_ubyte), POINTER(c_void_p)]),

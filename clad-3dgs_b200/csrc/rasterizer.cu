@@ -309,9 +309,14 @@ __global__ void preprocess_kernel(int P, const float* __restrict__ means,
   const int touched = (x1 - x0) * (y1 - y0);
   if (touched == 0) return;
   // SH colours come from sh_colour_kernel (coalesced coefficient reads).
+  // Given colours were clamped by whoever made them (if at all): no channel
+  // is masked in the seeds taken from this view.
   if (colors_precomp) {
 #pragma unroll
-    for (int k = 0; k < 3; ++k) g.rgb[3 * i + k] = colors_precomp[3 * i + k];
+    for (int k = 0; k < 3; ++k) {
+      g.rgb[3 * i + k] = colors_precomp[3 * i + k];
+      g.clamped[3 * i + k] = false;
+    }
   }
   g.depth[i] = t.z;
   g.radii[i] = radius;
@@ -1188,32 +1193,12 @@ __global__ void preprocess_backward_kernel(
   for (int k = 0; k < 4; ++k) o.drotations[4 * i + k] = dq4[k];
 }
 
-// SH colour of every drawn Gaussian (radius > 0): colour + 0.5, clamped at 0,
-// with the clamp flags the backward reads.
-__global__ void __launch_bounds__(32 * kShWarps)
-    sh_colour_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
-                     const float* __restrict__ campos, GeomState g) {
-  __shared__ float rows[kShWarps][32 * kShRow];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* blk = rows[warp];
-  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
-  if (i0 >= P) return;  // whole warp
-  const int n = min(32, P - i0);
-  stage_coefficients(sh, i0, n, lane, blk);
-  __syncwarp();
-  const int i = i0 + lane;
-  if (lane >= n || g.radii[i] <= 0) return;
-  const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
-                                     campos[0], campos[1], campos[2]);
-  float rgb[3] = {0.f, 0.f, 0.f};
-  colour_terms<0>(d, RowSource{blk + lane * kShRow}, i, (degree + 1) * (degree + 1), rgb);
-#pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    const float v = rgb[k] + 0.5f;
-    g.clamped[3 * i + k] = v < 0.f;
-    g.rgb[3 * i + k] = fmaxf(v, 0.f);
-  }
-}
+// SH colour of every drawn Gaussian: sh_backward.cu (one translation unit
+// without multiply-add contraction with the data-parallel colour production).
+cudaError_t launch_sh_colour(int P, int degree, const float* means, ShSource sh,
+                             const float* campos, const int* radii, bool* clamped, float* rgb,
+                             cudaStream_t stream);
+
 
 // The SH backward (sh_backward.cu, compiled without contraction so that the
 // data-parallel exchange's seed form rounds exactly alike).
@@ -1367,6 +1352,8 @@ extern "C" int clad3dgs_raster_forward(
     return fail(CLAD3DGS_INVALID_ARGUMENT, "SH degree must be between zero and three");
   if (width <= 0 || height <= 0)
     return fail(CLAD3DGS_INVALID_ARGUMENT, "image size must be positive");
+  if (P > 0 && !colors_precomp && !(sh_packed || (sh_dc && sh_rest)))
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "forward: neither colours nor SH coefficients");
   const Camera cam = make_camera(view, proj, campos, width, height, tan_x, tan_y);
   const int tiles = cam.grid_x * cam.grid_y;
   char* image_base = alloc(alloc_ctx, 1, image_bytes(width * height, tiles));
@@ -1383,9 +1370,8 @@ extern "C" int clad3dgs_raster_forward(
         P, means, scales, scale_modifier, rotations, opacities, colors_precomp, cov3d_precomp,
         cam, antialiasing != 0, g, radii);
     if (!colors_precomp) {
-      const int warps = (P + 31) / 32;
-      sh_colour_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
-          P, degree, means, sh, campos, g);
+      e = launch_sh_colour(P, degree, means, sh, campos, g.radii, g.clamped, g.rgb, stream);
+      if (e != cudaSuccess) return status_of(e, "SH colour");
     }
     uint32_t total = 0, pairs = 0;
     int status = order_and_count(P, g, total, pairs, stream);
@@ -1515,6 +1501,8 @@ extern "C" int clad3dgs_raster_backward(
   if (consume_sh < 0 || consume_sh > 2)
     return fail(CLAD3DGS_INVALID_ARGUMENT, "consume_sh must be 0, 1 or 2");
   if (P <= 0) return CLAD3DGS_OK;
+  if (!colors_precomp && consume_sh != 2 && !(sh_packed || (sh_dc && sh_rest)))
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "backward: neither colours nor SH coefficients");
   int status = clad3dgs_raster_render_backward(
       P, width, height, bg, geom_buffer, binning_buffer, num_rendered, image_buffer, dpixels,
       dinvdepth_pixels, dmean2d, dconic_scratch, dopacity, dcolor,

@@ -83,6 +83,43 @@ __global__ void __launch_bounds__(32 * kShWarps)
   for (int e = lane; e < n * 48; e += 32) dst[e] = blk[(e / 48) * kShRow + e % 48];
 }
 
+// SH colour of every drawn Gaussian (radius > 0): colour + 0.5, clamped at 0,
+// with the clamp flags the backward reads (the rasterizer's colour pass).
+__global__ void __launch_bounds__(32 * kShWarps)
+    sh_colour_kernel(int P, int degree, const float* __restrict__ means, ShSource sh,
+                     const float* __restrict__ campos, const int* __restrict__ radii,
+                     bool* __restrict__ clamped, float* __restrict__ rgb) {
+  __shared__ float rows[kShWarps][32 * kShRow];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* blk = rows[warp];
+  const int i0 = (blockIdx.x * kShWarps + warp) * 32;
+  if (i0 >= P) return;  // whole warp
+  const int n = min(32, P - i0);
+  stage_coefficients(sh, i0, n, lane, blk);
+  __syncwarp();
+  const int i = i0 + lane;
+  if (lane >= n || radii[i] <= 0) return;
+  const Direction d = make_direction(means[3 * i], means[3 * i + 1], means[3 * i + 2],
+                                     campos[0], campos[1], campos[2]);
+  float c[3];
+  bool cut[3];
+  shaded_colour(d, RowSource{blk + lane * kShRow}, i, (degree + 1) * (degree + 1), c, cut);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    clamped[3 * i + k] = cut[k];
+    rgb[3 * i + k] = c[k];
+  }
+}
+
+cudaError_t launch_sh_colour(int P, int degree, const float* means, ShSource sh,
+                             const float* campos, const int* radii, bool* clamped, float* rgb,
+                             cudaStream_t stream) {
+  const int warps = (P + 31) / 32;
+  sh_colour_kernel<<<(warps + kShWarps - 1) / kShWarps, 32 * kShWarps, 0, stream>>>(
+      P, degree, means, sh, campos, radii, clamped, rgb);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_sh_backward(int P, int degree, const float* means, ShSource sh,
                                const float* campos, const bool* clamped, const int* radii,
                                const float* dcolor, float* dsh, float* dmeans,
@@ -115,6 +152,11 @@ struct SeedParams {
   float* xyz_second;
   float step_xyz, step_dc, step_rest;
   double inv_bias2;
+  // Colour form: the owner renders each rank's next colours [N][3] from its
+  // next camera and keeps the clamped channels (bit 3q + k) of its share.
+  float* colours[kSeedRanks];
+  const float* next_cameras[kSeedRanks];
+  uint32_t* clamp_bits;
 };
 
 // Several views, term-outer: for each term J every view's contribution to
@@ -167,32 +209,10 @@ __device__ __forceinline__ void views_adjoint_terms(const float4 (&dir)[R],
   }
 }
 
-// The gradient row overwrites the coefficient row in place (each term's
-// coefficients are read, by every view, before its gradients are written) and
-// the Adam pass reloads the parameters: one row of shared memory per Gaussian.
-template <int R>
-__global__ void __launch_bounds__(32 * kSeedWarps)
-    shard_seed_kernel(const __grid_constant__ SeedParams a) {
-  constexpr bool kInPlace = true;
-  __shared__ float rows[kSeedWarps][(kInPlace ? 1 : 2) * 32 * kSeedRow];
-  __shared__ float cams[R][3];
-  using raster::CoefficientSum;
-  using raster::RowSource;
-  if (threadIdx.x < 3 * R) {
-    const int q = threadIdx.x / 3, k = threadIdx.x % 3;
-    cams[q][k] = a.cameras[q][k];
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t i0 = a.begin + (int64_t(blockIdx.x) * kSeedWarps + warp) * 32;
-  if (i0 >= a.end) return;  // whole warp
-  const int n = int(a.end - i0 < 32 ? a.end - i0 : 32);
-  float* cb = rows[warp];
-  float* sb = kInPlace ? cb : cb + 32 * kSeedRow;
-  // The block's coefficients, as float4 chunks (a chunk never straddles two
-  // Gaussians: 48 = 12 x 4), every load independent.
-  const int chunks = n * 12;
-  const float4* src = reinterpret_cast<const float4*>(a.sh[a.local] + 48 * i0);
+// The block's coefficients into rows of kSeedRow floats, as float4 chunks (a
+// chunk never straddles two Gaussians: 48 = 12 x 4), every load independent.
+__device__ __forceinline__ void stage_block(const float4* src, int chunks, int lane,
+                                            float* cb) {
   for (int c = lane; c < chunks; c += 32) {
     const float4 v = src[c];
     float* dst = cb + (c / 12) * kSeedRow + 4 * (c % 12);
@@ -201,7 +221,64 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
     dst[2] = v.z;
     dst[3] = v.w;
   }
+}
+
+// Colour form: Gaussian i's colour from every rank's next camera, by the
+// rasterizer's colour pass arithmetic (direction from the position to the
+// camera, SH sum + 0.5 clamped at 0; same translation unit, same flags), into
+// that rank's colour array, and the clamped channels into the share's bits.
+template <int R>
+__device__ __forceinline__ void emit_colours(const SeedParams& a, const float (*next)[3],
+                                             const float* row, int64_t i,
+                                             const float (&pos)[3]) {
+  uint32_t bits = 0;
+#pragma unroll
+  for (int q = 0; q < R; ++q) {
+    const Direction d =
+        make_direction(pos[0], pos[1], pos[2], next[q][0], next[q][1], next[q][2]);
+    float c[3];
+    bool cut[3];
+    raster::shaded_colour(d, raster::RowSource{row}, int(i), a.nterms, c, cut);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      __stcs(a.colours[q] + 3 * i + k, c[k]);
+      bits |= cut[k] ? 1u << (3 * q + k) : 0u;
+    }
+  }
+  a.clamp_bits[i - a.begin] = bits;
+}
+
+// The gradient row overwrites the coefficient row in place (each term's
+// coefficients are read, by every view, before its gradients are written) and
+// the Adam pass reloads the parameters: one row of shared memory per Gaussian.
+// In colour form the Adam pass leaves the new coefficients in the row for the
+// next colours, and the coefficients are stored into the owner's replica only.
+template <int R, bool Colours>
+__global__ void __launch_bounds__(32 * kSeedWarps)
+    shard_seed_kernel(const __grid_constant__ SeedParams a) {
+  constexpr bool kInPlace = true;
+  __shared__ float rows[kSeedWarps][(kInPlace ? 1 : 2) * 32 * kSeedRow];
+  __shared__ float cams[R][3];
+  __shared__ float next[Colours ? R : 1][3];
+  using raster::CoefficientSum;
+  using raster::RowSource;
+  if (threadIdx.x < 3 * R) {
+    const int q = threadIdx.x / 3, k = threadIdx.x % 3;
+    cams[q][k] = a.cameras[q][k];
+    if (Colours) next[q][k] = a.next_cameras[q][k];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = a.begin + (int64_t(blockIdx.x) * kSeedWarps + warp) * 32;
+  if (i0 >= a.end) return;  // whole warp
+  const int n = int(a.end - i0 < 32 ? a.end - i0 : 32);
+  float* cb = rows[warp];
+  float* sb = kInPlace ? cb : cb + 32 * kSeedRow;
+  const int chunks = n * 12;
+  const float4* src = reinterpret_cast<const float4*>(a.sh[a.local] + 48 * i0);
+  stage_block(src, chunks, lane, cb);
   __syncwarp();
+  float moved[3] = {0.f, 0.f, 0.f};  // the updated position (colour form)
   if (lane < n) {
     const int64_t i = i0 + lane;
     const float* row = cb + lane * kSeedRow;
@@ -217,6 +294,17 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
       seed[q] = a.seeds[q][i];
 #pragma unroll
       for (int k = 0; k < 3; ++k) geo[q][k] = a.geo_xyz[q][3 * i + k];
+    }
+    if constexpr (Colours) {
+      // View q rendered the colours this owner made for it: its seed carries
+      // every channel, and the channels the clamp cut have no gradient.
+      const uint32_t bits = a.clamp_bits[i - a.begin];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        if (bits & (1u << (3 * q))) seed[q].x = 0.f;
+        if (bits & (1u << (3 * q + 1))) seed[q].y = 0.f;
+        if (bits & (1u << (3 * q + 2))) seed[q].z = 0.f;
+      }
     }
     float x[3];
     if constexpr (R > 1) {
@@ -279,6 +367,7 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
       torch_adam(p, m, v, x[k], a.step_xyz, a.inv_bias2);
       a.xyz_first[mx + k] = m;
       a.xyz_second[mx + k] = v;
+      moved[k] = p;
 #pragma unroll
       for (int q = 0; q < R; ++q) __stcs(a.xyz[q] + 3 * i + k, p);
     }
@@ -316,28 +405,104 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
     first[c] = make_float4(m[0], m[1], m[2], m[3]);
     second[c] = make_float4(v[0], v[1], v[2], v[3]);
     const float4 out = make_float4(p[0], p[1], p[2], p[3]);
+    if constexpr (Colours) {
+      // This lane alone read these gradient elements: the row takes the new
+      // coefficients in their place.
 #pragma unroll
-    for (int q = 0; q < R; ++q) __stcs(reinterpret_cast<float4*>(a.sh[q] + 48 * i0) + c, out);
+      for (int t = 0; t < 4; ++t) sb[at + t] = p[t];
+      __stcs(reinterpret_cast<float4*>(a.sh[a.local] + 48 * i0) + c, out);
+    } else {
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+        __stcs(reinterpret_cast<float4*>(a.sh[q] + 48 * i0) + c, out);
+    }
     m4 = m_next;
     v4 = v_next;
     p4 = p_next;
+  }
+  if constexpr (Colours) {
+    __syncwarp();
+    if (lane < n) emit_colours<R>(a, next, sb + lane * kSeedRow, i0 + lane, moved);
   }
   // Make the peer stores visible system-wide before the kernel retires.
   if (R > 1) __threadfence_system();
 }
 
+// Colour form, before the first update: the share's colours from the current
+// positions and coefficients of the owner's replica.
 template <int R>
-cudaError_t launch_seed(const SeedParams& p, cudaStream_t stream) {
+__global__ void __launch_bounds__(32 * kSeedWarps)
+    shard_colour_kernel(const __grid_constant__ SeedParams a) {
+  __shared__ float rows[kSeedWarps][32 * kSeedRow];
+  __shared__ float next[R][3];
+  if (threadIdx.x < 3 * R) next[threadIdx.x / 3][threadIdx.x % 3] =
+      a.next_cameras[threadIdx.x / 3][threadIdx.x % 3];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = a.begin + (int64_t(blockIdx.x) * kSeedWarps + warp) * 32;
+  if (i0 >= a.end) return;  // whole warp
+  const int n = int(a.end - i0 < 32 ? a.end - i0 : 32);
+  float* cb = rows[warp];
+  stage_block(reinterpret_cast<const float4*>(a.sh[a.local] + 48 * i0), n * 12, lane, cb);
+  __syncwarp();
+  if (lane < n) {
+    const int64_t i = i0 + lane;
+    float pos[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) pos[k] = a.xyz[a.local][3 * i + k];
+    emit_colours<R>(a, next, cb + lane * kSeedRow, i, pos);
+  }
+  if (R > 1) __threadfence_system();
+}
+
+template <int R>
+cudaError_t launch_seed(const SeedParams& p, bool colours, bool update, cudaStream_t stream) {
   const int64_t warps = (p.end - p.begin + 31) / 32;
-  const int64_t blocks = (warps + kSeedWarps - 1) / kSeedWarps;
-  shard_seed_kernel<R><<<unsigned(blocks), 32 * kSeedWarps, 0, stream>>>(p);
+  const unsigned blocks = unsigned((warps + kSeedWarps - 1) / kSeedWarps);
+  if (!update)
+    shard_colour_kernel<R><<<blocks, 32 * kSeedWarps, 0, stream>>>(p);
+  else if (colours)
+    shard_seed_kernel<R, true><<<blocks, 32 * kSeedWarps, 0, stream>>>(p);
+  else
+    shard_seed_kernel<R, false><<<blocks, 32 * kSeedWarps, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
 bool aligned16(const void* p);  // train_step.cu
 
-// The SH and position groups of clad3dgs_shard_update in seed form (the
-// arguments are validated by the caller, except the seed fields).
+cudaError_t launch_for(const SeedParams& p, int ranks, bool colours, bool update,
+                       cudaStream_t stream) {
+  switch (ranks) {
+    case 1: return launch_seed<1>(p, colours, update, stream);
+    case 2: return launch_seed<2>(p, colours, update, stream);
+    case 3: return launch_seed<3>(p, colours, update, stream);
+    case 4: return launch_seed<4>(p, colours, update, stream);
+    case 5: return launch_seed<5>(p, colours, update, stream);
+    case 6: return launch_seed<6>(p, colours, update, stream);
+    case 7: return launch_seed<7>(p, colours, update, stream);
+    default: return launch_seed<8>(p, colours, update, stream);
+  }
+}
+
+// The colour form's fields: a colour array and a next camera per rank, the
+// share's clamp bits.
+int colour_fields(const clad3dgs_shard_update_args& x, SeedParams& p) {
+  for (int q = 0; q < x.ranks; ++q) {
+    if (!x.colours[q] || !x.next_cameras[q])
+      return fail(CLAD3DGS_INVALID_ARGUMENT,
+                  "shard update: the colour form needs every rank's colour array and next "
+                  "camera");
+    p.colours[q] = x.colours[q];
+    p.next_cameras[q] = x.next_cameras[q];
+  }
+  if (!x.clamp_bits)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard update: the colour form needs clamp bits");
+  p.clamp_bits = x.clamp_bits;
+  return CLAD3DGS_OK;
+}
+
+// The SH and position groups of clad3dgs_shard_update in seed (or colour)
+// form (the arguments are validated by the caller, except the seed fields).
 int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream) {
   if (x.degree < 0 || x.degree > 3)
     return fail(CLAD3DGS_INVALID_ARGUMENT, "shard update: SH degree must be 0..3");
@@ -359,6 +524,11 @@ int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream) 
     p.sh[q] = x.params[q][1];
     p.xyz[q] = x.params[q][0];
   }
+  const bool colours = x.colours[0] != nullptr;
+  if (colours) {
+    const int status = colour_fields(x, p);
+    if (status != CLAD3DGS_OK) return status;
+  }
   p.sh_first = x.first[1];
   p.sh_second = x.second[1];
   p.xyz_first = x.first[0];
@@ -367,17 +537,7 @@ int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream) 
   p.step_dc = float(x.rates[1] / double(x.bias1));
   p.step_rest = float(x.rates[2] / double(x.bias1));
   p.inv_bias2 = 1.0 / double(x.bias2_sqrt);
-  cudaError_t e = cudaSuccess;
-  switch (x.ranks) {
-    case 1: e = launch_seed<1>(p, stream); break;
-    case 2: e = launch_seed<2>(p, stream); break;
-    case 3: e = launch_seed<3>(p, stream); break;
-    case 4: e = launch_seed<4>(p, stream); break;
-    case 5: e = launch_seed<5>(p, stream); break;
-    case 6: e = launch_seed<6>(p, stream); break;
-    case 7: e = launch_seed<7>(p, stream); break;
-    default: e = launch_seed<8>(p, stream); break;
-  }
+  const cudaError_t e = launch_for(p, x.ranks, colours, true, stream);
   return e == cudaSuccess ? CLAD3DGS_OK
                           : fail(CLAD3DGS_CUDA_ERROR, std::string("shard update (seeds): ") +
                                                           cudaGetErrorString(e));
@@ -385,3 +545,38 @@ int shard_seed_update(const clad3dgs_shard_update_args& x, cudaStream_t stream) 
 
 }  // namespace train
 }  // namespace clad3dgs
+
+using namespace clad3dgs;
+using namespace clad3dgs::train;
+
+extern "C" int clad3dgs_shard_colours(const clad3dgs_shard_update_args* args,
+                                      cudaStream_t stream) {
+  if (!args) return fail(CLAD3DGS_INVALID_ARGUMENT, "shard colours: null arguments");
+  const clad3dgs_shard_update_args& x = *args;
+  if (x.ranks < 1 || x.ranks > kSeedRanks)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard colours: ranks must be 1..8");
+  if (x.local < 0 || x.local >= x.ranks)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard colours: local replica out of range");
+  if (x.begin < 0 || x.end < x.begin)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard colours: range must be ordered");
+  if (x.degree < 0 || x.degree > 3)
+    return fail(CLAD3DGS_INVALID_ARGUMENT, "shard colours: SH degree must be 0..3");
+  if (!x.params[x.local][0] || !x.params[x.local][1] || !aligned16(x.params[x.local][1]))
+    return fail(CLAD3DGS_INVALID_ARGUMENT,
+                "shard colours: the local positions and 16-byte aligned coefficients are "
+                "needed");
+  if (x.end == x.begin) return CLAD3DGS_OK;
+  SeedParams p{};
+  p.begin = x.begin;
+  p.end = x.end;
+  p.local = x.local;
+  p.nterms = (x.degree + 1) * (x.degree + 1);
+  p.sh[x.local] = x.params[x.local][1];
+  p.xyz[x.local] = x.params[x.local][0];
+  const int status = colour_fields(x, p);
+  if (status != CLAD3DGS_OK) return status;
+  const cudaError_t e = launch_for(p, x.ranks, true, false, stream);
+  return e == cudaSuccess ? CLAD3DGS_OK
+                          : fail(CLAD3DGS_CUDA_ERROR, std::string("shard colours: ") +
+                                                          cudaGetErrorString(e));
+}

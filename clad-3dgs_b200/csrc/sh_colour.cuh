@@ -70,6 +70,24 @@ __device__ __forceinline__ void colour_terms(const Direction& d, const Source& s
   }
 }
 
+// The rendered colour of one Gaussian seen along d: the SH colour + 0.5,
+// clamped at 0, and which channels the clamp cut (their colour adjoint is
+// dropped by the backward). The forward's colour pass and the data-parallel
+// owner's colour production (sh_backward.cu) both call this from one
+// translation unit, so they give the same bits.
+template <class Source>
+__device__ __forceinline__ void shaded_colour(const Direction& d, const Source& sh, int i,
+                                              int nterms, float rgb[3], bool clamped[3]) {
+  float sum[3] = {0.f, 0.f, 0.f};
+  colour_terms<0>(d, sh, i, nterms, sum);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float v = sum[k] + 0.5f;
+    clamped[k] = v < 0.f;
+    rgb[k] = fmaxf(v, 0.f);
+  }
+}
+
 // Where d colour / d c_j goes: stored (null: not wanted), or added to a sum
 // over views (`first`: the sum starts here). The sum rounds each product
 // before adding it, as a sum of stored per-view adjoints would (and as every

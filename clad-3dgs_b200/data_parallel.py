@@ -33,6 +33,15 @@ per-Gaussian update path. Per step on every rank:
      owner of a share evaluates every view's SH backward and view-direction
      adjoint inside the update, summed in rank order, bit-identical to the
      gradient form.
+   * ``"colours"`` (peer exchange or one rank): the seed form, and in
+     addition no rank holds the other shares' SH coefficients. The owner of a
+     share renders, inside the update, each rank's colours for that rank's
+     next camera (declared with the step) and stores 12 B per Gaussian into
+     the rank's colour array instead of 192 B of coefficients into its
+     replica; the rank renders from those colours (colors_precomp). The owner
+     keeps which channels its clamp cut and masks the seeds with them. Same
+     parameters, bit for bit, as the seed form; before the first step
+     `prime` renders the first colours.
    * ``"grads"``: each rank writes its full SH gradients and the update sums
      them (the form a collective reduce-scatter needs).
 
@@ -121,14 +130,18 @@ class ShardStep(NamedTuple):
     seeds: list = None    # seed form: [ranks] colour seed arrays [N][4]
     cameras: list = None  # seed form: [ranks] camera positions (3 floats)
     degree: int = 3       # seed form: SH degree
+    colours: list = None       # colour form: [ranks] colour arrays [N][3]
+    next_cameras: list = None  # colour form: [ranks] next camera positions
+    clamp_bits: object = None  # colour form: the share's clamp bits [end - begin]
 
 
 def _address(x):
+    if x is None:
+        return None
     return int(x) if isinstance(x, int) else x.data_ptr()
 
 
-def native_update(s: ShardStep, stream=None):
-    """clad3dgs_shard_update on the current stream."""
+def _arguments(s: ShardStep):
     args = native.ShardUpdateArgs()
     args.begin, args.end, args.grad_origin = s.begin, s.end, s.grad_origin
     args.ranks, args.local = len(s.grads), s.local
@@ -149,10 +162,28 @@ def native_update(s: ShardStep, stream=None):
         for q in range(len(s.seeds)):
             args.seeds[q] = _address(s.seeds[q])
             args.cameras[q] = _address(s.cameras[q])
-        args.degree = int(s.degree)
-    native.check(native.library().clad3dgs_shard_update(ctypes.byref(args),
+    args.degree = int(s.degree)
+    if s.colours is not None:
+        for q in range(len(s.colours)):
+            args.colours[q] = _address(s.colours[q])
+            args.next_cameras[q] = _address(s.next_cameras[q])
+        args.clamp_bits = _address(s.clamp_bits)
+    return args
+
+
+def native_update(s: ShardStep, stream=None):
+    """clad3dgs_shard_update on the current stream."""
+    native.check(native.library().clad3dgs_shard_update(ctypes.byref(_arguments(s)),
                                                         native.stream_handle(stream)),
                  "shard update")
+
+
+def native_colours(s: ShardStep, stream=None):
+    """clad3dgs_shard_colours (the colour form's first colours) on the current
+    stream."""
+    native.check(native.library().clad3dgs_shard_colours(ctypes.byref(_arguments(s)),
+                                                         native.stream_handle(stream)),
+                 "shard colours")
 
 
 class ShardedAdam:
@@ -163,7 +194,11 @@ class ShardedAdam:
     this rank's view), `first` / `second` (moments of the share [begin, end)),
     `saved` (activated scaling / rotation / opacity and |q|, [padded, .]); in
     seed form `seeds` ([padded, 4], this rank's view) and `camera` (its
-    position, 3 floats), written before each step.
+    position, 3 floats), written before each step; in colour form also
+    `next_camera` (the position this rank renders from at the next step,
+    written before each step) and `colours` ([padded, 3], what the owners
+    rendered for it; the replica's SH coefficients are current only in this
+    rank's share: `gather_sh` brings the others in).
     """
 
     def __init__(self, n, rates=None, *, group=None, exchange=None, device=None,
@@ -187,12 +222,12 @@ class ShardedAdam:
         if sh_exchange is None:
             collective = exchange == "collective" and self.world > 1
             sh_exchange = "seeds" if self.device.type == "cuda" and not collective else "grads"
-        if sh_exchange not in ("seeds", "grads"):
-            raise ValueError("sh_exchange must be 'seeds' or 'grads'")
-        if sh_exchange == "seeds" and exchange == "collective" and self.world > 1:
+        if sh_exchange not in ("seeds", "colours", "grads"):
+            raise ValueError("sh_exchange must be 'seeds', 'colours' or 'grads'")
+        if sh_exchange != "grads" and exchange == "collective" and self.world > 1:
             raise ValueError("the collective exchange reduces SH gradients: use 'grads'")
-        if sh_exchange == "seeds" and self.device.type != "cuda":
-            raise ValueError("the seed form needs CUDA devices")
+        if sh_exchange != "grads" and self.device.type != "cuda":
+            raise ValueError(f"the {sh_exchange[:-1]} form needs CUDA devices")
         self.sh_exchange = sh_exchange
         self.degree = int(degree)
         self.rates = dict(DEFAULT_RATES if rates is None else rates)
@@ -208,9 +243,13 @@ class ShardedAdam:
         total = FLOATS_PER_GAUSSIAN * self.padded
         self._own = []
         self._peers = []
-        # Seed slab: the camera position (4 floats, so the seeds stay 16-byte
-        # aligned), then [padded, 4] seeds; padding Gaussians keep zero seeds.
-        seed_total = 4 + 4 * self.padded if sh_exchange == "seeds" else 0
+        # Seed slab: the camera position and the next one (4 floats each, so
+        # the seeds stay 16-byte aligned), then [padded, 4] seeds; padding
+        # Gaussians keep zero seeds. Colour form: [padded, 3] colours after them.
+        seeded = sh_exchange != "grads"
+        coloured = sh_exchange == "colours"
+        seed_total = (8 + 4 * self.padded + (3 * self.padded if coloured else 0)
+                      if seeded else 0)
         if exchange == "peer" and self.world > 1:
             param_slab, param_handle = self._ipc_slab(total)
             grad_slab, grad_handle = self._ipc_slab(total)
@@ -225,11 +264,17 @@ class ShardedAdam:
         self.param_slab, self.grad_slab, self.seed_slab = param_slab, grad_slab, seed_slab
         self.params = carve(param_slab, self.padded)
         self.grads = carve(grad_slab, self.padded)
+        self.colours = self.next_camera = self.clamp_bits = None
         if seed_slab is not None:
             if exchange == "peer" and self.world > 1:
                 seed_slab.zero_()
             self.camera = seed_slab[:3]
-            self.seeds = seed_slab[4:].view(self.padded, 4)
+            self.next_camera = seed_slab[4:7]
+            self.seeds = seed_slab[8:8 + 4 * self.padded].view(self.padded, 4)
+            if coloured:
+                self.colours = seed_slab[8 + 4 * self.padded:].view(self.padded, 3)
+                self.clamp_bits = torch.zeros(self.share, dtype=torch.int32,
+                                              device=self.device)
         else:
             self.camera = self.seeds = None
         zeros = lambda *s: torch.zeros(s, dtype=torch.float32, device=self.device)
@@ -262,6 +307,7 @@ class ShardedAdam:
         offsets = group_offsets(self.padded)
         self.peer_params, self.peer_grads = [], []
         self.peer_seeds, self.peer_cameras = [], []
+        self.peer_next_cameras, self.peer_colours = [], []
         for q in range(self.world):
             if q == self.rank:
                 bases = [self.param_slab.data_ptr(), self.grad_slab.data_ptr()]
@@ -282,7 +328,9 @@ class ShardedAdam:
             self.peer_grads.append([bases[1] + 4 * offsets[name] for name, _ in GROUPS])
             if seed_handle:
                 self.peer_cameras.append(bases[2])
-                self.peer_seeds.append(bases[2] + 16)
+                self.peer_next_cameras.append(bases[2] + 16)
+                self.peer_seeds.append(bases[2] + 32)
+                self.peer_colours.append(bases[2] + 32 + 16 * self.padded)
 
     def close(self):
         """Unmaps the peers' memory and frees this rank's (collective call)."""
@@ -298,6 +346,7 @@ class ShardedAdam:
         if self.distributed and self.world > 1:
             dist.barrier(group=self.group)
         self.params = self.grads = self.seeds = self.camera = None
+        self.colours = self.next_camera = None
         self.param_slab = self.grad_slab = self.seed_slab = None
         for address in self._own:
             native.check(native.library().clad3dgs_ipc_free(address), "ipc free")
@@ -344,8 +393,9 @@ class ShardedAdam:
     def _barrier(self):
         dist.all_reduce(self._flag, group=self.group)
 
-    def _shard_step(self, grads, params, grad_origin, local, seeds=None, cameras=None):
-        t = self.t
+    def _shard_step(self, grads, params, grad_origin, local, seeds=None, cameras=None,
+                    colours=None, next_cameras=None):
+        t = max(self.t, 1)  # `prime` comes before the first step and reads no rate
         return ShardStep(
             begin=self.begin, end=self.end, grad_origin=grad_origin, grads=grads,
             params=params, local=local, first=[self.first[n] for n, _ in GROUPS],
@@ -353,7 +403,49 @@ class ShardedAdam:
             saved_opacity=self.saved["opacity"], saved_norm=self.saved["norm"],
             rates=tuple(self.rates[r] for r in RATE_NAMES), bias1=1.0 - 0.9 ** t,
             bias2_sqrt=math.sqrt(1.0 - 0.999 ** t), seeds=seeds, cameras=cameras,
-            degree=self.degree)
+            degree=self.degree, colours=colours, next_cameras=next_cameras,
+            clamp_bits=self.clamp_bits if colours is not None else None)
+
+    def _peer_step(self):
+        """The step's arguments over every rank's memory (one rank: its own)."""
+        names = [n for n, _ in GROUPS]
+        seeded = self.sh_exchange != "grads"
+        coloured = self.sh_exchange == "colours"
+        if self.world == 1:
+            return self._shard_step([[self.grads[n] for n in names]],
+                                    [[self.params[n] for n in names]], 0, 0,
+                                    [self.seeds] if seeded else None,
+                                    [self.camera] if seeded else None,
+                                    [self.colours] if coloured else None,
+                                    [self.next_camera] if coloured else None)
+        return self._shard_step(self.peer_grads, self.peer_params, 0, self.rank,
+                                self.peer_seeds if seeded else None,
+                                self.peer_cameras if seeded else None,
+                                self.peer_colours if coloured else None,
+                                self.peer_next_cameras if coloured else None)
+
+    def prime(self):
+        """Colour form, before the first step (collective): every owner renders
+        its share's colours for every rank's `next_camera` from the current
+        parameters."""
+        if self.sh_exchange != "colours":
+            raise ValueError("prime belongs to the colour form")
+        if self.world > 1:
+            self._barrier()
+        native_colours(self._peer_step())
+        if self.world > 1:
+            self._barrier()
+
+    def gather_sh(self):
+        """Colour form: brings the other shares' SH coefficients into this
+        rank's replica (collective; the seed and gradient forms keep every
+        replica current, so there it does nothing)."""
+        if self.sh_exchange != "colours" or self.world == 1:
+            return self.params["sh"]
+        full = self.params["sh"].view(-1)
+        mine = full[48 * self.begin:48 * self.end].clone()
+        dist.all_gather_into_tensor(full, mine, group=self.group)
+        return self.params["sh"]
 
     def step(self):
         """Sums the ranks' gradients of this rank's share, runs Adam on it and
@@ -362,17 +454,11 @@ class ShardedAdam:
         if self.gate is not None and self.world > 1:
             self.gate.arrive_and_wait(self.t)
         names = [n for n, _ in GROUPS]
-        seeded = self.sh_exchange == "seeds"
         if self.world == 1:
-            self._update(self._shard_step([[self.grads[n] for n in names]],
-                                          [[self.params[n] for n in names]], 0, 0,
-                                          [self.seeds] if seeded else None,
-                                          [self.camera] if seeded else None))
+            self._update(self._peer_step())
         elif self.exchange == "peer":
             self._barrier()
-            self._update(self._shard_step(self.peer_grads, self.peer_params, 0, self.rank,
-                                          self.peer_seeds if seeded else None,
-                                          self.peer_cameras if seeded else None))
+            self._update(self._peer_step())
             self._barrier()
         else:
             for n in names:
@@ -471,15 +557,42 @@ class DataParallelTrainer:
         self.loss = z(1)
         self.buffers = _Scratch(dev)
         self.image = self.dimage = None
+        self._declared = None  # colour form: the camera the colours were made for
 
     def close(self):
         self.adam.close()
 
-    def step(self, camera: Camera, target):
+    def prime(self, camera: Camera):
+        """Colour form (collective): declares the camera of the first step and
+        has the owners render its colours."""
+        a = self.adam
+        a.next_camera.copy_(camera.campos)
+        a.prime()
+        self._declared = camera
+
+    def step(self, camera: Camera, target, next_camera: Camera = None):
         """Render, loss, backward and the exchange + update; returns the loss
-        (a device tensor) and the number of tile instances rendered."""
+        (a device tensor) and the number of tile instances rendered.
+
+        Colour form: `next_camera` is the camera this rank renders at its
+        next step (the update renders its colours), and `camera` must be the
+        one declared so by the previous step (or the first camera, which
+        primes the colours)."""
+        a = self.adam
+        if a.sh_exchange == "colours":
+            if next_camera is None:
+                raise ValueError("the colour form needs the next step's camera")
+            if self._declared is None:
+                self.prime(camera)
+            elif camera is not self._declared:
+                raise ValueError("the colour form renders the camera declared as "
+                                 "next_camera at the previous step")
         loss, rendered = self.backward(camera, target)
-        self.adam.step()
+        if a.sh_exchange == "colours":
+            a.next_camera.copy_(next_camera.campos)
+        a.step()
+        if a.sh_exchange == "colours":
+            self._declared = next_camera
         return loss, rendered
 
     def backward(self, camera: Camera, target):
@@ -500,12 +613,15 @@ class DataParallelTrainer:
         self.loss.zero_()
         act = a.activate()
         p = a.params
+        # Colour form: the owners' colours for this view stand for the SH.
+        colours = a.colours.data_ptr() if a.sh_exchange == "colours" else None
+        sh = None if colours else p["sh"].data_ptr()
         rendered = ctypes.c_int(0)
         native.check(lib.clad3dgs_raster_forward(
-            n, self.degree, self.bg.data_ptr(), p["xyz"].data_ptr(), None,
+            n, self.degree, self.bg.data_ptr(), p["xyz"].data_ptr(), colours,
             act["opacity"].data_ptr(), act["scaling"].data_ptr(), 1.0,
             act["rotation"].data_ptr(), None, camera.view.data_ptr(), camera.proj.data_ptr(),
-            camera.tan_x, camera.tan_y, H, W, p["sh"].data_ptr(), None, None,
+            camera.tan_x, camera.tan_y, H, W, sh, None, None,
             camera.campos.data_ptr(), 0, ctypes.cast(self.buffers.callback, ctypes.c_void_p),
             None, self.image.data_ptr(), self.invdepth.data_ptr(), self.radii.data_ptr(),
             ctypes.byref(rendered), stream), "rasterize (forward)")
@@ -513,16 +629,16 @@ class DataParallelTrainer:
                                           self.dimage.data_ptr(), self.loss.data_ptr(),
                                           stream), "l1 loss")
         g, s = a.grads, self.scratch_grads
-        seeded = a.sh_exchange == "seeds"
+        seeded = a.sh_exchange != "grads"
         geom = self.buffers.tensors.get(0)
         image = self.buffers.tensors.get(1)
         binning = self.buffers.tensors.get(2)
         native.check(lib.clad3dgs_raster_backward(
             n, self.degree, self.bg.data_ptr(), p["xyz"].data_ptr(), self.radii.data_ptr(),
-            None, act["opacity"].data_ptr(), act["scaling"].data_ptr(), 1.0,
+            colours, act["opacity"].data_ptr(), act["scaling"].data_ptr(), 1.0,
             act["rotation"].data_ptr(), None, camera.view.data_ptr(), camera.proj.data_ptr(),
             camera.tan_x, camera.tan_y, H, W, self.dimage.data_ptr(),
-            None, p["sh"].data_ptr(), None, None,
+            None, sh, None, None,
             camera.campos.data_ptr(), geom.data_ptr(), rendered.value,
             binning.data_ptr() if binning is not None else None, image.data_ptr(), 0,
             s["mean2d"].data_ptr(), s["colors"].data_ptr(), g["opacity"].data_ptr(),

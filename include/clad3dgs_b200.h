@@ -431,7 +431,19 @@ int clad3dgs_l1_loss(int64_t n, const float* image, const float* target, float* 
  * over q of d colour_q / d coefficients and the position gradient the sum
  * over q of (geometry part + view-direction adjoint), both in rank order and
  * bit-identical to summing the per-view gradients that the full rasterizer
- * backward writes. grads[q][1] is not read; grad_origin must be 0. */
+ * backward writes. grads[q][1] is not read; grad_origin must be 0.
+ *
+ * Colour form (seed form with colours[0] non-null; no counterpart in the
+ * reference): the replicas hold no other share's SH coefficients. The owner
+ * renders instead, for every rank q, the colour of each of its Gaussians seen
+ * from q's next camera next_cameras[q] (SH + 0.5, clamped at 0: the colour the
+ * rasterizer's own colour pass would give, bit for bit) into colours[q]
+ * ([N][3], the array rank q renders from as colors_precomp), keeps which
+ * channels the clamp cut in clamp_bits[i - begin] (bit 3q + k), and stores the
+ * updated coefficients into params[local][1] only. Seeds then come from a
+ * forward with colors_precomp (no clamp masking at the rank): the owner masks
+ * view q's seed with the clamp bits of the colours it produced for q. Per
+ * Gaussian and peer 56 bytes cross NVLink instead of 236. */
 typedef struct clad3dgs_shard_update_args {
   int64_t begin, end, grad_origin;
   int ranks, local;
@@ -447,9 +459,17 @@ typedef struct clad3dgs_shard_update_args {
   const float* seeds[CLAD3DGS_MAX_RANKS];    /* seed form: [N][4] per rank, or null */
   const float* cameras[CLAD3DGS_MAX_RANKS];  /* seed form: camera position per rank */
   int degree;                                /* seed form: SH degree 0..3 */
+  float* colours[CLAD3DGS_MAX_RANKS];            /* colour form: [N][3] per rank */
+  const float* next_cameras[CLAD3DGS_MAX_RANKS]; /* colour form: next camera per rank */
+  uint32_t* clamp_bits;                          /* colour form: [end - begin] */
 } clad3dgs_shard_update_args;
 
 int clad3dgs_shard_update(const clad3dgs_shard_update_args* args, cudaStream_t stream);
+
+/* Colour form, before the first step: the owner of [begin, end) renders each
+ * rank's colours from next_cameras[q] with the current replicas' positions and
+ * params[local][1] coefficients (colours[q], clamp_bits as above). No update. */
+int clad3dgs_shard_colours(const clad3dgs_shard_update_args* args, cudaStream_t stream);
 
 /* Device memory shareable with other processes of this node (CUDA IPC):
  * zero-filled allocation + its 64-byte handle; open / close a peer's handle. */

@@ -120,17 +120,17 @@ def test_collective_exchange_on_two_gloo_ranks(tmp_path):
 
 
 def test_sh_exchange_form_choice_on_cpu():
-    """The seed form needs CUDA (its SH backward runs in the update kernel):
-    on the CPU the gradient form is the default and the seed form is refused;
-    an unknown form is refused everywhere."""
+    """The seed and colour forms need CUDA (their SH backward runs in the
+    update kernel): on the CPU the gradient form is the default and both are
+    refused; an unknown form is refused everywhere."""
     from data_parallel import ShardedAdam
 
     adam = ShardedAdam(37, RATES, device="cpu", update=oracle_update)
     assert adam.sh_exchange == "grads" and adam.seeds is None and adam.camera is None
-    with pytest.raises(ValueError):
-        ShardedAdam(37, RATES, device="cpu", update=oracle_update, sh_exchange="seeds")
-    with pytest.raises(ValueError):
-        ShardedAdam(37, RATES, device="cpu", update=oracle_update, sh_exchange="colours")
+    assert adam.colours is None and adam.clamp_bits is None
+    for form in ("seeds", "colours", "colors"):
+        with pytest.raises(ValueError):
+            ShardedAdam(37, RATES, device="cpu", update=oracle_update, sh_exchange=form)
 
 
 def _collective_seeds_worker(rank, world, port, out_dir):

@@ -326,13 +326,181 @@ def test_seed_form_matches_gradient_form_for_emulated_ranks(cuda, world):
     trainer.close()
 
 
+def _clamping_scene(n, cuda):
+    """The small scene with every fifth Gaussian's base colour pushed below
+    zero in one channel (so the colour clamp cuts channels in every view)."""
+    v = _small_scene(n, cuda)
+    sh = v["sh"].view(n, 16, 3)
+    idx = torch.arange(0, n, 5, device=cuda)
+    sh[idx, 0, (idx // 5) % 3] = -2.5
+    return v
+
+
+def _unmasked_seeds(trainer, n):
+    """This view's dL/dcolour with the drawn flag, no channel masked: what a
+    rank renders from the owners' colours publishes."""
+    a = trainer.adam
+    u = torch.zeros_like(a.seeds)
+    u[:n, :3] = trainer.scratch_grads["colors"]
+    u[:n, 3] = (trainer.radii > 0).float()
+    return u
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_colour_form_matches_seed_form_for_emulated_ranks(cuda, world):
+    """`world` views on one GPU stand for the ranks. The owners' first colours
+    (`clad3dgs_shard_colours`) render each view exactly as the SH do; their
+    clamp bits mask the unmasked seeds as each rank's clamp flags masked its
+    seeds, so the colour-form update of every share equals the seed-form
+    update bit for bit, over consecutive steps; the colours each update writes
+    equal the colours made afresh from the updated parameters."""
+    from data_parallel import DataParallelTrainer, ShardStep, carve, native_colours, native_update
+    from data_parallel import orbit_camera, plan
+
+    n, W, H = 2400, 96, 64
+    padded, share = plan(n, world)
+    values = _clamping_scene(n, cuda)
+    seeded = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="seeds")
+    coloured = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="colours")
+    a = seeded.adam
+    grads, masked, unmasked, cams, images = [], [], [], [], []
+    for q in range(world):
+        cam = orbit_camera((2 * q + 1) % 8, 8, width=W, height=H, device=cuda)
+        target = torch.rand(3, H, W, device=cuda,
+                            generator=torch.Generator(device=cuda).manual_seed(10 + q))
+        seeded.backward(cam, target)
+        grads.append(carve(a.grad_slab.clone(), padded))
+        masked.append(a.seeds.clone())
+        unmasked.append(_unmasked_seeds(seeded, n))
+        cams.append(a.camera.clone())
+        images.append((cam, target, seeded.image.clone()))
+    names = GROUP_NAMES
+    replica_s = carve(a.param_slab.clone(), padded)
+    replica_c = carve(a.param_slab.clone(), padded)
+    saved = a.saved
+    colours = [torch.zeros(padded, 3, device=cuda) for _ in range(world)]
+    bits = torch.zeros(padded, dtype=torch.int32, device=cuda)
+
+    def shares(replica, **extra):
+        for r in range(world):
+            yield ShardStep(begin=r * share, end=(r + 1) * share, grad_origin=0,
+                            grads=[[grads[q][k] for k in names] for q in range(world)],
+                            params=[[replica[k] for k in names]] * world, local=0,
+                            first=[None] * 5, second=[None] * 5,
+                            saved_scaling=saved["scaling"],
+                            saved_opacity=saved["opacity"], saved_norm=saved["norm"],
+                            rates=RATE_TUPLE, bias1=1.0, bias2_sqrt=1.0, degree=3,
+                            **extra), r
+
+    def prime(replica, out, out_bits):
+        for step, r in shares(replica, colours=out, next_cameras=cams):
+            native_colours(step._replace(clamp_bits=out_bits[r * share:(r + 1) * share]))
+
+    prime(replica_c, colours, bits)
+    torch.cuda.synchronize()
+    # The colours render every view as its SH do (the rasterizer's own pass).
+    for q, (cam, target, image) in enumerate(images):
+        coloured.adam.colours.copy_(colours[q])
+        coloured.backward(cam, target)
+        assert torch.equal(coloured.image, image), q
+    assert int((bits != 0).sum()) > n // 20
+    zeros = lambda: {k: torch.zeros(share, w, device=cuda) for k, w in zip(names, WIDTHS)}
+    moments = [(zeros(), zeros(), zeros(), zeros()) for _ in range(world)]
+    for step in range(2):
+        b1, b2 = _bias(step + 1)
+        if step:
+            # Seed form: each view's seeds masked by its clamp flags at the
+            # current parameters (the bits the colour form keeps).
+            masked = [u.clone() for u in unmasked]
+            for q in range(world):
+                for k in range(3):
+                    cut = (bits >> (3 * q + k)) & 1 == 1
+                    masked[q][:, k] = torch.where(cut, 0.0, masked[q][:, k])
+        for (s_step, r), (c_step, _) in zip(shares(replica_s), shares(replica_c)):
+            m_s, v_s, m_c, v_c = moments[r]
+            native_update(s_step._replace(first=[m_s[k] for k in names],
+                                          second=[v_s[k] for k in names],
+                                          bias1=b1, bias2_sqrt=b2, seeds=masked,
+                                          cameras=cams))
+            native_update(c_step._replace(first=[m_c[k] for k in names],
+                                          second=[v_c[k] for k in names],
+                                          bias1=b1, bias2_sqrt=b2, seeds=unmasked,
+                                          cameras=cams, colours=colours, next_cameras=cams,
+                                          clamp_bits=bits[r * share:(r + 1) * share]))
+        torch.cuda.synchronize()
+        for r in range(world):
+            m_s, v_s, m_c, v_c = moments[r]
+            for k in names:
+                assert torch.equal(m_s[k], m_c[k]), (step, r, k)
+                assert torch.equal(v_s[k], v_c[k]), (step, r, k)
+        for k in names:
+            assert torch.equal(replica_s[k], replica_c[k]), (step, k)
+        fresh = [torch.zeros(padded, 3, device=cuda) for _ in range(world)]
+        fresh_bits = torch.zeros_like(bits)
+        prime(replica_c, fresh, fresh_bits)
+        torch.cuda.synchronize()
+        for q in range(world):
+            assert torch.equal(colours[q][:n], fresh[q][:n]), (step, q)
+        assert torch.equal(bits, fresh_bits), step
+    assert not torch.equal(replica_c["sh"], a.params["sh"])
+    seeded.close()
+    coloured.close()
+
+
+def test_colour_form_trainer_renders_the_updated_parameters(cuda):
+    """The colour-form trainer on one GPU: each step renders, from the
+    colours the previous update made for the declared camera, the image the
+    autograd front end renders from the current SH coefficients; a step whose
+    camera is not the declared one, or without a next camera, is refused."""
+    import rasterizer
+    from data_parallel import DataParallelTrainer, orbit_camera
+
+    n, W, H = 3000, 96, 64
+    values = _clamping_scene(n, cuda)
+    trainer = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="colours")
+    a = trainer.adam
+    views = [orbit_camera(v, 8, width=W, height=H, device=cuda) for v in (1, 4, 6, 3)]
+    torch.manual_seed(2)
+    targets = [torch.rand(3, H, W, device=cuda) for _ in views]
+    with pytest.raises(ValueError):
+        trainer.step(views[0], targets[0])
+    trainer.step(views[0], targets[0], next_camera=views[1])
+    with pytest.raises(ValueError):
+        trainer.step(views[2], targets[2], next_camera=views[3])
+    for t in (1, 2):
+        cam = views[t]
+        trainer.backward(cam, targets[t])
+        got = trainer.image.clone()
+        p, act = a.params, a.saved
+        settings = rasterizer.GaussianRasterizationSettings(
+            image_height=H, image_width=W, tanfovx=cam.tan_x, tanfovy=cam.tan_y,
+            bg=torch.zeros(3, device=cuda), scale_modifier=1.0, viewmatrix=cam.view,
+            projmatrix=cam.proj, sh_degree=3, campos=cam.campos, prefiltered=False,
+            debug=False)
+        with torch.no_grad():
+            image, _radii, _depth = rasterizer.GaussianRasterizer(settings)(
+                means3D=p["xyz"][:n], means2D=torch.zeros(n, 3, device=cuda),
+                opacities=act["opacity"][:n], shs=p["sh"][:n].view(n, 16, 3),
+                scales=act["scaling"][:n], rotations=act["rotation"][:n])
+        assert torch.equal(got, image), t
+        # The rest of the step, with the next camera declared.
+        a.next_camera.copy_(views[t + 1].campos)
+        a.step()
+        trainer._declared = views[t + 1]
+    moved = (a.params["xyz"][:n] != values["xyz"]).any(dim=1)
+    assert moved.sum() > n // 4
+    trainer.close()
+
+
 def test_seed_form_rejects_bad_arguments(cuda):
     from data_parallel import DataParallelTrainer, ShardedAdam, native_update
 
     with pytest.raises(ValueError):
         ShardedAdam(64, RATES, device="cpu", sh_exchange="seeds")
     with pytest.raises(ValueError):
-        ShardedAdam(64, RATES, device=cuda, sh_exchange="colours")
+        ShardedAdam(64, RATES, device=cuda, sh_exchange="colors")
+    with pytest.raises(ValueError):
+        ShardedAdam(64, RATES, device="cpu", sh_exchange="colours")
     trainer = DataParallelTrainer(_small_scene(64, cuda), RATES, device=cuda)
     a = trainer.adam
     a.t = 1
@@ -379,25 +547,34 @@ def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir, size="small"):
                                       sh_exchange=sh_exchange)
         a = trainer.adam
         assert a.world == world and a.exchange == exchange and a.sh_exchange == sh_exchange
-        seeded = sh_exchange == "seeds"
+        seeded = sh_exchange != "grads"
+        coloured = sh_exchange == "colours"
         cam = orbit_camera(rank, 8, width=W, height=H, device=device)
         target = torch.rand(3, H, W, device=device,
                             generator=torch.Generator(device=device).manual_seed(rank))
+        if coloured:
+            trainer.prime(cam)
         for step in range(3):
             trainer.backward(cam, target)
+            if coloured:
+                a.next_camera.copy_(cam.campos)
             # Every rank's gradients, the replica and this share's moments before the exchange.
             mine = a.grad_slab.clone()
             every = torch.empty(world * mine.numel(), device=device)
             dist.all_gather_into_tensor(every, mine)
             every = every.view(world, -1)
-            seeds = cameras = None
+            seeds = cameras = colours = next_cameras = bits = None
             if seeded:
                 mine = a.seed_slab.clone()
                 all_seeds = torch.empty(world * mine.numel(), device=device)
                 dist.all_gather_into_tensor(all_seeds, mine)
                 all_seeds = all_seeds.view(world, -1)
-                seeds = [all_seeds[q, 4:].view(-1, 4) for q in range(world)]
+                seeds = [all_seeds[q, 8:8 + 4 * a.padded].view(-1, 4) for q in range(world)]
                 cameras = [all_seeds[q, :3] for q in range(world)]
+            if coloured:
+                next_cameras = [all_seeds[q, 4:7] for q in range(world)]
+                colours = [torch.zeros(a.padded, 3, device=device) for _ in range(world)]
+                bits = a.clamp_bits.clone()
             params = a.param_slab.clone()
             first = {k: v.clone() for k, v in a.first.items()}
             second = {k: v.clone() for k, v in a.second.items()}
@@ -415,17 +592,35 @@ def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir, size="small"):
                                     [first[k] for k in names],
                                     [second[k] for k in names], a.saved["scaling"],
                                     a.saved["opacity"], a.saved["norm"], RATE_TUPLE, b1, b2,
-                                    seeds, cameras, 3))
+                                    seeds, cameras, 3, colours, next_cameras, bits))
             lo, hi = a.begin, a.end
             torch.cuda.synchronize()
             for k in names:
                 assert torch.equal(a.params[k][lo:hi], replica[k][lo:hi]), (rank, step, k)
                 assert torch.equal(a.first[k], first[k]), (rank, step, k)
                 assert torch.equal(a.second[k], second[k]), (rank, step, k)
-            # Replicas agree across ranks.
+            # Replicas agree across ranks (colour form: all but the SH, which
+            # only their owner keeps; the colours it made for every rank).
             ref = a.param_slab.clone()
             dist.broadcast(ref, 0)
-            assert torch.equal(ref, a.param_slab), (rank, step)
+            ref = carve(ref, a.padded)
+            for k in names:
+                if not (coloured and k == "sh"):
+                    assert torch.equal(ref[k], a.params[k]), (rank, step, k)
+            if coloured:
+                assert torch.equal(a.clamp_bits, bits), (rank, step)
+                mine = a.colours.clone()
+                made = torch.empty(world * mine.numel(), device=device)
+                dist.all_gather_into_tensor(made, mine)
+                made = made.view(world, a.padded, 3)
+                for q in range(world):
+                    assert torch.equal(made[q, lo:hi], colours[q][lo:hi]), (rank, step, q)
+        if coloured:
+            # After gather_sh every replica holds every share's coefficients.
+            a.gather_sh()
+            ref = a.params["sh"].clone()
+            dist.broadcast(ref, 0)
+            assert torch.equal(ref, a.params["sh"]), rank
         with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
             f.write("ok")
     finally:
@@ -436,7 +631,8 @@ def _dp_worker(rank, world, port, exchange, sh_exchange, out_dir, size="small"):
 
 
 @pytest.mark.parametrize("exchange,sh_exchange",
-                         [("peer", "seeds"), ("peer", "grads"), ("collective", "grads")])
+                         [("peer", "seeds"), ("peer", "colours"), ("peer", "grads"),
+                          ("collective", "grads")])
 def test_two_gpu_exchange_matches_emulation(cuda, exchange, sh_exchange, tmp_path):
     import torch.multiprocessing as mp
 
@@ -447,7 +643,8 @@ def test_two_gpu_exchange_matches_emulation(cuda, exchange, sh_exchange, tmp_pat
     assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
 
 
-@pytest.mark.parametrize("exchange,sh_exchange", [("peer", "seeds"), ("collective", "grads")])
+@pytest.mark.parametrize("exchange,sh_exchange",
+                         [("peer", "seeds"), ("peer", "colours"), ("collective", "grads")])
 def test_two_gpu_exchange_matches_emulation_at_full_size(cuda, exchange, sh_exchange,
                                                          tmp_path):
     """The 8-view data-parallel configuration on two GPUs: 6,000,000 Gaussians,
