@@ -74,8 +74,8 @@ def parse():
                     help="train-step: gradient exchange (default: peer memory on >1 GPU)")
     ap.add_argument("--sh-exchange", choices=["seeds", "colours", "grads"], default=None,
                     help="train-step: what a view publishes for the SH coefficients "
-                         "(default: colour seeds unless the exchange is collective; "
-                         "colours: the owners also render each rank's next colours)")
+                         "(default: colours, the owners rendering each rank's next "
+                         "colours, unless the exchange is collective)")
     ap.add_argument("--pixel-gaussians", type=int, default=3_000_000,
                     help="pixel-backward: 2D Gaussians (smaller cases are for profiling only)")
     ap.add_argument("--pixel-modes", default="2,1,0",
@@ -683,8 +683,12 @@ def measure_train_step(args, steps, warmup, with_e2e):
 
     n = args.train_gaussians
     values = train_values(n, device)
+    # Colour form unless the exchange is the collective one over several ranks.
+    form = args.sh_exchange
+    if form is None:
+        form = "grads" if args.exchange == "collective" and world > 1 else "colours"
     trainer = DataParallelTrainer(values, exchange=args.exchange, device=device,
-                                  sh_exchange=args.sh_exchange)
+                                  sh_exchange=form)
     del values
     # The 8 orbit cameras and a fixed random target per camera. Like a trainer
     # drawing its views from a shuffled stack, step k uses a seeded permutation
@@ -766,6 +770,18 @@ def measure_train_step(args, steps, warmup, with_e2e):
     # The exchange + update alone (gradients of a real backward in place).
     exchange_steps = max(3, min(steps, 20))
     total = backward_total = 0.0
+    # The update kernels alone (between the exchange's two barriers).
+    update_events = []
+    plain_update = trainer.adam._update
+
+    def timed_update(step):
+        u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        u0.record(stream)
+        plain_update(step)
+        u1.record(stream)
+        update_events.append((u0, u1))
+
+    trainer.adam._update = timed_update
     for _ in range(exchange_steps):
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record(stream)
@@ -783,7 +799,10 @@ def measure_train_step(args, steps, warmup, with_e2e):
         e1.record(stream)
         torch.cuda.synchronize()
         total += e0.elapsed_time(e1)
+    trainer.adam._update = plain_update
     exchange_ms = max_over_ranks(total / exchange_steps, "exchange_ms")
+    update_ms = max_over_ranks(sum(u0.elapsed_time(u1) for u0, u1 in update_events)
+                               / max(len(update_events), 1), "update_kernels_ms")
     max_over_ranks(backward_total / exchange_steps, "render_and_backward_ms")
     adam = trainer.adam
     baseline_ms = None
@@ -841,31 +860,37 @@ def measure_train_step(args, steps, warmup, with_e2e):
     trainer.close()
     if rank != 0:
         return None
-    # Exchange roofline: bytes that must cross NVLink per GPU and direction,
-    # per Gaussian of this share and peer: out, this share's parameters (236 B;
-    # colour form: 44 B without the SH, and 12 B of colours); in, the peers'
-    # gradients (236 B; seed and colour forms: 16 B colour seeds and 44 B of
-    # geometry gradients). The busier direction against the measured 770 GB/s
-    # peer copy. With one GPU the update is HBM-bound (inputs, params, moments
-    # read; params, moments written; colour form: colours and clamp bits).
+    # Exchange roofline, per GPU, in units of one Gaussian of its share (R
+    # ranks). Across NVLink per direction, per peer: out, the share's updated
+    # parameters (236 B; colour form: 44 B without the SH, and 12 B of
+    # colours); in, the peer's view inputs (236 B of gradients; seed and colour
+    # forms: 16 B colour seeds and 44 B of geometry gradients). From this GPU's
+    # HBM: its moments read and written (944 B), its replica's parameters of
+    # the share read and written (2 x 236 B), its view inputs read by all R
+    # owners, the peers' parameter stores into its replica, and in colour form
+    # its colours (12 B) and the share's clamp bits (8 B). The bound is the
+    # slower of the two against the measured peer copy (770 GB/s per
+    # direction) and the measured HBM copy.
     floats = 59
     seeded = adam.sh_exchange != "grads"
+    coloured = adam.sh_exchange == "colours"
     inputs = (16 + 11 * 4) if seeded else floats * 4  # per Gaussian and view
-    outputs = (11 * 4 + 12) if adam.sh_exchange == "colours" else floats * 4
-    if world > 1:
-        link = (world - 1) * share * max(inputs, outputs)
+    outputs = (11 * 4 + 12) if coloured else floats * 4
+    link = (world - 1) * share * max(inputs, outputs)
+    hbm = share * (944 + 2 * floats * 4 + world * inputs + (world - 1) * outputs
+                   + (20 if coloured else 0))
+    peak, peak_kind = measured_peaks()
+    link_s, hbm_s = link / 770e9, hbm / (peak * 1e9)
+    if link_s > hbm_s:
         exchange_roof = {"bound": "nvlink", "achieved": link / (exchange_ms / 1e3) / 1e9,
                          "peak": 770.0, "unit": "GB/s",
-                         "frac": link / (exchange_ms / 1e3) / 1e9 / 770.0,
-                         "bytes_per_direction": link,
                          "peak_kind": "measured peer copy per direction"}
     else:
-        hbm = share * (inputs + floats * 4 * 6 + (20 if adam.sh_exchange == "colours" else 0))
-        peak, peak_kind = measured_peaks()
         exchange_roof = {"bound": "hbm", "achieved": hbm / (exchange_ms / 1e3) / 1e9,
-                         "peak": peak, "unit": "GB/s",
-                         "frac": hbm / (exchange_ms / 1e3) / 1e9 / peak,
-                         "algorithmic_bytes": hbm, "peak_kind": peak_kind}
+                         "peak": peak, "unit": "GB/s", "peak_kind": peak_kind}
+    exchange_roof.update(frac=max(link_s, hbm_s) / (exchange_ms / 1e3),
+                         link_bytes_per_direction=link, hbm_bytes=hbm,
+                         bound_ms=max(link_s, hbm_s) * 1e3)
     line = {
         "metric": "data-parallel training step, views/s (one 1920x1080 view per GPU)",
         "value": world / (step_ms / 1e3), "unit": "views/s", "n_gpus": world,
@@ -884,7 +909,8 @@ def measure_train_step(args, steps, warmup, with_e2e):
                    "l2": "parameters 1.4 GB per replica exceed the 126 MB L2"},
         "loss": {"first": first_loss, "last": last_loss},
         "per_rank": dict(per_rank, tile_instances=instances_all),
-        "exchange": {"ms": exchange_ms, "nccl_baseline_ms": baseline_ms,
+        "exchange": {"ms": exchange_ms, "update_kernels_ms": update_ms,
+                     "nccl_baseline_ms": baseline_ms,
                      "roofline": exchange_roof},
         "clocks": clocks.summary(),
         "e2e": e2e,

@@ -181,14 +181,15 @@ __device__ __forceinline__ Direction direction_from(float4 u) {
 
 template <int J, int R>
 __device__ __forceinline__ void views_adjoint_terms(const float4 (&dir)[R],
-                                                    const float4 (&seed)[R], float* row,
-                                                    int nterms, float (&dd)[R][3]) {
+                                                    const float3 (&seed)[R], uint32_t drawn,
+                                                    float* row, int nterms,
+                                                    float (&dd)[R][3]) {
   if constexpr (J < 16) {
     float acc[3];
 #pragma unroll
     for (int q = 0; q < R; ++q) {
       float prod[3] = {0.f, 0.f, 0.f};
-      if (seed[q].w != 0.f && J < nterms) {
+      if ((drawn >> q & 1u) && J < nterms) {
         float b, gx, gy, gz;
         sh_basis<J>(direction_from(dir[q]), b, gx, gy, gz);
         const float* c = row + 3 * J;
@@ -205,7 +206,7 @@ __device__ __forceinline__ void views_adjoint_terms(const float4 (&dir)[R],
     }
 #pragma unroll
     for (int k = 0; k < 3; ++k) row[3 * J + k] = acc[k];
-    views_adjoint_terms<J + 1, R>(dir, seed, row, nterms, dd);
+    views_adjoint_terms<J + 1, R>(dir, seed, drawn, row, nterms, dd);
   }
 }
 
@@ -286,14 +287,16 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
     float pos[3];
 #pragma unroll
     for (int k = 0; k < 3; ++k) pos[k] = a.xyz[a.local][3 * i + k];
-    // Every view's loads first (independent, many in flight over NVLink).
+    // Every view's seed first (independent loads, many in flight over
+    // NVLink); with one view its geometry gradient too (with several, those
+    // loads wait until the SH backward is done: fewer live registers).
     float4 seed[R];
-    float geo[R][3];
+    float geo[1][3];
 #pragma unroll
-    for (int q = 0; q < R; ++q) {
-      seed[q] = a.seeds[q][i];
+    for (int q = 0; q < R; ++q) seed[q] = a.seeds[q][i];
+    if constexpr (R == 1) {
 #pragma unroll
-      for (int k = 0; k < 3; ++k) geo[q][k] = a.geo_xyz[q][3 * i + k];
+      for (int k = 0; k < 3; ++k) geo[0][k] = a.geo_xyz[0][3 * i + k];
     }
     if constexpr (Colours) {
       // View q rendered the colours this owner made for it: its seed carries
@@ -309,27 +312,36 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
     float x[3];
     if constexpr (R > 1) {
       float4 dir[R];
+      float3 colour_seed[R];
       float dd[R][3];
+      uint32_t drawn = 0;
 #pragma unroll
       for (int q = 0; q < R; ++q) {
         dir[q] = make_float4(0.f, 0.f, 0.f, 1.f);
+        colour_seed[q] = make_float3(seed[q].x, seed[q].y, seed[q].z);
         if (seed[q].w != 0.f) {
+          drawn |= 1u << q;
           const Direction d = make_direction(pos[0], pos[1], pos[2], cams[q][0], cams[q][1],
                                              cams[q][2]);
           dir[q] = make_float4(d.x, d.y, d.z, d.r);
         }
         dd[q][0] = dd[q][1] = dd[q][2] = 0.f;
       }
-      views_adjoint_terms<0, R>(dir, seed, sum, a.nterms, dd);
+      views_adjoint_terms<0, R>(dir, colour_seed, drawn, sum, a.nterms, dd);
+      float geo_q[R][3];
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) geo_q[q][k] = a.geo_xyz[q][3 * i + k];
 #pragma unroll
       for (int q = 0; q < R; ++q) {
-        float xq[3] = {geo[q][0], geo[q][1], geo[q][2]};
-        if (seed[q].w != 0.f) {
+        float xq[3] = {geo_q[q][0], geo_q[q][1], geo_q[q][2]};
+        if (drawn >> q & 1u) {
           float om[3];
           direction_vjp(direction_from(dir[q]), dd[q][0], dd[q][1], dd[q][2], om[0], om[1],
                         om[2]);
 #pragma unroll
-          for (int k = 0; k < 3; ++k) xq[k] = geo[q][k] + om[k];
+          for (int k = 0; k < 3; ++k) xq[k] = geo_q[q][k] + om[k];
         }
 #pragma unroll
         for (int k = 0; k < 3; ++k) x[k] = q == 0 ? xq[k] : x[k] + xq[k];
