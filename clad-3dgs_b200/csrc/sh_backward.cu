@@ -278,15 +278,35 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
   const int chunks = n * 12;
   const float4* src = reinterpret_cast<const float4*>(a.sh[a.local] + 48 * i0);
   stage_block(src, chunks, lane, cb);
+  // With one or two views the Adam pass's first chunk (moments and
+  // parameters) and the position moments are loaded now, so their latency
+  // overlaps the SH backward (with more views the registers they hold cost
+  // more occupancy than the overlap gains).
+  constexpr bool kEarly = R <= 2;
+  float4* first = reinterpret_cast<float4*>(a.sh_first + 48 * (i0 - a.begin));
+  float4* second = reinterpret_cast<float4*>(a.sh_second + 48 * (i0 - a.begin));
+  float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = m4, p4 = m4;
+  if (kEarly && lane < chunks) {
+    m4 = first[lane];
+    v4 = second[lane];
+    if (kInPlace) p4 = src[lane];
+  }
   __syncwarp();
   float moved[3] = {0.f, 0.f, 0.f};  // the updated position (colour form)
   if (lane < n) {
     const int64_t i = i0 + lane;
     const float* row = cb + lane * kSeedRow;
     float* sum = sb + lane * kSeedRow;
-    float pos[3];
+    float pos[3], xm[3] = {0.f, 0.f, 0.f}, xv[3] = {0.f, 0.f, 0.f};
+    const int64_t mx = 3 * (i - a.begin);
 #pragma unroll
-    for (int k = 0; k < 3; ++k) pos[k] = a.xyz[a.local][3 * i + k];
+    for (int k = 0; k < 3; ++k) {
+      pos[k] = a.xyz[a.local][3 * i + k];
+      if (kEarly) {
+        xm[k] = a.xyz_first[mx + k];
+        xv[k] = a.xyz_second[mx + k];
+      }
+    }
     // Every view's seed first (independent loads, many in flight over
     // NVLink); with one view its geometry gradient too (with several, those
     // loads wait until the SH backward is done: fewer live registers).
@@ -372,10 +392,10 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
       for (int k = 0; k < 3; ++k) x[k] = q == 0 ? xq[k] : x[k] + xq[k];
     }
     }
-    const int64_t mx = 3 * (i - a.begin);
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      float p = pos[k], m = a.xyz_first[mx + k], v = a.xyz_second[mx + k];
+      float p = pos[k], m = kEarly ? xm[k] : a.xyz_first[mx + k];
+      float v = kEarly ? xv[k] : a.xyz_second[mx + k];
       torch_adam(p, m, v, x[k], a.step_xyz, a.inv_bias2);
       a.xyz_first[mx + k] = m;
       a.xyz_second[mx + k] = v;
@@ -387,10 +407,7 @@ __global__ void __launch_bounds__(32 * kSeedWarps)
   __syncwarp();
   // Adam over the block's coefficients in float4 chunks, coalesced; each
   // lane loads its next chunk's moments before updating the current one.
-  float4* first = reinterpret_cast<float4*>(a.sh_first + 48 * (i0 - a.begin));
-  float4* second = reinterpret_cast<float4*>(a.sh_second + 48 * (i0 - a.begin));
-  float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = m4, p4 = m4;
-  if (lane < chunks) {
+  if (!kEarly && lane < chunks) {
     m4 = first[lane];
     v4 = second[lane];
     if (kInPlace) p4 = src[lane];
