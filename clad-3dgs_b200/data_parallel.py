@@ -371,6 +371,30 @@ class ShardedAdam:
             v = values[name].reshape(self.n, k)
             self.params[name][:self.n].copy_(v)
 
+    def state_dict(self):
+        """This rank's part of a checkpoint (collective in colour form, whose
+        replicas are first completed by `gather_sh`): the step counter, the
+        parameters of the n Gaussians and the moments of this rank's share."""
+        self.gather_sh()
+        return {"t": self.t, "n": self.n, "world": self.world, "rank": self.rank,
+                "params": {k: v[:self.n].detach().cpu().clone() for k, v in self.params.items()},
+                "first": {k: v.detach().cpu().clone() for k, v in self.first.items()},
+                "second": {k: v.detach().cpu().clone() for k, v in self.second.items()}}
+
+    def load_state_dict(self, state):
+        """Restores `state_dict` output of the same rank of a group of the
+        same size (the moments are sharded by Gaussian index). In colour form
+        the colours must be made again (`prime`) before the next step."""
+        if (state["n"], state["world"], state["rank"]) != (self.n, self.world, self.rank):
+            raise ValueError(
+                f"checkpoint of rank {state['rank']} of {state['world']} over {state['n']} "
+                f"Gaussians does not fit rank {self.rank} of {self.world} over {self.n}")
+        self.load(state["params"])
+        for name, _ in GROUPS:
+            self.first[name].copy_(state["first"][name])
+            self.second[name].copy_(state["second"][name])
+        self.t = int(state["t"])
+
     def activate(self):
         """Activated scaling / rotation / opacity and |q| for every Gaussian."""
         p, s = self.params, self.saved
@@ -561,6 +585,16 @@ class DataParallelTrainer:
 
     def close(self):
         self.adam.close()
+
+    def state_dict(self):
+        """This rank's checkpoint (collective in colour form)."""
+        return self.adam.state_dict()
+
+    def load_state_dict(self, state):
+        """Restores `state_dict`; in colour form the next step primes the
+        colours again from the camera it renders."""
+        self.adam.load_state_dict(state)
+        self._declared = None
 
     def prime(self, camera: Camera):
         """Colour form (collective): declares the camera of the first step and

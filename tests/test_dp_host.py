@@ -158,3 +158,53 @@ def test_collective_exchange_refuses_the_seed_form(tmp_path):
     mp.spawn(_collective_seeds_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2)
     for rank in range(2):
         assert (tmp_path / f"refused{rank}").read_text() == "True"
+
+
+def _resume_worker(rank, world, port, n, out_dir):
+    from datetime import timedelta
+
+    from data_parallel import ShardedAdam
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        def run(adam, steps):
+            for step in steps:
+                grads = view_gradients(rank, step, adam.padded, n)
+                for name in GROUP_NAMES:
+                    adam.grads[name].copy_(grads[name])
+                _apply_saved(adam)
+                adam.step()
+
+        first = ShardedAdam(n, RATES, device="cpu", update=oracle_update)
+        first.load(initial_values(n))
+        run(first, range(2))
+        state = first.state_dict()
+        run(first, range(2, 4))
+        resumed = ShardedAdam(n, RATES, device="cpu", update=oracle_update)
+        resumed.load_state_dict(state)
+        assert resumed.t == 2
+        run(resumed, range(2, 4))
+        for k in GROUP_NAMES:
+            assert torch.equal(resumed.params[k], first.params[k]), (rank, k)
+            assert torch.equal(resumed.first[k], first.first[k]), (rank, k)
+            assert torch.equal(resumed.second[k], first.second[k]), (rank, k)
+        other = dict(state, rank=1 - rank)
+        try:
+            resumed.load_state_dict(other)
+            refused = False
+        except ValueError:
+            refused = True
+        with open(os.path.join(out_dir, f"resumed{rank}"), "w") as f:
+            f.write(str(refused))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_checkpoint_resume_on_two_gloo_ranks(tmp_path):
+    """A rank's `state_dict` after two steps, loaded into a fresh optimizer,
+    continues bit for bit like the uninterrupted run (parameters, sharded
+    moments, step counter); another rank's checkpoint is refused."""
+    mp.spawn(_resume_worker, args=(2, _free_port(), 37, str(tmp_path)), nprocs=2)
+    for rank in range(2):
+        assert (tmp_path / f"resumed{rank}").read_text() == "True"

@@ -489,6 +489,20 @@ def test_colour_form_trainer_renders_the_updated_parameters(cuda):
         trainer._declared = views[t + 1]
     moved = (a.params["xyz"][:n] != values["xyz"]).any(dim=1)
     assert moved.sum() > n // 4
+    # A checkpoint restores the step: a fresh trainer primes the declared
+    # camera's colours from it and renders the same image.
+    state = trainer.state_dict()
+    assert state["t"] == a.t
+    resumed = DataParallelTrainer(_clamping_scene(n, cuda), RATES, device=cuda,
+                                  sh_exchange="colours")
+    resumed.load_state_dict(state)
+    resumed.prime(views[3])
+    trainer.backward(views[3], targets[3])
+    resumed.backward(views[3], targets[3])
+    assert torch.equal(resumed.image, trainer.image)
+    for k in GROUP_NAMES:
+        assert torch.equal(resumed.adam.params[k][:n], a.params[k][:n]), k
+    resumed.close()
     trainer.close()
 
 
