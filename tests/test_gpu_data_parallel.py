@@ -346,8 +346,9 @@ def _unmasked_seeds(trainer, n):
     return u
 
 
-@pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_colour_form_matches_seed_form_for_emulated_ranks(cuda, world):
+@pytest.mark.parametrize("world,degree", [(1, 3), (2, 3), (4, 3), (8, 3), (2, 0), (4, 1),
+                                          (3, 2)])
+def test_colour_form_matches_seed_form_for_emulated_ranks(cuda, world, degree):
     """`world` views on one GPU stand for the ranks. The owners' first colours
     (`clad3dgs_shard_colours`) render each view exactly as the SH do; their
     clamp bits mask the unmasked seeds as each rank's clamp flags masked its
@@ -360,8 +361,10 @@ def test_colour_form_matches_seed_form_for_emulated_ranks(cuda, world):
     n, W, H = 2400, 96, 64
     padded, share = plan(n, world)
     values = _clamping_scene(n, cuda)
-    seeded = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="seeds")
-    coloured = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="colours")
+    seeded = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="seeds",
+                                 degree=degree)
+    coloured = DataParallelTrainer(values, RATES, device=cuda, sh_exchange="colours",
+                                   degree=degree)
     a = seeded.adam
     grads, masked, unmasked, cams, images = [], [], [], [], []
     for q in range(world):
@@ -389,7 +392,7 @@ def test_colour_form_matches_seed_form_for_emulated_ranks(cuda, world):
                             first=[None] * 5, second=[None] * 5,
                             saved_scaling=saved["scaling"],
                             saved_opacity=saved["opacity"], saved_norm=saved["norm"],
-                            rates=RATE_TUPLE, bias1=1.0, bias2_sqrt=1.0, degree=3,
+                            rates=RATE_TUPLE, bias1=1.0, bias2_sqrt=1.0, degree=degree,
                             **extra), r
 
     def prime(replica, out, out_bits):
