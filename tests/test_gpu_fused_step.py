@@ -65,16 +65,25 @@ def test_fused_step_bit_exact(cuda, n):
             assert _bits_equal(da[k][j].cpu().numpy(), want_act[k][j]), (k, j)
 
 
+@pytest.mark.parametrize("memory", ["pinned", "pageable", "mixed"])
 @pytest.mark.parametrize("n,chunk", [(1, 64), (1000, 256), (100_000, 8192)])
-def test_host_buffer_pipeline_bit_exact(cuda, n, chunk):
+def test_host_buffer_pipeline_bit_exact(cuda, n, chunk, memory):
+    """The staged copy pipeline with pinned, pageable or mixed host buffers
+    (pageable copies are synchronous on the host side): bit-exact."""
     import consume
 
     sh, act = _problem(n, seed=3)
     step = 2
     b1, b2 = cases.bias(step)
     ab1, ab2 = [0.19, 0.19, 0.19], [0.0447, 0.0447, 0.0447]
-    h = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in sh.items()}
-    ha = {k: [torch.from_numpy(np.ascontiguousarray(x)).pin_memory() for x in act[k]]
+
+    def host(v, pageable):
+        t = torch.from_numpy(np.array(v, copy=True))  # the oracle keeps the inputs
+        return t if pageable else t.pin_memory()
+
+    h = {k: host(v, memory == "pageable" or (memory == "mixed" and k == "rest"))
+         for k, v in sh.items()}
+    ha = {k: [host(x, memory == "pageable") for x in act[k]]
           for k in ("params", "seeds", "saved", "first", "second")}
     ws = torch.empty(consume.host_step_workspace(chunk), dtype=torch.uint8, device=cuda)
     consume.gaussian_step_host(h["means"], h["radii"], h["clamped"], h["camera"], h["seed"],
