@@ -239,6 +239,7 @@ class ShardedAdam:
         self.begin = self.rank * self.share
         self.end = self.begin + self.share
         self.t = 0
+        self._settled = 0  # gate passes outside the steps
         self._update = update or native_update
         total = FLOATS_PER_GAUSSIAN * self.padded
         self._own = []
@@ -417,6 +418,13 @@ class ShardedAdam:
     def _barrier(self):
         dist.all_reduce(self._flag, group=self.group)
 
+    def _settle(self, what):
+        """The step gate for a collective outside the step (priming the
+        colours, gathering the SH): every rank present, or RankFailure."""
+        if self.gate is not None and self.world > 1:
+            self._settled += 1
+            self.gate.arrive_and_wait(f"{what}-{self._settled}")
+
     def _shard_step(self, grads, params, grad_origin, local, seeds=None, cameras=None,
                     colours=None, next_cameras=None):
         t = max(self.t, 1)  # `prime` comes before the first step and reads no rate
@@ -454,6 +462,7 @@ class ShardedAdam:
         parameters."""
         if self.sh_exchange != "colours":
             raise ValueError("prime belongs to the colour form")
+        self._settle("colours")
         if self.world > 1:
             self._barrier()
         native_colours(self._peer_step())
@@ -466,6 +475,7 @@ class ShardedAdam:
         replica current, so there it does nothing)."""
         if self.sh_exchange != "colours" or self.world == 1:
             return self.params["sh"]
+        self._settle("gather")
         full = self.params["sh"].view(-1)
         mine = full[48 * self.begin:48 * self.end].clone()
         dist.all_gather_into_tensor(full, mine, group=self.group)
