@@ -1,11 +1,12 @@
-// The SH backward, in its two forms, in one translation unit compiled without
-// multiply-add contraction (every product and sum rounded on its own, in
-// source order), so that both forms give the same bits:
+// The SH colour and its backward, each in two forms, in one translation unit
+// compiled without multiply-add contraction (every product and sum rounded on
+// its own, in source order), so that the forms give the same bits:
 //
-// * the rasterizer's, per view (sh_backward_kernel): d colour / d
-//   coefficients and the view direction's adjoint of every drawn Gaussian;
-// * the seed form of the data-parallel exchange for the SH and position
-//   groups (shard_seed_kernel), below.
+// * the rasterizer's, per view: the colour pass (sh_colour_kernel) and
+//   d colour / d coefficients with the view direction's adjoint of every drawn
+//   Gaussian (sh_backward_kernel);
+// * the data-parallel exchange's, for the SH and position groups of a share
+//   (shard_seed_kernel; shard_colour_kernel), below.
 //
 // Seed form. Every rank renders its own view. Instead of the 48 SH gradients of every
 // Gaussian, a rank publishes the colour seed of its view (dL/dcolour with the
@@ -17,6 +18,13 @@
 // summed, and runs torch-fused Adam on the 48 coefficients and 3 positions,
 // storing the parameters into every replica. The other groups (scaling,
 // rotation, opacity) go through the chunked update of train_step.cu.
+//
+// Colour form. The owner keeps the updated coefficients in its own replica
+// only and, from the rows still in shared memory, renders every rank's colour
+// of its Gaussians for that rank's next camera (the colour pass's arithmetic),
+// 12 bytes per Gaussian and rank instead of 192; it keeps which channels the
+// clamp cut and masks the next seeds with them, as each rank's clamp flags
+// masked its seeds in the seed form.
 //
 // One warp per 32 Gaussians: the warp stages its coefficient block in shared
 // memory (rows of 48 floats + 1, so each lane's row starts in its own bank),
