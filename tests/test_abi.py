@@ -2,8 +2,13 @@
 function include/clad3dgs_b200.h declares (no compute calls)."""
 
 import ctypes
+import os
 import re
+import shutil
+import subprocess
 from pathlib import Path
+
+import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 
@@ -48,3 +53,32 @@ def test_product_modules_do_not_reach_the_oracle():
         text = path.read_text()
         assert "import oracle" not in text and "oracle/" not in text, path
         assert "torch_cpu_path" not in text, path
+
+
+def test_shard_update_args_layout_matches_header(tmp_path):
+    """The ctypes mirror of clad3dgs_shard_update_args has the C struct's
+    size and every field at the C offset (a probe compiled with gcc against
+    include/clad3dgs_b200.h)."""
+    import _native
+    from torch.utils.cpp_extension import CUDA_HOME
+
+    if shutil.which("gcc") is None or CUDA_HOME is None:
+        pytest.skip("gcc or the CUDA headers are not available")
+    fields = [name for name, _ in _native.ShardUpdateArgs._fields_]
+    probe = tmp_path / "probe.c"
+    probe.write_text(
+        "#include <stdio.h>\n#include <stddef.h>\n#include \"clad3dgs_b200.h\"\n"
+        "int main(void) {\n"
+        "  printf(\"size %zu\\n\", sizeof(clad3dgs_shard_update_args));\n"
+        + "".join(f"  printf(\"{f} %zu\\n\", offsetof(clad3dgs_shard_update_args, {f}));\n"
+                  for f in fields)
+        + "  return 0;\n}\n")
+    exe = tmp_path / "probe"
+    cuda_include = os.path.join(CUDA_HOME, "include")
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", f"-I{cuda_include}",
+                    str(probe), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run(
+        [str(exe)], check=True, capture_output=True, text=True).stdout.splitlines())
+    assert int(out["size"]) == ctypes.sizeof(_native.ShardUpdateArgs)
+    for f in fields:
+        assert int(out[f]) == getattr(_native.ShardUpdateArgs, f).offset, f
