@@ -55,22 +55,26 @@ def test_product_modules_do_not_reach_the_oracle():
         assert "torch_cpu_path" not in text, path
 
 
-def test_shard_update_args_layout_matches_header(tmp_path):
-    """The ctypes mirror of clad3dgs_shard_update_args has the C struct's
-    size and every field at the C offset (a probe compiled with gcc against
+@pytest.mark.parametrize("mirror,c_name", [("ShardUpdateArgs", "clad3dgs_shard_update_args"),
+                                            ("AdamConfig", "AdamConfig"),
+                                            ("TorchAdamConfig", "TorchAdamConfig")])
+def test_struct_layouts_match_header(tmp_path, mirror, c_name):
+    """Each ctypes mirror of a header struct has the C struct's size and
+    every field at the C offset (a probe compiled with gcc against
     include/clad3dgs_b200.h)."""
     import _native
     from torch.utils.cpp_extension import CUDA_HOME
 
     if shutil.which("gcc") is None or CUDA_HOME is None:
         pytest.skip("gcc or the CUDA headers are not available")
-    fields = [name for name, _ in _native.ShardUpdateArgs._fields_]
+    struct = getattr(_native, mirror)
+    fields = [name for name, _ in struct._fields_]
     probe = tmp_path / "probe.c"
     probe.write_text(
         "#include <stdio.h>\n#include <stddef.h>\n#include \"clad3dgs_b200.h\"\n"
         "int main(void) {\n"
-        "  printf(\"size %zu\\n\", sizeof(clad3dgs_shard_update_args));\n"
-        + "".join(f"  printf(\"{f} %zu\\n\", offsetof(clad3dgs_shard_update_args, {f}));\n"
+        f"  printf(\"size %zu\\n\", sizeof({c_name}));\n"
+        + "".join(f"  printf(\"{f} %zu\\n\", offsetof({c_name}, {f}));\n"
                   for f in fields)
         + "  return 0;\n}\n")
     exe = tmp_path / "probe"
@@ -79,6 +83,6 @@ def test_shard_update_args_layout_matches_header(tmp_path):
                     str(probe), "-o", str(exe)], check=True)
     out = dict(line.split() for line in subprocess.run(
         [str(exe)], check=True, capture_output=True, text=True).stdout.splitlines())
-    assert int(out["size"]) == ctypes.sizeof(_native.ShardUpdateArgs)
+    assert int(out["size"]) == ctypes.sizeof(struct)
     for f in fields:
-        assert int(out[f]) == getattr(_native.ShardUpdateArgs, f).offset, f
+        assert int(out[f]) == getattr(struct, f).offset, f
