@@ -86,3 +86,34 @@ def test_struct_layouts_match_header(tmp_path, mirror, c_name):
     assert int(out["size"]) == ctypes.sizeof(struct)
     for f in fields:
         assert int(out[f]) == getattr(struct, f).offset, f
+
+
+def _declared_arity():
+    """Parameter count of every function the header declares."""
+    arity = {}
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        for m in re.finditer(r"\b([a-z_][a-z0-9_]*)\s*\(([^;{]*?)\)\s*;", text, re.S):
+            name, params = m.group(1), m.group(2).strip()
+            if name in {"if", "while", "for", "return", "sizeof"}:
+                continue
+            depth, count = 0, 0 if params in ("", "void") else 1
+            for ch in params:
+                depth += ch == "("
+                depth -= ch == ")"
+                count += ch == "," and depth == 0
+            arity[name] = count
+    return arity
+
+
+def test_binding_argument_counts_match_header():
+    """Every ctypes signature takes as many arguments as the header's
+    prototype declares."""
+    import _native
+
+    arity = _declared_arity()
+    signatures = _native._SIGNATURES
+    assert set(signatures) <= set(arity)
+    wrong = {name: (len(argtypes), arity[name]) for name, (_, argtypes) in signatures.items()
+             if len(argtypes) != arity[name]}
+    assert not wrong, wrong
